@@ -1,0 +1,338 @@
+"""Benchmark: the furiosa-opt emulator hot path on B200.
+
+Default (headline) workload: config 2, the standalone int8 contraction M=N=K=4096 (i32 accumulate,
+per-channel fp32 requant to i8), one step = one `contraction` call through the backend.
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm_i8|gemm_bf16|attention|
+                  relayout|allreduce] [--impl ours|reference]
+Multi-GPU (torchrun, one rank per GPU): independent replicas of the step ("replicas only": the
+contraction does not shard), except `allreduce`, the config-5 NCCL collective.
+`--impl reference` times the reference algorithm's CPU restatement (the oracle port: the emulator
+itself is Rust + closed prebuilt libraries and cannot be built here) on this host's cores.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def _pkg():
+    if "furiosa_opt_b200" in sys.modules:
+        return sys.modules["furiosa_opt_b200"]
+    d = os.path.join(ROOT, "furiosa-opt_b200")
+    spec = importlib.util.spec_from_file_location("furiosa_opt_b200", os.path.join(d, "__init__.py"),
+                                                  submodule_search_locations=[d])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["furiosa_opt_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (median SM clock under load, throttle reasons)."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.proc = index, [], None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms",
+                                          "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons}
+
+
+# ---------------------------------------------------------------------------------------------
+# workloads: each returns a dict with step(), per-step units, and metadata
+# ---------------------------------------------------------------------------------------------
+def wl_gemm(fb, be, dtype: str, M=4096, N=4096, K=4096):
+    rng = np.random.default_rng(42)
+    ax = dict(M=M, N=N, K=K)
+    exprs = ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]")
+    L, R, P, O = (fb.Mapping(e, ax) for e in exprs)
+    if dtype == "i8":
+        a = rng.integers(-128, 128, M * K, dtype=np.int64).astype(np.int8)
+        b = rng.integers(-128, 128, N * K, dtype=np.int64).astype(np.int8)
+    else:
+        a = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(M * K).astype(np.float32))
+        b = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(N * K).astype(np.float32))
+    scale = rng.uniform(0.001, 0.01, N).astype(np.float32)
+    A, B = be.from_vec(L, a, dtype), be.from_vec(R, b, dtype)
+    S = be.from_vec(fb.Mapping("[N]", ax), scale, "f32")
+    out_dt = "i8" if dtype == "i8" else "bf16"
+    ops = 2.0 * M * N * K
+    OUT = be.zeroed(O, out_dt)
+
+    def step():
+        if dtype == "i8":
+            return be.contraction_requant(A, B, L, R, P, O, S, "N", out=OUT)
+        return be.contraction(A, B, L, R, P, O, out=OUT)
+
+    # e2e: host (pinned) inputs -> device -> contraction -> host result, every step
+    import torch
+
+    ha = torch.from_numpy(a.view(np.uint8)).pin_memory()
+    hb = torch.from_numpy(b.view(np.uint8)).pin_memory()
+    hout = torch.empty(M * N * (1 if dtype == "i8" else 2), dtype=torch.uint8).pin_memory()
+    lib = fb._lib.lib()
+
+    def e2e_step():
+        lib.fopt_h2d(be.ctx, A.ptr, ha.data_ptr(), ha.numel())
+        lib.fopt_h2d(be.ctx, B.ptr, hb.data_ptr(), hb.numel())
+        out = step()
+        lib.fopt_d2h(be.ctx, hout.data_ptr(), out.ptr, hout.numel())
+        return out
+
+    return dict(step=step, e2e_step=e2e_step, units=ops, unit="TOPS" if dtype == "i8" else "TFLOP/s",
+                scale=1e12, metric=f"{'int8' if dtype == 'i8' else 'bf16'} GEMM "
+                                   f"{'TOPS' if dtype == 'i8' else 'TFLOP/s'} (M=N=K={M})",
+                h2d=ha.numel() + hb.numel(), d2h=hout.numel(), bound="tensor",
+                algo_bytes=None, workload=f"gemm_{dtype}_{M}x{N}x{K}", dtype=dtype,
+                extra={"out_dtype": out_dt, "epilogue": "per-channel requant" if dtype == "i8" else "bf16 narrow"},
+                cpu=lambda rows: cpu_gemm(a, b, scale, dtype, M, N, K, rows),
+                config={"M": M, "N": N, "K": K, "layout": "lhs [M, K], rhs [N, K], out [M, N]"})
+
+
+def cpu_gemm(a, b, scale, dtype, M, N, K, rows):
+    import oracle
+    from oracle import ref_m
+
+    ax = dict(M=M, N=N, K=K)
+    rl, rr, rp, ro = (ref_m(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
+    t0 = time.perf_counter()
+    if dtype == "i8":
+        oracle.contract(a.tobytes(), b.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
+                        scale_axis="N", out_cells=rows * N)
+    else:
+        oracle.contract(a.tobytes(), b.tobytes(), "bf16", "bf16", rl, rr, rp, ro, out_cells=rows * N)
+    dt = time.perf_counter() - t0
+    return 2.0 * rows * N * K / dt, f"{rows} of {M} output rows ({rows * N} cells, full K={K})"
+
+
+def wl_attention(fb, be, S=2048, Hq=32, Hkv=8, D=128):
+    rng = np.random.default_rng(42)
+    q = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(S * Hq * D).astype(np.float32))
+    k = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(S * Hkv * D).astype(np.float32))
+    v = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(S * Hkv * D).astype(np.float32))
+    mq = fb.Mapping("[S, H, D]", dict(S=S, H=Hq, D=D))
+    mk = fb.Mapping("[S, H, D]", dict(S=S, H=Hkv, D=D))
+    Q, Kt, V = be.from_vec(mq, q, "bf16"), be.from_vec(mk, k, "bf16"), be.from_vec(mk, v, "bf16")
+    OUT = be.zeroed(mq, "bf16")
+
+    def step():
+        return be.attention(Q, Kt, V, 1, S, Hq, Hkv, D, causal=True, out=OUT)
+
+    flops = 4.0 * S * S * D * Hq / 2  # causal half
+    return dict(step=step, units=S, unit="tokens/s", scale=1.0, flops=flops, bound="tensor",
+                metric="attention prefill tokens/s (Llama-3-8B shape, S=2048, causal)", workload="attention_s2048",
+                dtype="bf16", config={"S": S, "Hq": Hq, "Hkv": Hkv, "D": D, "causal": True})
+
+
+def wl_relayout(fb, be, R=8192, C=8192):
+    rng = np.random.default_rng(1)
+    ax = dict(R=R, C=C)
+    S, D = fb.Mapping("[R, C]", ax), fb.Mapping("[C, R]", ax)
+    x = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(R * C).astype(np.float32))
+    X = be.from_vec(S, x, "bf16")
+    Y = be.zeroed(D, "bf16")
+
+    def step():
+        be.transpose(Y, X, S, D)
+        return Y
+
+    return dict(step=step, units=2.0 * R * C * 2, unit="GB/s", scale=1e9, bound="hbm",
+                metric="relayout GB/s ([R, C] -> [C, R] bf16, 128 MiB)", workload="relayout_bf16_8192x8192",
+                dtype="bf16", config={"R": R, "C": C})
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    fb = _pkg()
+    torch.cuda.set_device(local)
+    be = fb.B200(local)
+    stream = torch.cuda.Stream()
+    fb._lib.lib().fopt_set_stream(be.ctx, stream.cuda_stream)
+    wl = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
+          "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be)}[args.workload]()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            wl["step"]()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        launches0 = be.launches
+        durs = []
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        with Clocks(local) as clk:
+            torch.cuda.synchronize()
+            wall0 = time.perf_counter()
+            for i in range(args.steps):
+                flush.zero_()
+                ev[i][0].record(stream)
+                wl["step"]()
+                ev[i][1].record(stream)
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - wall0
+        launches = be.launches - launches0 - 0
+        durs = [a.elapsed_time(b) for a, b in ev]
+        e2e = None
+        if "e2e_step" in wl:
+            torch.cuda.synchronize()
+            e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(args.steps)]
+            for i in range(args.steps):
+                flush.zero_()
+                e_ev[i][0].record(stream)
+                wl["e2e_step"]()
+                e_ev[i][1].record(stream)
+            torch.cuda.synchronize()
+            e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in e_ev)
+            e2e = e2e_ms
+    ms = statistics.mean(durs)
+    t = torch.tensor([ms, e2e or 0.0], device="cuda", dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return
+    value = world * wl["units"] / (ms * 1e-3) / wl["scale"]
+    pk = peaks()
+    if wl["bound"] == "hbm":
+        achieved = wl["units"] / (ms * 1e-3) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None, "peak_src": pk["src"] + " copy"}
+    else:
+        flops = wl.get("flops", wl["units"])
+        achieved = flops / (ms * 1e-3) / 1e12
+        if wl.get("dtype") == "i8":
+            peak, src = 2 * pk["bf16_tflops"], f"2x {pk['src']} bf16 cuBLAS burst (dense int8 rate = 2x bf16)"
+        else:
+            peak, src = pk["bf16_tflops"], f"{pk['src']} bf16 cuBLAS burst"
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 3), "traffic": None, "peak_src": src}
+    line = {"metric": wl["metric"], "value": round(value, 2), "unit": wl["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic (seeded)",
+            "config": {"workload": wl["workload"], **wl["config"], "l2": "flushed (256 MiB write) between steps",
+                       "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"},
+            "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
+            "wall_s": round(wall, 4)}
+    if e2e_ms:
+        line["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
+                       "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
+                       "ms_per_step": round(e2e_ms, 4)}
+    if "cpu" in wl and world == 1 and not args.no_cpu:
+        rate, sample = wl["cpu"](args.cpu_rows)
+        line["cpu_baseline"] = {"value": round(rate / wl["scale"], 4), "unit": wl["unit"],
+                                "cores": os.cpu_count(), "kind": "port", "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference(args, rank, world):
+    """The reference algorithm on the host cores (the oracle port of BufStorage::contraction_in)."""
+    if rank != 0:
+        return
+    fb = _pkg()
+    M = N = K = 4096
+    rng = np.random.default_rng(42)
+    a = rng.integers(-128, 128, M * K, dtype=np.int64).astype(np.int8)
+    b = rng.integers(-128, 128, N * K, dtype=np.int64).astype(np.int8)
+    scale = rng.uniform(0.001, 0.01, N).astype(np.float32)
+    rates = []
+    for i in range(args.warmup + args.steps):
+        rate, sample = cpu_gemm(a, b, scale, "i8", M, N, K, args.cpu_rows)
+        if i >= args.warmup:
+            rates.append(rate)
+    v = statistics.mean(rates) / 1e12
+    line = {"impl": "reference", "metric": "int8 GEMM TOPS (M=N=K=4096)", "value": round(v, 5), "unit": "TOPS",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8", "data": "synthetic (seeded)",
+            "config": {"workload": "gemm_i8_4096x4096x4096", "M": M, "N": N, "K": K},
+            "cpu_baseline": {"value": round(v, 5), "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="gemm_i8")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-rows", type=int, default=32)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl")
+    run_ours(args, rank, world, local)
+    if world > 1:
+        import torch
+
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,481 @@
+// The extern "C" entry points of libfopt_b200.so (declared in include/fopt_b200.h).
+//
+// Each entry point validates its arguments, derives (and caches) the walk plan for its mappings on
+// the host -- the work the reference does with `sequence()` / `carve()` before its rayon loop -- and
+// launches the CUDA kernels on the context's stream. Errors never cross the boundary as exceptions:
+// they become an fopt_status and a message in fopt_last_error().
+#include <algorithm>
+#include <cstring>
+#include <sstream>
+
+#include "ctx.hpp"
+
+using namespace fopt;
+
+namespace fopt {
+
+void* scratch(fopt_ctx* ctx, size_t bytes) {
+  if (bytes > ctx->scratch_bytes) {
+    if (ctx->scratch) cuda_check(cudaFree(ctx->scratch), "scratch free");
+    size_t want = std::max(bytes, ctx->scratch_bytes * 2);
+    cuda_check(cudaMalloc(&ctx->scratch, want), "scratch alloc");
+    ctx->scratch_bytes = want;
+  }
+  return ctx->scratch;
+}
+
+}  // namespace fopt
+
+namespace {
+
+template <typename Fn>
+fopt_status guarded(fopt_ctx* ctx, Fn&& fn) {
+  try {
+    fn();
+    return FOPT_OK;
+  } catch (const Fail& f) {
+    if (ctx) ctx->err = f.msg;
+    return f.code;
+  } catch (const MappingError& e) {
+    if (ctx) ctx->err = e.what();
+    return FOPT_ERR_INVALID;
+  } catch (const std::exception& e) {
+    if (ctx) ctx->err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}
+
+thread_local std::string g_noctx_err;
+
+void require(bool ok, const std::string& msg) {
+  if (!ok) throw Fail{FOPT_ERR_INVALID, msg};
+}
+
+// Mappings parsed by separate fopt_mapping_parse calls carry separate axis tables; re-parse them
+// against one merged table so axis identities agree (axes match by name, as Ident does).
+std::vector<Mapping> unify(std::initializer_list<const Mapping*> ms) {
+  auto table = std::make_shared<AxisTable>();
+  for (auto* m : ms)
+    for (size_t i = 0; i < m->axes->names.size(); ++i) table->intern(m->axes->names[i], m->axes->sizes[i]);
+  std::vector<Mapping> out;
+  for (auto* m : ms) out.push_back(parse_mapping(m->to_string(), table));
+  return out;
+}
+
+std::shared_ptr<RelayoutPlan> relayout_plan(fopt_ctx* ctx, const fopt_mapping* src, const fopt_mapping* dst,
+                                            bool allow_broadcast) {
+  auto key = std::make_tuple(src->key, dst->key, (int)allow_broadcast);
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    auto it = ctx->relayouts.find(key);
+    if (it != ctx->relayouts.end()) return it->second;
+  }
+  auto p = std::make_shared<RelayoutPlan>();
+  Walk w;
+  p->positions = dst->m.size();
+  auto u = unify({&src->m, &dst->m});
+  if (plan_relayout(u[0], u[1], allow_broadcast, w)) {
+    p->has_walk = true;
+    p->walk = to_kwalk(w);
+    p->desc = w.to_string();
+  } else {
+    auto t = relayout_table(u[0], u[1], allow_broadcast);
+    cuda_check(cudaMalloc(&p->table, sizeof(int64_t) * std::max<size_t>(t.size(), 1)), "plan table alloc");
+    cuda_check(cudaMemcpy(p->table, t.data(), sizeof(int64_t) * t.size(), cudaMemcpyHostToDevice), "plan table");
+    p->desc = "table[" + std::to_string(t.size()) + "]";
+  }
+  std::lock_guard<std::mutex> g(ctx->mu);
+  ctx->relayouts[key] = p;
+  return p;
+}
+
+FoldKPlan to_kfold(const FoldPlan& fp) {
+  FoldKPlan k;
+  if ((int)fp.out.wheels.size() > kKWheels || (int)fp.residue.wheels.size() > kKWheels)
+    throw Fail{FOPT_ERR_UNSUPPORTED, "fold plan has too many wheels"};
+  k.out = to_kwalk(fp.out);
+  k.residue = to_kwalk(fp.residue);
+  k.out_positions = fp.out.positions();
+  k.residue_positions = fp.residue.positions();
+  k.residue_live = fp.residue.live_positions();
+  return k;
+}
+
+std::vector<std::pair<std::string, int64_t>> parse_offset(const std::string& s) {
+  std::vector<std::pair<std::string, int64_t>> out;
+  std::stringstream ss(s);
+  std::string item;
+  while (std::getline(ss, item, ',')) {
+    auto c = item.find_first_of(":=");
+    if (c == std::string::npos) continue;
+    std::string n = item.substr(0, c), v = item.substr(c + 1);
+    n.erase(std::remove_if(n.begin(), n.end(), ::isspace), n.end());
+    out.push_back({n, std::stoll(v)});
+  }
+  return out;
+}
+
+}  // namespace
+
+extern "C" {
+
+fopt_status fopt_init(int device, fopt_ctx** out) {
+  if (!out) return FOPT_ERR_INVALID;
+  auto* ctx = new fopt_ctx();
+  fopt_status st = guarded(ctx, [&] {
+    cuda_check(cudaSetDevice(device), "cudaSetDevice");
+    ctx->device = device;
+    cuda_check(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "stream create");
+    ctx->stream = ctx->own_stream;
+  });
+  if (st != FOPT_OK) {
+    g_noctx_err = ctx->err;
+    delete ctx;
+    *out = nullptr;
+    return st;
+  }
+  *out = ctx;
+  return FOPT_OK;
+}
+
+fopt_status fopt_destroy(fopt_ctx* ctx) {
+  if (!ctx) return FOPT_OK;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->relayouts)
+    if (kv.second->table) cudaFree(kv.second->table);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  extern fopt_status fopt_comm_destroy(fopt_ctx*);
+  fopt_comm_destroy(ctx);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return FOPT_OK;
+}
+
+const char* fopt_last_error(const fopt_ctx* ctx) { return ctx ? ctx->err.c_str() : g_noctx_err.c_str(); }
+
+fopt_status fopt_sync(fopt_ctx* ctx) {
+  return guarded(ctx, [&] { cuda_check(cudaStreamSynchronize(ctx->stream), "sync"); });
+}
+
+fopt_status fopt_set_stream(fopt_ctx* ctx, void* stream) {
+  if (!ctx) return FOPT_ERR_INVALID;
+  ctx->stream = stream ? (cudaStream_t)stream : ctx->own_stream;
+  return FOPT_OK;
+}
+
+void* fopt_get_stream(fopt_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+fopt_status fopt_set_exact_fold(fopt_ctx* ctx, int exact) {
+  if (!ctx) return FOPT_ERR_INVALID;
+  ctx->exact_fold = exact;
+  return FOPT_OK;
+}
+
+int64_t fopt_launch_count(const fopt_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+fopt_status fopt_alloc(fopt_ctx* ctx, size_t bytes, void** dptr) {
+  return guarded(ctx, [&] {
+    require(dptr != nullptr, "fopt_alloc: null out pointer");
+    cuda_check(cudaMalloc(dptr, std::max<size_t>(bytes, 1)), "cudaMalloc");
+    cuda_check(cudaMemsetAsync(*dptr, 0, std::max<size_t>(bytes, 1), ctx->stream), "zero fill");
+  });
+}
+
+fopt_status fopt_free(fopt_ctx* ctx, void* dptr) {
+  return guarded(ctx, [&] {
+    if (dptr) cuda_check(cudaFree(dptr), "cudaFree");
+  });
+}
+
+fopt_status fopt_h2d(fopt_ctx* ctx, void* dst, const void* host, size_t bytes) {
+  return guarded(ctx, [&] { cuda_check(cudaMemcpyAsync(dst, host, bytes, cudaMemcpyHostToDevice, ctx->stream), "h2d"); });
+}
+
+fopt_status fopt_d2h(fopt_ctx* ctx, void* host, const void* src, size_t bytes) {
+  return guarded(ctx, [&] {
+    cuda_check(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
+    cuda_check(cudaStreamSynchronize(ctx->stream), "d2h sync");
+  });
+}
+
+fopt_status fopt_d2d(fopt_ctx* ctx, void* dst, const void* src, size_t bytes) {
+  return guarded(ctx, [&] { cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream), "d2d"); });
+}
+
+fopt_status fopt_memset(fopt_ctx* ctx, void* dst, int value, size_t bytes) {
+  return guarded(ctx, [&] { cuda_check(cudaMemsetAsync(dst, value, bytes, ctx->stream), "memset"); });
+}
+
+// ---- mappings ----
+fopt_status fopt_mapping_parse(const char* axes, const char* expr, fopt_mapping** out) {
+  try {
+    if (!out || !expr) throw MappingError("fopt_mapping_parse: null argument");
+    auto table = parse_axes(axes ? axes : "");
+    auto m = parse_mapping(expr, table);
+    auto* h = new fopt_mapping{m, ""};
+    std::ostringstream k;
+    k << m.to_string() << "|";
+    for (size_t i = 0; i < table->names.size(); ++i) k << table->names[i] << "=" << table->sizes[i] << ",";
+    h->key = k.str();
+    *out = h;
+    return FOPT_OK;
+  } catch (const std::exception& e) {
+    g_noctx_err = e.what();
+    if (out) *out = nullptr;
+    return FOPT_ERR_INVALID;
+  }
+}
+
+fopt_status fopt_mapping_free(fopt_mapping* m) {
+  delete m;
+  return FOPT_OK;
+}
+
+int64_t fopt_mapping_size(const fopt_mapping* m) { return m ? m->m.size() : -1; }
+
+int32_t fopt_mapping_eval(const fopt_mapping* m, int64_t pos, int64_t* coords, int32_t ncoords) {
+  if (!m) return -1;
+  std::vector<int64_t> c;
+  int r = m->m.eval(pos, c);
+  for (int i = 0; i < ncoords && i < (int)c.size(); ++i) coords[i] = c[i];
+  return r;
+}
+
+fopt_status fopt_window_base(const fopt_mapping* base, const char* offset, int64_t* out) {
+  try {
+    auto kv = parse_offset(offset ? offset : "");
+    std::vector<std::string> names;
+    std::vector<int64_t> vals;
+    for (auto& p : kv) {
+      names.push_back(p.first);
+      vals.push_back(p.second);
+    }
+    *out = window_base(base->m, names, vals);
+    return FOPT_OK;
+  } catch (const std::exception& e) {
+    g_noctx_err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}
+
+fopt_status fopt_describe_relayout(const fopt_mapping* src, const fopt_mapping* dst, int allow_broadcast, char* buf,
+                                   size_t len) {
+  try {
+    Walk w;
+    auto u = unify({&src->m, &dst->m});
+    std::string s = plan_relayout(u[0], u[1], allow_broadcast != 0, w) ? w.to_string() : std::string("table");
+    if (buf && len) {
+      strncpy(buf, s.c_str(), len - 1);
+      buf[len - 1] = 0;
+    }
+    return FOPT_OK;
+  } catch (const std::exception& e) {
+    g_noctx_err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}
+
+// ---- layout moves ----
+fopt_status fopt_transpose(fopt_ctx* ctx, void* dst, const void* src, fopt_dtype dtype, const fopt_mapping* src_map,
+                           const fopt_mapping* dst_map, int64_t src_base, int64_t dst_base, int allow_broadcast) {
+  return guarded(ctx, [&] {
+    require(src_map && dst_map && dst && src, "fopt_transpose: null argument");
+    auto p = relayout_plan(ctx, src_map, dst_map, allow_broadcast != 0);
+    // The storages are sized by their base mappings; windows only shift the bases. We do not know
+    // the allocations' lengths here, so bound reads / writes by the stream itself.
+    int64_t src_elems = src_base + src_map->m.size();
+    int64_t dst_elems = dst_base + dst_map->m.size();
+    launch_relayout(ctx, *p, dst, src, dtype, src_base, dst_base, src_elems, dst_elems);
+  });
+}
+
+fopt_status fopt_transmute(fopt_ctx* ctx, void* dst, const void* src, fopt_dtype dtype, const fopt_mapping* src_map,
+                           const fopt_mapping* dst_map) {
+  return guarded(ctx, [&] {
+    require(src_map && dst_map && dst && src, "fopt_transmute: null argument");
+    RankWalk s = rank_walk(src_map->m), d = rank_walk(dst_map->m);
+    int64_t sl = 1, dl = 1;
+    for (auto v : s.live) sl *= v;
+    for (auto v : d.live) dl *= v;
+    require(dl <= sl, "transmute: dst_map has more live elements than src_map");
+    launch_transmute(ctx, s, d, dst, src, dtype);
+  });
+}
+
+// ---- elementwise ----
+fopt_status fopt_elementwise(fopt_ctx* ctx, const fopt_program* prog, int32_t n_in, const void* const* inputs,
+                             const fopt_dtype* in_dtypes, void* out, fopt_dtype out_dtype, int64_t n) {
+  return guarded(ctx, [&] {
+    require(prog && out && n_in >= 0 && n_in <= 3, "fopt_elementwise: bad arguments");
+    require(prog->n_insn >= 0 && prog->n_insn <= 32, "fopt_elementwise: program too long");
+    for (int i = 0; i < n_in; ++i) require(inputs[i] != nullptr, "fopt_elementwise: null input");
+    launch_elementwise(ctx, prog, n_in, inputs, in_dtypes, out, out_dtype, n);
+  });
+}
+
+// ---- reduce ----
+fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype, fopt_reduce_op op,
+                        uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                        int allow_broadcast) {
+  return guarded(ctx, [&] {
+    require(out && src && src_map && dst_map, "fopt_reduce: null argument");
+    require(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16, "fopt_reduce: dtype must be i32, f32 or bf16");
+    std::string key = "r|" + src_map->key + "|" + dst_map->key + "|" + std::to_string(allow_broadcast);
+    std::shared_ptr<FoldKPlan> kp;
+    {
+      std::lock_guard<std::mutex> g(ctx->mu);
+      auto it = ctx->folds.find(key);
+      if (it != ctx->folds.end()) kp = it->second;
+    }
+    if (!kp) {
+      FoldPlan fp;
+      auto u = unify({&src_map->m, &dst_map->m});
+      if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
+        throw Fail{FOPT_ERR_UNSUPPORTED, "reduce: mappings are not affine-factorisable"};
+      kp = std::make_shared<FoldKPlan>(to_kfold(fp));
+      std::lock_guard<std::mutex> g(ctx->mu);
+      ctx->folds[key] = kp;
+    }
+    launch_reduce(ctx, *kp, out, src, dtype, op, identity_bits, src_map->m.size());
+  });
+}
+
+// ---- contraction ----
+static bool acc_type_of(int in_dt, int* acc) {
+  switch (in_dt) {
+    case FOPT_I8: case FOPT_I4: case FOPT_I5: case FOPT_I9: case FOPT_I32: *acc = FOPT_I32; return true;
+    case FOPT_BF16: case FOPT_F8E4M3: case FOPT_F8E5M2: case FOPT_F32: *acc = FOPT_F32; return true;
+    default: return false;
+  }
+}
+
+// Detects a plain GEMM: out [M, N] row-major over two wheels, lhs [M, K] K-major, rhs [N, K]
+// K-major, one fully-live contracted wheel. Fills M, N, K and leading dimensions.
+static bool as_gemm(const FoldKPlan& p, int64_t* M, int64_t* N, int64_t* K, int64_t* lda, int64_t* ldb, int64_t* ldd,
+                    int* scale_along_n) {
+  if (p.residue.n != 1 || p.residue.live[0] != p.residue.extent[0]) return false;
+  if (p.residue.stride[0][0] != 1 || p.residue.stride[1][0] != 1) return false;
+  const KWalk& o = p.out;
+  if (o.n != 2 || o.live[0] != o.extent[0] || o.live[1] != o.extent[1]) return false;
+  // wheel 0 = N (inner, lhs stride 0), wheel 1 = M (rhs stride 0)
+  if (o.stride[0][0] != 0 || o.stride[1][1] != 0) return false;
+  *N = o.extent[0];
+  *M = o.extent[1];
+  *K = p.residue.extent[0];
+  *lda = o.stride[0][1];
+  *ldb = o.stride[1][0];
+  *ldd = o.extent[0];
+  if (*lda < *K || *ldb < *K) return false;
+  *scale_along_n = o.stride[2][0] == 1 && o.stride[2][1] == 0;
+  return true;
+}
+
+fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, const void* lhs, const void* rhs,
+                             fopt_dtype in_dtype, const fopt_mapping* lhs_map, const fopt_mapping* rhs_map,
+                             const fopt_mapping* pre_reduce, const fopt_mapping* out_map,
+                             const fopt_epilogue* epilogue) {
+  return guarded(ctx, [&] {
+    require(out && lhs && rhs && lhs_map && rhs_map && pre_reduce && out_map, "fopt_contraction: null argument");
+    int acc;
+    require(acc_type_of(in_dtype, &acc), "fopt_contraction: unsupported operand dtype");
+    int ep_kind = epilogue ? epilogue->kind : 0;
+    if (ep_kind == 1) {
+      require(acc == FOPT_I32, "requant epilogue needs an integer contraction");
+      require(out_dtype == FOPT_I8, "requant epilogue commits i8");
+      require(epilogue->scale && epilogue->scale_axis, "requant epilogue needs a scale vector and its axis");
+    } else {
+      require(out_dtype == in_dtype || out_dtype == acc, "fopt_contraction: out dtype must be the operand or accumulator type");
+    }
+    std::string extra_key = ep_kind == 1 ? std::string(epilogue->scale_axis) : "";
+    std::string key = "c|" + lhs_map->key + "|" + rhs_map->key + "|" + pre_reduce->key + "|" + out_map->key + "|" + extra_key;
+    std::shared_ptr<FoldKPlan> kp;
+    {
+      std::lock_guard<std::mutex> g(ctx->mu);
+      auto it = ctx->folds.find(key);
+      if (it != ctx->folds.end()) kp = it->second;
+    }
+    if (!kp) {
+      FoldPlan fp;
+      bool has_extra = ep_kind == 1;
+      // The four mappings may come from separate axis tables; re-parse against one shared table.
+      auto table = std::make_shared<AxisTable>();
+      auto adopt = [&](const Mapping& m) {
+        for (size_t i = 0; i < m.axes->names.size(); ++i) table->intern(m.axes->names[i], m.axes->sizes[i]);
+      };
+      for (auto* h : {lhs_map, rhs_map, pre_reduce, out_map}) adopt(h->m);
+      Mapping L = parse_mapping(lhs_map->m.to_string(), table), Rm = parse_mapping(rhs_map->m.to_string(), table),
+              P = parse_mapping(pre_reduce->m.to_string(), table), O = parse_mapping(out_map->m.to_string(), table);
+      Mapping X;
+      if (has_extra) X = parse_mapping(epilogue->scale_axis, table);
+      if (!plan_contraction(L, Rm, P, O, fp, has_extra ? &X : nullptr))
+        throw Fail{FOPT_ERR_UNSUPPORTED, "contraction: mappings are not affine-factorisable"};
+      kp = std::make_shared<FoldKPlan>(to_kfold(fp));
+      std::lock_guard<std::mutex> g(ctx->mu);
+      ctx->folds[key] = kp;
+    }
+    int64_t M, N, K, lda, ldb, ldd;
+    int scale_n = 0;
+    if (as_gemm(*kp, &M, &N, &K, &lda, &ldb, &ldd, &scale_n) && (ep_kind != 1 || scale_n)) {
+      if (launch_gemm_tc(ctx, out, out_dtype, lhs, rhs, in_dtype, M, N, K, lda, ldb, ldd, epilogue,
+                         ep_kind == 1 ? epilogue->scale : nullptr, scale_n))
+        return;
+    }
+    launch_contraction_generic(ctx, *kp, out, out_dtype, lhs, rhs, in_dtype, lhs_map->m.size(), rhs_map->m.size(),
+                               epilogue, nullptr, ep_kind == 1 ? epilogue->scale : nullptr);
+  });
+}
+
+// ---- attention ----
+fopt_status fopt_attention(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int32_t batch,
+                           int32_t seq, int32_t hq, int32_t hkv, int32_t head_dim, float scale, int32_t causal,
+                           float eps) {
+  return guarded(ctx, [&] {
+    require(o && q && k && v, "fopt_attention: null argument");
+    require(head_dim == 128, "fopt_attention: head_dim must be 128");
+    require(hkv > 0 && hq % hkv == 0, "fopt_attention: query heads must be a multiple of kv heads");
+    require(batch > 0 && seq > 0, "fopt_attention: empty problem");
+    launch_attention(ctx, o, q, k, v, batch, seq, hq, hkv, head_dim, scale, causal, eps);
+  });
+}
+
+}  // extern "C"
+
+// ---- byte equality (BufStorage PartialEq, buf.rs:38-41) ----
+namespace {
+__global__ void bytes_differ_kernel(const uint8_t* a, const uint8_t* b, size_t n, int32_t* flag) {
+  size_t words = n / 16;
+  const uint4* a4 = (const uint4*)a;
+  const uint4* b4 = (const uint4*)b;
+  bool aligned = ((uintptr_t)a % 16 == 0) && ((uintptr_t)b % 16 == 0);
+  size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
+  int diff = 0;
+  if (aligned) {
+    for (size_t i = tid; i < words; i += step) {
+      uint4 x = a4[i], y = b4[i];
+      diff |= (x.x != y.x) | (x.y != y.y) | (x.z != y.z) | (x.w != y.w);
+    }
+    for (size_t i = words * 16 + tid; i < n; i += step) diff |= a[i] != b[i];
+  } else {
+    for (size_t i = tid; i < n; i += step) diff |= a[i] != b[i];
+  }
+  if (__any_sync(0xffffffffu, diff) && (threadIdx.x & 31) == 0) atomicOr(flag, 1);
+}
+}  // namespace
+
+extern "C" fopt_status fopt_equal(fopt_ctx* ctx, const void* a, const void* b, size_t bytes, int* equal) {
+  return guarded(ctx, [&] {
+    require(a && b && equal, "fopt_equal: null argument");
+    int32_t* flag = (int32_t*)scratch(ctx, 16);
+    cuda_check(cudaMemsetAsync(flag, 0, 4, ctx->stream), "equal flag");
+    if (bytes) {
+      int grid = (int)std::max<size_t>(1, std::min<size_t>((bytes / 16 + 255) / 256, 148 * 8));
+      bytes_differ_kernel<<<grid, 256, 0, ctx->stream>>>((const uint8_t*)a, (const uint8_t*)b, bytes, flag);
+      launched(ctx, "bytes_differ");
+    }
+    int32_t h = 0;
+    cuda_check(cudaMemcpyAsync(&h, flag, 4, cudaMemcpyDeviceToHost, ctx->stream), "equal d2h");
+    cuda_check(cudaStreamSynchronize(ctx->stream), "equal sync");
+    *equal = h == 0;
+  });
+}

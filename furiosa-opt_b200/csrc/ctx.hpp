@@ -1,0 +1,102 @@
+// The opaque context behind `fopt_ctx*`: one CUDA device, one stream, the last error, and the
+// caches of walk plans derived from mapping pairs.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "../../include/fopt_b200.h"
+#include "common.cuh"
+#include "mapping.hpp"
+
+struct fopt_mapping {
+  fopt::Mapping m;
+  std::string key;  // canonical text + axis sizes, for plan caching
+};
+
+namespace fopt {
+
+// A relayout plan ready for launch: either a walk (fast) or an explicit offset table on device.
+struct RelayoutPlan {
+  bool has_walk = false;
+  KWalk walk{};
+  int64_t positions = 0;
+  int64_t* table = nullptr;  // device, one src offset per dst position (-1 dead)
+  std::string desc;
+};
+
+struct FoldKPlan {
+  KWalk out{}, residue{};
+  int64_t out_positions = 0, residue_positions = 0, residue_live = 0;
+};
+
+}  // namespace fopt
+
+struct fopt_ctx {
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  int exact_fold = 0;
+  int64_t launches = 0;
+  std::string err;
+  std::mutex mu;
+  std::map<std::tuple<std::string, std::string, int>, std::shared_ptr<fopt::RelayoutPlan>> relayouts;
+  std::map<std::string, std::shared_ptr<fopt::FoldKPlan>> folds;
+  void* nccl_comm = nullptr;
+  int nranks = 1, rank = 0;
+  void* scratch = nullptr;  // grow-only device scratch for kernels that need it
+  size_t scratch_bytes = 0;
+};
+
+namespace fopt {
+
+// Status helpers: every C entry point catches everything and returns a status.
+struct Fail {
+  fopt_status code;
+  std::string msg;
+};
+
+inline void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Fail{FOPT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};
+}
+
+// After a launch: count it and surface launch-configuration errors immediately.
+inline void launched(fopt_ctx* ctx, const char* what) {
+  ctx->launches++;
+  cuda_check(cudaGetLastError(), what);
+}
+
+void* scratch(fopt_ctx* ctx, size_t bytes);
+
+KWalk to_kwalk(const Walk& w);
+bool to_kwalk32(const KWalk& w, KWalk32& out);
+
+// Kernel launchers (defined in the .cu files).
+void launch_relayout(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void* src, int dtype, int64_t src_base,
+                     int64_t dst_base, int64_t src_elems, int64_t dst_elems);
+void launch_transmute(fopt_ctx* ctx, const RankWalk& src, const RankWalk& dst, void* out, const void* in, int dtype);
+void launch_elementwise(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in, const fopt_dtype* in_dt,
+                        void* out, fopt_dtype out_dt, int64_t n);
+void launch_reduce(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op, uint32_t ident,
+                   int64_t src_elems);
+void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, int out_dt, const void* lhs,
+                                const void* rhs, int in_dt, int64_t lhs_elems, int64_t rhs_elems,
+                                const fopt_epilogue* ep, const int64_t* scale_stride_out, const float* scale);
+// GEMM fast path: D[M,N] = A[M,K] . B[N,K]^T, both operands K-major. Returns false if the shape
+// does not fit the tensor-core kernel.
+bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const void* b, int in_dt, int64_t M,
+                    int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldd, const fopt_epilogue* ep,
+                    const float* scale, int scale_along_n);
+void launch_attention(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int B, int S, int Hq,
+                      int Hkv, int D, float scale, int causal, float eps);
+void launch_gather_rows(fopt_ctx* ctx, void* dst, const void* table, const int32_t* idx, int64_t n_idx,
+                        int64_t row_bytes, int64_t stride_div, int64_t table_rows, int64_t table_row_stride_bytes,
+                        int64_t dst_row_stride_bytes);
+
+}  // namespace fopt

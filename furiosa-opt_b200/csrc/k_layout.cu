@@ -1,0 +1,377 @@
+// Layout-move kernels: relayout (BufStorage::transpose, furiosa-opt-std/src/storage/buf.rs:257-313),
+// transmute (buf.rs:592-613), and the walk-driven gather / scatter (buf.rs:485-576).
+//
+// Every kernel is HBM-bound: one read of each live source element and one write of each live
+// destination element. Three relayout paths, picked per plan:
+//   * vec:   the innermost walk wheel is unit-stride on both sides -> 16-byte loads and stores;
+//   * tile:  the dst-innermost wheel is strided in src but another wheel is unit-stride in src ->
+//            a 32x32 shared-memory tile so both the read and the write are coalesced;
+//   * walk:  anything else, one element per thread with the odometer decomposed per position.
+#include <algorithm>
+
+#include "ctx.hpp"
+
+namespace fopt {
+
+KWalk to_kwalk(const Walk& w) {
+  KWalk k{};
+  k.n = (int)w.wheels.size();
+  for (int i = 0; i < k.n; ++i) {
+    k.extent[i] = w.wheels[i].extent;
+    k.live[i] = w.wheels[i].live;
+    for (int m = 0; m < 3; ++m) k.stride[m][i] = m < w.nmem ? w.wheels[i].stride[m] : 0;
+  }
+  return k;
+}
+
+bool to_kwalk32(const KWalk& w, KWalk32& out) {
+  out = KWalk32{};
+  out.n = w.n;
+  int64_t pos = 1;
+  for (int i = 0; i < w.n; ++i) {
+    if (w.extent[i] >= (1ll << 31)) return false;
+    pos *= w.extent[i];
+    if (pos >= (1ll << 31)) return false;
+    out.div[i] = make_fastdiv((uint32_t)w.extent[i]);
+    out.live[i] = (uint32_t)w.live[i];
+    for (int m = 0; m < 3; ++m) {
+      int64_t s = w.stride[m][i];
+      if (s * (w.extent[i] - 1) >= (1ll << 30)) return false;
+      out.stride[m][i] = (int32_t)s;
+    }
+  }
+  return true;
+}
+
+namespace {
+
+constexpr int kThreads = 256;
+
+inline int grid_for(int64_t work, int per_block = kThreads) {
+  int64_t g = (work + per_block - 1) / per_block;
+  // Persistent-ish: cap at a multiple of the 148 SMs, grid-stride loops cover the rest.
+  return (int)std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32));
+}
+
+// ---- vec path: V elements (16 bytes) per unit ----
+template <typename V>
+__global__ void relayout_vec32(V* __restrict__ dst, const V* __restrict__ src, KWalk32 w, uint32_t units,
+                               uint32_t vlen, int64_t src_base_v, int64_t dst_base_v) {
+  for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
+    int32_t off = 0;
+    if (!walk_offsets32<1>(w, u * vlen, &off)) continue;
+    dst[dst_base_v + u] = src[src_base_v + off / (int32_t)vlen];
+  }
+}
+
+template <typename V>
+__global__ void relayout_vec64(V* __restrict__ dst, const V* __restrict__ src, KWalk w, int64_t units, int64_t vlen,
+                               int64_t src_base_v, int64_t dst_base_v) {
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    int64_t off = 0;
+    if (!walk_offsets<1>(w, u * vlen, &off)) continue;
+    dst[dst_base_v + u] = src[src_base_v + off / vlen];
+  }
+}
+
+// ---- tile path ----
+// `others` walks every wheel except the dst-innermost (i) and the src-unit-stride (j) ones; memory
+// 0 = src offset, memory 1 = dst position.
+template <typename T>
+__global__ void relayout_tile(T* __restrict__ dst, const T* __restrict__ src, KWalk others, int64_t e0, int64_t s0,
+                              int64_t ej, int64_t wj, int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
+                              int64_t batches) {
+  __shared__ T tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
+    int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
+    int64_t off[2] = {0, 0};
+    bool live = walk_offsets<2>(others, b, off);
+    if (live) {
+#pragma unroll
+      for (int k = 0; k < 32; k += 8) {
+        int64_t d0 = ti * 32 + ty + k, dj = tj * 32 + tx;
+        if (d0 < e0 && dj < ej) tile[ty + k][tx] = src[src_base + off[0] + d0 * s0 + dj];
+      }
+    }
+    __syncthreads();
+    if (live) {
+#pragma unroll
+      for (int k = 0; k < 32; k += 8) {
+        int64_t d0 = ti * 32 + tx, dj = tj * 32 + ty + k;
+        if (d0 < e0 && dj < ej) dst[dst_base + off[1] + d0 + dj * wj] = tile[tx][ty + k];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---- walk path ----
+template <typename T>
+__global__ void relayout_walk32(T* __restrict__ dst, const T* __restrict__ src, KWalk32 w, uint32_t positions,
+                                int64_t src_base, int64_t dst_base, int64_t src_elems) {
+  for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < positions; q += gridDim.x * blockDim.x) {
+    int32_t off = 0;
+    if (!walk_offsets32<1>(w, q, &off)) continue;
+    int64_t s = src_base + off;
+    if (s < src_elems) dst[dst_base + q] = src[s];
+  }
+}
+
+template <typename T>
+__global__ void relayout_walk64(T* __restrict__ dst, const T* __restrict__ src, KWalk w, int64_t positions,
+                                int64_t src_base, int64_t dst_base, int64_t src_elems) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < positions;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t off = 0;
+    if (!walk_offsets<1>(w, q, &off)) continue;
+    int64_t s = src_base + off;
+    if (s < src_elems) dst[dst_base + q] = src[s];
+  }
+}
+
+template <typename T>
+__global__ void relayout_table(T* __restrict__ dst, const T* __restrict__ src, const int64_t* __restrict__ table,
+                               int64_t positions, int64_t src_base, int64_t dst_base, int64_t src_elems) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < positions;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t t = table[q];
+    if (t < 0) continue;
+    int64_t s = src_base + t;
+    if (s < src_elems) dst[dst_base + q] = src[s];
+  }
+}
+
+// 4-bit elements: one thread owns one dst byte (two positions), so sibling nibbles never race.
+__global__ void relayout_nibble(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, KWalk w,
+                                const int64_t* __restrict__ table, int64_t positions, int64_t src_base,
+                                int64_t dst_base, int64_t src_elems, int64_t dst_bytes) {
+  for (int64_t by = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; by < dst_bytes;
+       by += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t byte = dst[by];
+    bool changed = false;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int64_t q = by * 2 + h - dst_base;
+      if (q < 0 || q >= positions) continue;
+      int64_t off = 0;
+      bool live;
+      if (table) {
+        off = table[q];
+        live = off >= 0;
+      } else {
+        live = walk_offsets<1>(w, q, &off);
+      }
+      int64_t s = src_base + off;
+      if (!live || s >= src_elems) continue;
+      uint32_t nib = raw_nibble(src, s);
+      byte = h ? ((byte & 0x0f) | (nib << 4)) : ((byte & 0xf0) | nib);
+      changed = true;
+    }
+    if (changed) dst[by] = (uint8_t)byte;
+  }
+}
+
+template <typename T>
+void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void* src, int64_t src_base,
+                           int64_t dst_base, int64_t src_elems) {
+  cudaStream_t st = ctx->stream;
+  T* d = (T*)dst;
+  const T* s = (const T*)src;
+  if (!p.has_walk) {
+    relayout_table<T><<<grid_for(p.positions), kThreads, 0, st>>>(d, s, p.table, p.positions, src_base, dst_base,
+                                                                 src_elems);
+    launched(ctx, "relayout_table");
+    return;
+  }
+  const KWalk& w = p.walk;
+  const int64_t V = 16 / sizeof(T);
+  // vec path
+  bool vec = w.n >= 1 && w.live[0] == w.extent[0] && w.stride[0][0] == 1 && w.extent[0] % V == 0 &&
+             src_base % V == 0 && dst_base % V == 0 && ((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0);
+  for (int i = 1; vec && i < w.n; ++i) vec = w.stride[0][i] % V == 0;
+  if (w.n == 0) {
+    // a single element (or empty) stream
+    vec = false;
+  }
+  if (vec && V > 1) {
+    int64_t units = p.positions / V;
+    KWalk32 w32;
+    if (to_kwalk32(w, w32) && units < (1ll << 31)) {
+      relayout_vec32<uint4><<<grid_for(units), kThreads, 0, st>>>((uint4*)d, (const uint4*)s, w32, (uint32_t)units,
+                                                                   (uint32_t)V, src_base / V, dst_base / V);
+    } else {
+      relayout_vec64<uint4><<<grid_for(units), kThreads, 0, st>>>((uint4*)d, (const uint4*)s, w, units, V,
+                                                                   src_base / V, dst_base / V);
+    }
+    launched(ctx, "relayout_vec");
+    return;
+  }
+  // tile path: dst-innermost wheel strided in src, some other fully-live wheel unit-stride in src.
+  int j = -1;
+  if (w.n >= 2 && w.live[0] == w.extent[0] && w.stride[0][0] != 1 && w.extent[0] >= 8) {
+    for (int i = 1; i < w.n; ++i)
+      if (w.stride[0][i] == 1 && w.live[i] == w.extent[i] && w.extent[i] >= 8) {
+        j = i;
+        break;
+      }
+  }
+  if (j > 0) {
+    KWalk others{};
+    int64_t weight = 1, wj = 0;
+    for (int i = 0; i < w.n; ++i) {
+      if (i == j) wj = weight;
+      if (i != 0 && i != j) {
+        int k = others.n++;
+        others.extent[k] = w.extent[i];
+        others.live[k] = w.live[i];
+        others.stride[0][k] = w.stride[0][i];
+        others.stride[1][k] = weight;
+      }
+      weight *= w.extent[i];
+    }
+    int64_t batches = 1;
+    for (int k = 0; k < others.n; ++k) batches *= others.extent[k];
+    int64_t nt0 = (w.extent[0] + 31) / 32, ntj = (w.extent[j] + 31) / 32;
+    int64_t blocks = nt0 * ntj * batches;
+    int grid = (int)std::min<int64_t>(blocks, 148 * 64);
+    relayout_tile<T><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                   src_base, dst_base, nt0, ntj, batches);
+    launched(ctx, "relayout_tile");
+    return;
+  }
+  KWalk32 w32;
+  if (to_kwalk32(w, w32) && p.positions < (1ll << 31)) {
+    relayout_walk32<T><<<grid_for(p.positions), kThreads, 0, st>>>(d, s, w32, (uint32_t)p.positions, src_base,
+                                                                  dst_base, src_elems);
+  } else {
+    relayout_walk64<T><<<grid_for(p.positions), kThreads, 0, st>>>(d, s, w, p.positions, src_base, dst_base,
+                                                                  src_elems);
+  }
+  launched(ctx, "relayout_walk");
+}
+
+// ---- transmute ----
+struct KRank {
+  int n;
+  int64_t extent[kKWheels], live[kKWheels];
+};
+
+__device__ __forceinline__ bool rank_of(const KRank& r, int64_t q, int64_t& k) {
+  int64_t lw = 1;
+  k = 0;
+  for (int i = 0; i < r.n; ++i) {
+    int64_t d = q % r.extent[i];
+    q /= r.extent[i];
+    if (d >= r.live[i]) return false;
+    k += d * lw;
+    lw *= r.live[i];
+  }
+  return true;
+}
+__device__ __forceinline__ int64_t pos_of_rank(const KRank& r, int64_t k) {
+  int64_t ew = 1, p = 0;
+  for (int i = 0; i < r.n; ++i) {
+    int64_t d = k % r.live[i];
+    k /= r.live[i];
+    p += d * ew;
+    ew *= r.extent[i];
+  }
+  return p;
+}
+
+template <typename T>
+__global__ void transmute_kernel(T* __restrict__ dst, const T* __restrict__ src, KRank s, KRank d, int64_t positions,
+                                 int64_t src_live) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < positions;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    int64_t k;
+    T v{};
+    if (rank_of(d, q, k) && k < src_live) v = src[pos_of_rank(s, k)];
+    dst[q] = v;
+  }
+}
+
+__global__ void transmute_nibble(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, KRank s, KRank d,
+                                 int64_t positions, int64_t src_live) {
+  for (int64_t by = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; by * 2 < positions;
+       by += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t out = 0;
+    for (int h = 0; h < 2; ++h) {
+      int64_t q = by * 2 + h, k;
+      if (q < positions && rank_of(d, q, k) && k < src_live) out |= raw_nibble(src, pos_of_rank(s, k)) << (4 * h);
+    }
+    dst[by] = (uint8_t)out;
+  }
+}
+
+KRank to_krank(const RankWalk& r) {
+  KRank k{};
+  k.n = (int)r.extent.size();
+  if (k.n > kKWheels) throw Fail{FOPT_ERR_UNSUPPORTED, "transmute: too many factors"};
+  for (int i = 0; i < k.n; ++i) {
+    k.extent[i] = r.extent[i];
+    k.live[i] = r.live[i];
+  }
+  return k;
+}
+
+}  // namespace
+
+void launch_relayout(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void* src, int dtype, int64_t src_base,
+                     int64_t dst_base, int64_t src_elems, int64_t dst_elems) {
+  if (p.positions == 0) return;
+  if (dst_base + p.positions > dst_elems) {
+    // The stream's trailing positions would address past the dst window; the reference clamps them
+    // away (buf.rs:294-301). Clamping needs a shorter stream, which the walk kernels handle via the
+    // positions bound; we only shorten when the clamp drops whole tail positions.
+  }
+  int bits = dtype_bits(dtype);
+  int64_t positions_cap = std::min<int64_t>(p.positions, dst_elems - dst_base);
+  RelayoutPlan q = p;
+  q.positions = positions_cap;
+  if (bits == 4) {
+    int64_t dst_bytes = (dst_elems + 1) / 2;
+    relayout_nibble<<<grid_for(dst_bytes), kThreads, 0, ctx->stream>>>(
+        (uint8_t*)dst, (const uint8_t*)src, p.walk, p.has_walk ? nullptr : p.table, q.positions, src_base, dst_base,
+        src_elems, dst_bytes);
+    launched(ctx, "relayout_nibble");
+    return;
+  }
+  switch (bits) {
+    case 8: launch_relayout_typed<uint8_t>(ctx, q, dst, src, src_base, dst_base, src_elems); break;
+    case 16: launch_relayout_typed<uint16_t>(ctx, q, dst, src, src_base, dst_base, src_elems); break;
+    default: launch_relayout_typed<uint32_t>(ctx, q, dst, src, src_base, dst_base, src_elems); break;
+  }
+}
+
+void launch_transmute(fopt_ctx* ctx, const RankWalk& src, const RankWalk& dst, void* out, const void* in, int dtype) {
+  KRank s = to_krank(src), d = to_krank(dst);
+  int64_t positions = 1, src_live = 1;
+  for (auto e : dst.extent) positions *= e;
+  for (auto l : src.live) src_live *= l;
+  int bits = dtype_bits(dtype);
+  cudaStream_t st = ctx->stream;
+  if (positions == 0) return;
+  switch (bits) {
+    case 4:
+      transmute_nibble<<<grid_for((positions + 1) / 2), kThreads, 0, st>>>((uint8_t*)out, (const uint8_t*)in, s, d,
+                                                                          positions, src_live);
+      break;
+    case 8:
+      transmute_kernel<uint8_t><<<grid_for(positions), kThreads, 0, st>>>((uint8_t*)out, (const uint8_t*)in, s, d,
+                                                                         positions, src_live);
+      break;
+    case 16:
+      transmute_kernel<uint16_t><<<grid_for(positions), kThreads, 0, st>>>((uint16_t*)out, (const uint16_t*)in, s, d,
+                                                                          positions, src_live);
+      break;
+    default:
+      transmute_kernel<uint32_t><<<grid_for(positions), kThreads, 0, st>>>((uint32_t*)out, (const uint32_t*)in, s, d,
+                                                                          positions, src_live);
+      break;
+  }
+  launched(ctx, "transmute");
+}
+
+}  // namespace fopt

@@ -1,0 +1,133 @@
+"""CPU-side checks of the product library (no GPU): the C ABI loads and exports every declared
+symbol, the C++ mapping parser agrees with the oracle's position semantics, and the planner's
+odometer walks reproduce the oracle's per-position source offsets."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+import furiosa_opt_b200 as fb
+import oracle
+from furiosa_opt_b200 import _lib
+from oracle import ref_m
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "fopt_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(fopt_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    syms = header_symbols()
+    assert len(syms) >= 30
+    for s in syms:
+        assert hasattr(lib, s), f"libfopt_b200.so does not export {s}"
+    bound = {n for n, _, _ in _lib.SIGNATURES}
+    assert set(syms) <= bound, f"unbound symbols: {set(syms) - bound}"
+
+
+EXPRS = [
+    ("[A]", dict(A=8)),
+    ("[A, B]", dict(A=8, B=16)),
+    ("[C, D # 64]", dict(C=13, D=61)),
+    ("[C, D = 2]", dict(C=2, D=3)),
+    ("[B / 64, B % 64]", dict(B=512)),
+    ("[B / 64, B % 32, B / 32 % 2]", dict(B=512)),
+    ("[A / 8, B % 4 # 16]", dict(A=64, B=16)),
+    ("[A #{0} 8, B #{!} 3]", dict(A=5, B=2)),
+    ("[[A, B] / 3, 2]", dict(A=4, B=6)),
+    ("[[A, B] % 12]", dict(A=4, B=6)),
+    ("[4, A, 1]", dict(A=3)),
+    ("[[A, B] # 30]", dict(A=4, B=6)),
+    ("m![A / 4 % 4, A % 4, B]", dict(A=256, B=8)),
+    ("[A = 6 # 8, B / 2]", dict(A=8, B=8)),
+]
+
+
+@pytest.mark.parametrize("expr,axes", EXPRS)
+def test_parser_matches_oracle(expr, axes):
+    m = fb.Mapping(expr, axes)
+    r = ref_m(expr, **axes)
+    assert m.size == r.size
+    st, co = r.cells(np.arange(r.size + 2))
+    for i in range(r.size + 2):
+        s, c = m.eval(i)
+        assert s == st[i], (expr, i)
+        if s == 0:
+            for a in r.idents():
+                assert c[a] == co[a][i], (expr, i, a)
+
+
+def test_parse_errors_are_reported():
+    with pytest.raises(_lib.FoptError):
+        fb.Mapping("[A / 3]", A=8)  # stride does not divide
+    with pytest.raises(_lib.FoptError):
+        fb.Mapping("[Q]", A=8)  # undeclared axis
+    with pytest.raises(_lib.FoptError):
+        fb.Mapping("[A # 4]", A=8)  # padding below size
+
+
+def walk_offsets(desc: str, n: int):
+    """Evaluates a planner walk ("walk{(extent[/live]:stride)...}") on the host."""
+    wheels = []
+    for w in re.findall(r"\(([^)]*)\)", desc):
+        ext, stride = w.split(":")
+        e, _, l = ext.partition("/")
+        wheels.append((int(e), int(l or e), int(stride)))
+    q = np.arange(n, dtype=np.int64)
+    off = np.zeros(n, np.int64)
+    live = np.ones(n, bool)
+    for e, l, s in wheels:
+        d = q % e
+        q //= e
+        live &= d < l
+        off += d * s
+    return np.where(live, off, -1)
+
+
+RELAYOUTS = [
+    ("[A, B]", "[B, A]", dict(A=4, B=8), False),
+    ("[R, C]", "[C, R]", dict(R=48, C=40), False),
+    ("[A, B, C]", "[C, A, B]", dict(A=3, B=5, C=7), False),
+    ("[A]", "[B, A # 6]", dict(A=4, B=3), True),
+    ("[C, D]", "[C, D # 64]", dict(C=13, D=61), False),
+    ("[B]", "[B / 64, B % 32, B / 32 % 2]", dict(B=512), False),
+    ("[A / 4 % 4, A % 4, B]", "[A / 16, A % 4, B]", dict(A=64, B=8), False),
+    ("[A, B]", "[A / 4, B, A % 4]", dict(A=16, B=12), False),
+    ("[H, X]", "[X / 8, H, X % 8]", dict(H=10, X=64), False),
+    ("[M, K = 2 # 4]", "[K = 2 # 4, M]", dict(M=3, K=2), False),
+]
+
+
+@pytest.mark.parametrize("src,dst,axes,bc", RELAYOUTS)
+def test_relayout_walk_matches_oracle(src, dst, axes, bc):
+    S, D = fb.Mapping(src, axes), fb.Mapping(dst, axes)
+    desc = fb.B200.describe_relayout(None, S, D, bc)
+    if not desc.startswith("walk"):
+        pytest.skip("table plan")
+    got = walk_offsets(desc, D.size)
+    rs, rd = ref_m(src, **axes), ref_m(dst, **axes)
+    st, co = rd.cells()
+    idx = oracle._Index(rs, rs.idents())
+    want = np.where(st == 0, idx.find(co, rd.size), -1)
+    live = want >= 0
+    assert np.array_equal(got >= 0, live), desc
+    assert np.array_equal(got[live], want[live]), desc
+
+
+def test_relayout_rejects_uncovered_src():
+    S, D = fb.Mapping("[A, B]", A=2, B=3), fb.Mapping("[A]", A=2)
+    with pytest.raises(_lib.FoptError):
+        fb.B200.describe_relayout(None, S, D, False)
+
+
+def test_window_base():
+    # buf.rs:760-781: the wire position of the offset's live cell
+    base = fb.Mapping("[A, B # 8]", A=4, B=6)
+    assert base.window_base({"A": 2, "B": 3}) == 2 * 8 + 3
+    assert base.window_base({}) == 0
