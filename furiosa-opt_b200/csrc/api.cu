@@ -127,6 +127,8 @@ fopt_status fopt_init(int device, fopt_ctx** out) {
     ctx->device = device;
     cuda_check(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "stream create");
     ctx->stream = ctx->own_stream;
+    cuda_check(cudaMalloc(&ctx->dev_err, sizeof(int32_t)), "error word");
+    cuda_check(cudaMemset(ctx->dev_err, 0, sizeof(int32_t)), "error word");
   });
   if (st != FOPT_OK) {
     g_noctx_err = ctx->err;
@@ -145,6 +147,7 @@ fopt_status fopt_destroy(fopt_ctx* ctx) {
   for (auto& kv : ctx->relayouts)
     if (kv.second->table) cudaFree(kv.second->table);
   if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->dev_err) cudaFree(ctx->dev_err);
   extern fopt_status fopt_comm_destroy(fopt_ctx*);
   fopt_comm_destroy(ctx);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
@@ -154,8 +157,21 @@ fopt_status fopt_destroy(fopt_ctx* ctx) {
 
 const char* fopt_last_error(const fopt_ctx* ctx) { return ctx ? ctx->err.c_str() : g_noctx_err.c_str(); }
 
+// After a stream sync: surface (and clear) a device-side bounded-wait expiry.
+static void check_device_error(fopt_ctx* ctx) {
+  int32_t code = 0;
+  cuda_check(cudaMemcpy(&code, ctx->dev_err, sizeof(code), cudaMemcpyDeviceToHost), "error word read");
+  if (code) {
+    cuda_check(cudaMemset(ctx->dev_err, 0, sizeof(code)), "error word clear");
+    throw Fail{FOPT_ERR_TIMEOUT, "a kernel's bounded wait expired (code " + std::to_string(code) + ")"};
+  }
+}
+
 fopt_status fopt_sync(fopt_ctx* ctx) {
-  return guarded(ctx, [&] { cuda_check(cudaStreamSynchronize(ctx->stream), "sync"); });
+  return guarded(ctx, [&] {
+    cuda_check(cudaStreamSynchronize(ctx->stream), "sync");
+    check_device_error(ctx);
+  });
 }
 
 fopt_status fopt_set_stream(fopt_ctx* ctx, void* stream) {
@@ -196,6 +212,7 @@ fopt_status fopt_d2h(fopt_ctx* ctx, void* host, const void* src, size_t bytes) {
   return guarded(ctx, [&] {
     cuda_check(cudaMemcpyAsync(host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream), "d2h");
     cuda_check(cudaStreamSynchronize(ctx->stream), "d2h sync");
+    check_device_error(ctx);
   });
 }
 
@@ -294,12 +311,38 @@ fopt_status fopt_transmute(fopt_ctx* ctx, void* dst, const void* src, fopt_dtype
                            const fopt_mapping* dst_map) {
   return guarded(ctx, [&] {
     require(src_map && dst_map && dst && src, "fopt_transmute: null argument");
-    RankWalk s = rank_walk(src_map->m), d = rank_walk(dst_map->m);
-    int64_t sl = 1, dl = 1;
-    for (auto v : s.live) sl *= v;
-    for (auto v : d.live) dl *= v;
-    require(dl <= sl, "transmute: dst_map has more live elements than src_map");
-    launch_transmute(ctx, s, d, dst, src, dtype);
+    std::vector<Factor> fs, fd;
+    if (src_map->m.flatten(fs) && dst_map->m.flatten(fd) && fs.size() <= (size_t)kKWheels &&
+        fd.size() <= (size_t)kKWheels) {
+      RankWalk s = rank_walk(src_map->m), d = rank_walk(dst_map->m);
+      int64_t sl = 1, dl = 1;
+      for (auto v : s.live) sl *= v;
+      for (auto v : d.live) dl *= v;
+      require(dl <= sl, "transmute: dst_map has more live elements than src_map");
+      launch_transmute(ctx, s, d, dst, src, dtype);
+      return;
+    }
+    // Not affine-factorisable: pair the k-th live src position with the k-th live dst position by
+    // brute-force evaluation once, then move the elements on the GPU.
+    std::vector<int64_t> live_src, c;
+    for (int64_t p = 0; p < src_map->m.size(); ++p)
+      if (src_map->m.eval(p, c) == 0) live_src.push_back(p);
+    RelayoutPlan plan;
+    plan.positions = dst_map->m.size();
+    std::vector<int64_t> t(plan.positions, -1);
+    size_t k = 0;
+    for (int64_t q = 0; q < plan.positions; ++q)
+      if (dst_map->m.eval(q, c) == 0) {
+        require(k < live_src.size(), "transmute: dst_map has more live elements than src_map");
+        t[q] = live_src[k++];
+      }
+    int64_t* dt = (int64_t*)scratch(ctx, sizeof(int64_t) * std::max<size_t>(t.size(), 1));
+    cuda_check(cudaMemcpyAsync(dt, t.data(), sizeof(int64_t) * t.size(), cudaMemcpyHostToDevice, ctx->stream),
+               "transmute table");
+    cuda_check(cudaMemsetAsync(dst, 0, (size_t)(plan.positions * dtype_bits(dtype) + 7) / 8, ctx->stream),
+               "transmute zero");
+    plan.table = dt;
+    launch_relayout(ctx, plan, dst, src, dtype, 0, 0, src_map->m.size(), plan.positions);
   });
 }
 

@@ -50,6 +50,7 @@ struct fopt_ctx {
   std::map<std::string, std::shared_ptr<fopt::FoldKPlan>> folds;
   void* nccl_comm = nullptr;
   int nranks = 1, rank = 0;
+  int32_t* dev_err = nullptr;  // device error word: bounded waits that expire write a code here
   void* scratch = nullptr;  // grow-only device scratch for kernels that need it
   size_t scratch_bytes = 0;
 };

@@ -1,12 +1,485 @@
-// Tensor-core GEMM for the plain-GEMM contractions (placeholder until the tcgen05 kernel lands):
-// returns false so the generic per-cell contraction runs.
+// Tensor-core contraction for GEMM-shaped BufStorage::contraction_in calls
+// (furiosa-opt-std/src/storage/buf.rs:401-447): D[M, N] = sum_k A[M, k] * B[N, k], both operands
+// K-major in HBM, on the 5th-generation tensor cores.
+//
+//   * int8 x int8 -> s32 (tcgen05.mma kind::i8) and bf16 x bf16 -> f32 (kind::f16) accumulate in
+//     TMEM (Tensor Memory); the accumulator is exact for int8 (s32, K <= 2^17 at |x| <= 128), so the
+//     result is bit-identical to the reference's per-cell i32 fold.
+//   * Operands stream HBM -> shared memory through TMA (cp.async.bulk.tensor, 128-byte swizzle) into
+//     a 4-stage ring; one elected thread issues the MMAs; a tcgen05.commit per stage frees the slot.
+//   * Persistent CTAs (one per SM, 192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (and
+//     TMEM owner), warps 2-5 = epilogue. Two TMEM accumulators (2 x BN columns) let the epilogue
+//     of tile i overlap the MMAs of tile i+1.
+//   * The epilogue fuses the narrow that follows the fold: i32 -> i8 wrap, f32 -> bf16 (RNE, flush,
+//     NaN canonical), or the vector-engine requant chain FxpToFp -> MulF(scale[n]) -> FpToFxp ->
+//     Clip -> i8, each in the reference's exact arithmetic.
+//   * Every wait is bounded (about 2 s of %globaltimer); on expiry the CTA records an error code
+//     in the context's device error word and leaves its loops, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "ctx.hpp"
 
 namespace fopt {
+namespace gemm {
 
-bool launch_gemm_tc(fopt_ctx*, void*, int, const void*, const void*, int, int64_t, int64_t, int64_t, int64_t, int64_t,
-                    int64_t, const fopt_epilogue*, const float*, int) {
-  return false;
+constexpr int BM = 128;
+constexpr int BKB = 128;  // bytes of K per stage row (one 128-byte swizzle atom row)
+constexpr int STAGES = 4;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, splitting the columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: returns false (and raises the shared abort flag) after ~kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row core-matrix groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+#define R32(i) "=r"(r[i])
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : R32(0), R32(1), R32(2), R32(3), R32(4), R32(5), R32(6), R32(7), R32(8), R32(9), R32(10), R32(11), R32(12),
+        R32(13), R32(14), R32(15), R32(16), R32(17), R32(18), R32(19), R32(20), R32(21), R32(22), R32(23), R32(24),
+        R32(25), R32(26), R32(27), R32(28), R32(29), R32(30), R32(31)
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+#undef R32
+
+struct Params {
+  void* D;
+  int M, N, K;  // K in elements
+  int64_t ldd;  // elements
+  int out_dt;   // FOPT_I8 / FOPT_I32 / FOPT_BF16 / FOPT_F32
+  int ep_kind;  // 0 none, 1 requant, 2 relu
+  const float* scale;
+  int int_width, clip_lo, clip_hi;
+  int* err;
+};
+
+// Requant of one accumulator (FxpToFp -> MulF -> FpToFxp -> Clip). For int_width 31,
+// fixedpoint_to_float is exactly IEEE round-to-nearest-even int -> f32 and float_to_fixedpoint is
+// round-half-away-from-zero then saturation, so both collapse to single instructions.
+__device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, float s) {
+  if (p.int_width == 31) {
+    float y = __fmul_rn(__int2float_rn(acc), s);
+    float r = roundf(y);
+    int32_t q;
+    if (r != r) q = (__float_as_uint(r) >> 31) ? INT32_MIN : INT32_MAX;
+    else if (r >= 2147483648.0f) q = INT32_MAX;
+    else if (r <= -2147483648.0f) q = INT32_MIN;
+    else q = (int32_t)r;
+    return max(p.clip_lo, min(p.clip_hi, q));
+  }
+  float y = __uint_as_float(fxp_to_fp_bits(acc, (uint32_t)p.int_width));
+  y = __fmul_rn(y, s);
+  int32_t q = fp_to_fxp(y, (uint32_t)p.int_width);
+  return max(p.clip_lo, min(p.clip_hi, q));
+}
+
+// Epilogue for 32 consecutive columns of one row.
+template <bool IS_F16>
+__device__ __forceinline__ void epilogue_store(const Params& p, int row, int col, const uint32_t* r) {
+  uint8_t* base = (uint8_t*)p.D;
+  if (!IS_F16) {
+    if (p.ep_kind == 1 || p.out_dt == FOPT_I8) {
+      uint32_t packed[8];
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          int32_t acc = (int32_t)r[j + t];
+          int32_t q;
+          if (p.ep_kind == 1) {
+            q = requant_one(p, acc, __ldg(p.scale + col + j + t));
+          } else {
+            q = p.ep_kind == 2 ? max(acc, 0) : acc;
+          }
+          w |= ((uint32_t)q & 0xffu) << (8 * t);
+        }
+        packed[j / 4] = w;
+      }
+      uint4* dst = (uint4*)(base + (int64_t)row * p.ldd + col);
+      dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+    } else {  // wide i32
+      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 4);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        uint32_t v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) v[t] = p.ep_kind == 2 ? (uint32_t)max((int32_t)r[j + t], 0) : r[j + t];
+        dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  } else {
+    if (p.out_dt == FOPT_BF16) {
+      uint32_t packed[16];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        uint32_t lo, hi;
+        if (p.ep_kind == 2) {
+          uint32_t a = r[j], b = r[j + 1];
+          bool na = (a & 0x7fffffffu) > 0x7f800000u, nb = (b & 0x7fffffffu) > 0x7f800000u;
+          lo = (!na && (a >> 31)) ? 0u : f32_to_bf16w(a);
+          hi = (!nb && (b >> 31)) ? 0u : f32_to_bf16w(b);
+        } else {
+          lo = f32_to_bf16w(r[j]);
+          hi = f32_to_bf16w(r[j + 1]);
+        }
+        packed[j / 2] = (lo >> 16) | (hi & 0xffff0000u);
+      }
+      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 2);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    } else {  // wide f32
+      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 4);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        uint32_t v[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          v[t] = p.ep_kind == 2 ? __float_as_uint(fmaxf(__uint_as_float(r[j + t]), 0.0f)) : r[j + t];
+        dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
+      }
+    }
+  }
+}
+
+template <bool IS_F16, int BN>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  constexpr int A_BYTES = BM * BKB;
+  constexpr int B_BYTES = BN * BKB;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int KSTEP_BYTES = 32;  // K bytes per MMA (int8: 32 elements; bf16: 16 elements)
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* acc_full = bars + 2 * STAGES;
+  uint64_t* acc_empty = bars + 2 * STAGES + 2;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_m = p.M / BM, tiles_n = p.N / BN;
+  const int ntiles = tiles_m * tiles_n;
+  const int kblocks = p.K * (IS_F16 ? 2 : 1) / BKB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 32 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 101)) goto done_producer;
+          const uint32_t fb = smem_u32(&full[stage]);
+          mbar_expect_tx(fb, STAGE_BYTES);
+          const int kx = kb * (IS_F16 ? BKB / 2 : BKB);
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          tma_load_2d(sa, &tmA, fb, kx, m0);
+          tma_load_2d(sa + A_BYTES, &tmB, fb, kx, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Drain: wait until the MMAs released every slot we filled, so no TMA write is in flight at exit.
+      for (int s = 0; s < STAGES; ++s) {
+        if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 102)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  done_producer:;
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t idesc;
+      if (IS_F16)
+        idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      else
+        idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, 103)) break;
+        fence_after();
+        const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
+        bool aborted = false;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, 104)) {
+            aborted = true;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t da = smem_desc(sa), db = smem_desc(sa + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BKB / KSTEP_BYTES; ++k) {
+            const uint64_t adv = (uint64_t)((k * KSTEP_BYTES) >> 4);
+            if (IS_F16)
+              mma_f16(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+            else
+              mma_i8(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+          }
+          mma_commit(smem_u32(&empty[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (aborted) break;
+        mma_commit(smem_u32(&acc_full[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue (warps 2..2+EPI_WARPS) ----------------
+    const int sub = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;  // which interleaved half of the 32-column chunks
+    const int row_in_tile = sub * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * BN;
+      bool ok = mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_flag, p.err, 105);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      fence_after();
+      const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(sub * 32) << 16);
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
+        uint32_t r[32];
+        tmem_ld32(tbase + (uint32_t)(c * 32), r);
+        epilogue_store<IS_F16>(p, m0 + row_in_tile, n0 + c * 32, r);
+      }
+      fence_before();
+      mbar_arrive(smem_u32(&acc_empty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ---- host side ----
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  if (!fn) throw Fail{FOPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable"};
+  return fn;
+}
+
+CUtensorMap make_map(const void* base, bool f16, int64_t inner, int64_t outer, int64_t ld_elems, int box_outer) {
+  CUtensorMap m;
+  const int esz = f16 ? 2 : 1;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * esz)};
+  cuuint32_t box[2] = {(cuuint32_t)(BKB / esz), (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, f16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                           const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "cuTensorMapEncodeTiled failed"};
+  return m;
+}
+
+template <bool IS_F16, int BN>
+void launch(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Params& p) {
+  constexpr int smem = STAGES * (BM * BKB + BN * BKB) + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cuda_check(cudaFuncSetAttribute(gemm_tc_kernel<IS_F16, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "gemm smem attribute");
+    attr = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+  int tiles = (p.M / BM) * (p.N / BN);
+  int grid = std::min(tiles, sms);
+  gemm_tc_kernel<IS_F16, BN><<<grid, THREADS, smem, ctx->stream>>>(a, b, p);
+  launched(ctx, "gemm_tc");
+}
+
+}  // namespace gemm
+
+bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const void* b, int in_dt, int64_t M,
+                    int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldd, const fopt_epilogue* ep,
+                    const float* scale, int scale_along_n) {
+  using namespace gemm;
+  const bool f16 = in_dt == FOPT_BF16;
+  if (!(in_dt == FOPT_I8 || f16)) return false;
+  if (getenv("FOPT_DISABLE_TC")) return false;
+  const int esz = f16 ? 2 : 1;
+  if (M % BM || K * esz % BKB || M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return false;
+  int bn = N % 256 == 0 ? 256 : (N % 128 == 0 ? 128 : 0);
+  if (!bn) return false;
+  if ((uintptr_t)a % 16 || (uintptr_t)b % 16 || (uintptr_t)out % 16) return false;
+  if ((lda * esz) % 16 || (ldb * esz) % 16) return false;
+  int ep_kind = ep ? ep->kind : 0;
+  if (ep_kind == 1 && !scale_along_n) return false;
+  int odt = out_dt;
+  int osz = dtype_bits(odt) / 8;
+  if ((ldd * osz) % 16) return false;
+  Params p{};
+  p.D = out;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.ldd = ldd;
+  p.out_dt = odt;
+  p.ep_kind = ep_kind;
+  p.scale = scale;
+  p.int_width = ep ? ep->int_width : 31;
+  p.clip_lo = ep ? ep->clip_lo : INT32_MIN;
+  p.clip_hi = ep ? ep->clip_hi : INT32_MAX;
+  p.err = ctx->dev_err;
+  CUtensorMap ma = make_map(a, f16, K, M, lda, BM);
+  CUtensorMap mb = make_map(b, f16, K, N, ldb, bn);
+  if (f16) {
+    if (bn == 256) launch<true, 256>(ctx, ma, mb, p);
+    else launch<true, 128>(ctx, ma, mb, p);
+  } else {
+    if (bn == 256) launch<false, 256>(ctx, ma, mb, p);
+    else launch<false, 128>(ctx, ma, mb, p);
+  }
+  return true;
 }
 
 }  // namespace fopt

@@ -8,6 +8,7 @@
 //            a 32x32 shared-memory tile so both the read and the write are coalesced;
 //   * walk:  anything else, one element per thread with the odometer decomposed per position.
 #include <algorithm>
+#include <type_traits>
 
 #include "ctx.hpp"
 
@@ -76,30 +77,46 @@ __global__ void relayout_vec64(V* __restrict__ dst, const V* __restrict__ src, K
 
 // ---- tile path ----
 // `others` walks every wheel except the dst-innermost (i) and the src-unit-stride (j) ones; memory
-// 0 = src offset, memory 1 = dst position.
-template <typename T>
-__global__ void relayout_tile(T* __restrict__ dst, const T* __restrict__ src, KWalk others, int64_t e0, int64_t s0,
-                              int64_t ej, int64_t wj, int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
-                              int64_t batches) {
-  __shared__ T tile[32][33];
+// 0 = src offset, memory 1 = dst position. A (32 V) x (32 V) tile moves through shared memory; each
+// thread reads V consecutive src elements (a 4-byte word for 1- and 2-byte types) and writes V
+// consecutive dst elements, so both global sides move whole 128-byte lines per warp.
+template <typename T, int V>
+__global__ void __launch_bounds__(256) relayout_tile(T* __restrict__ dst, const T* __restrict__ src, KWalk others,
+                                                     int64_t e0, int64_t s0, int64_t ej, int64_t wj, int64_t src_base,
+                                                     int64_t dst_base, int64_t nt0, int64_t ntj, int64_t batches) {
+  constexpr int TT = 32 * V;
+  using W = typename std::conditional<V == 4, uint32_t, typename std::conditional<V == 2, uint32_t, T>::type>::type;
+  static_assert(sizeof(T) * V == sizeof(W), "vector width");
+  __shared__ T tile[TT][TT + 2 / sizeof(T) + (sizeof(T) == 4 ? 1 : 0)];
   const int tx = threadIdx.x, ty = threadIdx.y;
   for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
     int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
     int64_t off[2] = {0, 0};
     bool live = walk_offsets<2>(others, b, off);
     if (live) {
+      const int64_t dj = tj * TT + tx * V;
+#pragma unroll 4
+      for (int r = ty; r < TT; r += 8) {
+        int64_t d0 = ti * TT + r;
+        if (d0 < e0 && dj < ej) {
+          W w = *(const W*)(src + src_base + off[0] + d0 * s0 + dj);
 #pragma unroll
-      for (int k = 0; k < 32; k += 8) {
-        int64_t d0 = ti * 32 + ty + k, dj = tj * 32 + tx;
-        if (d0 < e0 && dj < ej) tile[ty + k][tx] = src[src_base + off[0] + d0 * s0 + dj];
+          for (int k = 0; k < V; ++k) tile[r][tx * V + k] = ((const T*)&w)[k];
+        }
       }
     }
     __syncthreads();
     if (live) {
+      const int64_t d0 = ti * TT + tx * V;
+#pragma unroll 4
+      for (int c = ty; c < TT; c += 8) {
+        int64_t dj = tj * TT + c;
+        if (d0 < e0 && dj < ej) {
+          W w;
 #pragma unroll
-      for (int k = 0; k < 32; k += 8) {
-        int64_t d0 = ti * 32 + tx, dj = tj * 32 + ty + k;
-        if (d0 < e0 && dj < ej) dst[dst_base + off[1] + d0 + dj * wj] = tile[tx][ty + k];
+          for (int k = 0; k < V; ++k) ((T*)&w)[k] = tile[tx * V + k][c];
+          *(W*)(dst + dst_base + off[1] + d0 + dj * wj) = w;
+        }
       }
     }
     __syncthreads();
@@ -232,11 +249,21 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
     }
     int64_t batches = 1;
     for (int k = 0; k < others.n; ++k) batches *= others.extent[k];
-    int64_t nt0 = (w.extent[0] + 31) / 32, ntj = (w.extent[j] + 31) / 32;
+    // Vector width: whole 4-byte words per thread when every offset stays word-aligned.
+    constexpr int VW = sizeof(T) >= 4 ? 1 : 4 / (int)sizeof(T);
+    bool wide = VW > 1 && w.extent[0] % VW == 0 && w.extent[j] % VW == 0 && w.stride[0][0] % VW == 0 &&
+                src_base % VW == 0 && dst_base % VW == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0;
+    for (int k = 0; wide && k < others.n; ++k) wide = others.stride[0][k] % VW == 0;
+    const int TT = wide ? 32 * VW : 32;
+    int64_t nt0 = (w.extent[0] + TT - 1) / TT, ntj = (w.extent[j] + TT - 1) / TT;
     int64_t blocks = nt0 * ntj * batches;
-    int grid = (int)std::min<int64_t>(blocks, 148 * 64);
-    relayout_tile<T><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
-                                                   src_base, dst_base, nt0, ntj, batches);
+    int grid = (int)std::min<int64_t>(blocks, 148 * 16);
+    if (wide)
+      relayout_tile<T, VW><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                         src_base, dst_base, nt0, ntj, batches);
+    else
+      relayout_tile<T, 1><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                        src_base, dst_base, nt0, ntj, batches);
     launched(ctx, "relayout_tile");
     return;
   }

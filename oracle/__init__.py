@@ -17,6 +17,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import subprocess
+import time
 
 import numpy as np
 
@@ -34,13 +35,14 @@ def build() -> str:
     src = os.path.join(HERE, "storage_ref.c")
     if os.path.exists(SO) and os.path.getmtime(SO) >= os.path.getmtime(src):
         return SO
-    cmd = ["gcc", "-O3", "-march=native", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-shared", "-fPIC",
+    cmd = ["gcc", "-O3", "-march=x86-64-v3", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-shared", "-fPIC",
            "-include", "stdlib.h", src, "-o", SO, "-lm"]
     subprocess.run(cmd, check=True)
     return SO
 
 
 _lib = None
+last_fold_seconds = 0.0  # duration of the last ref_contract fold (the timed CPU loop)
 
 
 def lib():
@@ -123,7 +125,18 @@ def transpose(dst: bytes, src: bytes, dtype: str, Src: RefMapping, Dst: RefMappi
 
 
 def _residue(P: RefMapping, kept: list):
-    """Live positions of P whose kept coordinates are all 0, ascending: the carve residue walk."""
+    """Live positions of P whose kept coordinates are all 0, ascending: the carve residue walk.
+
+    For a large P the kept axes are re-declared with size 1 first (same wire order of the residue
+    cells when the kept axes are whole symbols), so only the residue positions are evaluated."""
+    if P.size > (1 << 24) and kept:
+        try:
+            small = RefMapping(P.expr, {a: (1 if a in kept else n) for a, n in P.axes.items()})
+            st, co = small.cells()
+            rows = np.nonzero(st == 0)[0]
+            return {a: co[a][rows] for a in small.idents() if a not in kept}
+        except AssertionError:
+            pass
     st, co = P.cells()
     sel = st == 0
     for a in kept:
@@ -132,12 +145,12 @@ def _residue(P: RefMapping, kept: list):
     return {a: co[a][rows] for a in P.idents() if a not in kept}
 
 
-def _plan(X: RefMapping, O: RefMapping, residue: dict, n_res: int):
+def _plan(X: RefMapping, O: RefMapping, residue: dict, n_res: int, n_out=None):
     """ReadPlan for operand X: base[o] (out cell o at the first residue coordinate) and delta[r]."""
     x_axes = X.idents()
     idx = _Index(X, x_axes)
-    st, oco = O.cells()
-    n_out = O.size
+    n_out = O.size if n_out is None else int(n_out)
+    st, oco = O.cells(np.arange(n_out))
     co = {}
     for a in x_axes:
         if a in residue:
@@ -180,9 +193,9 @@ def contract(lhs: bytes, rhs: bytes, in_dtype: str, out_dtype: str, L: RefMappin
     kept = O.idents()
     res = _residue(P, kept)
     n_res = len(next(iter(res.values())))
-    bl, dl = _plan(L, O, res, n_res)
-    br, dr = _plan(R, O, res, n_res)
     n_out = O.size if out_cells is None else int(out_cells)
+    bl, dl = _plan(L, O, res, n_res, n_out)
+    br, dr = _plan(R, O, res, n_res, n_out)
     sidx = np.zeros(n_out, np.int64)
     sc = np.zeros(1, np.float32)
     if ep_kind == 1:
@@ -191,9 +204,12 @@ def contract(lhs: bytes, rhs: bytes, in_dtype: str, out_dtype: str, L: RefMappin
         sc = np.asarray(scale, np.float32)
     out = np.zeros(nbytes(out_dtype, n_out) + 4, np.uint8)
     lb, rb = _buf(lhs), _buf(rhs)
+    global last_fold_seconds
+    t0 = time.perf_counter()
     lib().ref_contract(_p(out), DT[out_dtype], _p(lb), _p(rb), DT[in_dtype], _p(bl), _p(dl), _p(br), _p(dr),
                        C.c_int64(n_out), C.c_int64(n_res), C.c_int64(L.size), C.c_int64(R.size), ep_kind, _p(sc),
                        _p(sidx), int_width, clip_lo, clip_hi)
+    last_fold_seconds = time.perf_counter() - t0
     return out[: nbytes(out_dtype, n_out)].tobytes()
 
 

@@ -277,3 +277,16 @@ def test_transpose_broadcast_and_padding():  # buf.rs:268-313 (broadcast stride 
     assert list(got) == [1, 2, 3, 4, -1, -1] * 3
     with pytest.raises(AssertionError):
         oracle.transpose(canvas.tobytes(), data.tobytes(), "i32", src, dst, allow_broadcast=False)
+
+
+def test_fxp_to_fp_iw31_is_ieee_rne():
+    """fixedpoint_to_float at int_width 31 equals IEEE round-to-nearest-even int -> f32, the fact
+    the GEMM epilogue's fast path rests on (float/mod.rs:113-159)."""
+    lib = oracle.lib()
+    rng = np.random.default_rng(3)
+    vals = np.concatenate([rng.integers(-2 ** 31, 2 ** 31, 200000, dtype=np.int64),
+                           np.array([0, 1, -1, 2 ** 24, 2 ** 24 + 1, 2 ** 24 + 3, -(2 ** 24 + 1), 2 ** 25 + 2,
+                                     2 ** 31 - 1, -(2 ** 31), -(2 ** 31) + 1, 16777217, 33554435])])
+    for v in vals:
+        got = lib.ref_fxp_to_fp(int(v), 31)
+        assert got == int(np.float32(np.int32(v)).view(np.uint32)), int(v)
