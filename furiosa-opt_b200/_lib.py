@@ -66,6 +66,7 @@ SIGNATURES = [
     ("fopt_elementwise", _I32, [_VP, C.POINTER(Program), _I32, C.POINTER(_VP), C.POINTER(C.c_int), _VP, C.c_int,
                                 _I64]),
     ("fopt_reduce", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
+    ("fopt_reduce_noalloc", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_contraction", _I32, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP, _VP, _VP, C.POINTER(Epilogue)]),
     ("fopt_attention", _I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, C.c_float]),
     ("fopt_comm_unique_id", _I32, [_VP]),

@@ -86,6 +86,9 @@ void launch_elementwise(fopt_ctx* ctx, const fopt_program* prog, int n_in, const
                         void* out, fopt_dtype out_dt, int64_t n);
 void launch_reduce(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op, uint32_t ident,
                    int64_t src_elems);
+std::vector<int64_t> host_deltas(const KWalk& rw);
+void launch_reduce_cells(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op,
+                         uint32_t ident, int64_t src_elems, const int64_t* d_delta, int64_t nd);
 void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, int out_dt, const void* lhs,
                                 const void* rhs, int in_dt, int64_t lhs_elems, int64_t rhs_elems,
                                 const fopt_epilogue* ep, const int64_t* scale_stride_out, const float* scale);

@@ -275,4 +275,31 @@ void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, in
   launched(ctx, "contract_cell");
 }
 
+// Live residue deltas of memory 0 computed on the host (walk order), without touching device memory.
+std::vector<int64_t> host_deltas(const KWalk& rw) {
+  std::vector<int64_t> d;
+  int64_t n = 1;
+  for (int i = 0; i < rw.n; ++i) n *= rw.extent[i];
+  for (int64_t r = 0; r < n; ++r) {
+    int64_t q = r, off = 0;
+    bool live = true;
+    for (int i = 0; i < rw.n; ++i) {
+      int64_t dd = q % rw.extent[i];
+      q /= rw.extent[i];
+      live &= dd < rw.live[i];
+      off += dd * rw.stride[0][i];
+    }
+    if (live) d.push_back(off);
+  }
+  return d;
+}
+
+// The per-cell reduce over a delta list the caller has already placed in device memory.
+void launch_reduce_cells(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op,
+                         uint32_t ident, int64_t src_elems, const int64_t* d_delta, int64_t nd) {
+  reduce_cell_kernel<<<grid_for(p.out_positions), 256, 0, ctx->stream>>>(out, src, dtype, op, ident, p.out,
+                                                                          p.out_positions, d_delta, nd, src_elems);
+  launched(ctx, "reduce_cell");
+}
+
 }  // namespace fopt

@@ -1,0 +1,107 @@
+// fopt_reduce_noalloc: the reduce entry point for callers that must not allocate device memory.
+//
+// fopt_reduce keeps its per-cell residue delta table in a context scratch buffer that grows with
+// cudaMalloc (and frees the old one with cudaFree, which synchronises the device). Some callers cannot
+// allow either:
+//   * a host runtime that has handed the whole device memory budget to its own allocator up front,
+//     so any allocation made behind its back can fail or break its accounting;
+//   * a latency-critical loop where the implicit device synchronisation of cudaFree, or a
+//     cudaMalloc that has to wait for the driver, is not acceptable.
+// This variant never allocates: its delta table lives in the fixed-size device array below, and
+// everything else it needs (plans, host vectors) is host memory.
+//
+// Contract:
+//   * the delta table holds at most kNoAllocMaxDeltas (32768) entries, 256 KiB of int64, which every
+//     GPU that loads this library reserves until the process exits; a reduce whose live residue is
+//     larger is rejected with FOPT_ERR_INVALID and a message;
+//   * the first call on each device looks up the array's device address (cudaGetSymbolAddress with
+//     that device current); make that first call before any stream capture;
+//   * all calls share the one array, and each call overwrites the part it uses: two calls whose
+//     kernels can overlap on the GPU (different streams, no ordering between them) race on it;
+//   * the fold always runs per output cell in the reference's wire order, so every dtype matches
+//     fopt_reduce with exact fold on (and i32 results match fopt_reduce in either mode).
+#include <mutex>
+
+#include "ctx.hpp"
+
+namespace fopt {
+namespace {
+
+constexpr int64_t kNoAllocMaxDeltas = 32768;
+constexpr int kMaxDevices = 64;
+
+// File-scope device scratch. In host code `g_noalloc_deltas` names a host-side stand-in, not a
+// device address: only the pointer obtained from cudaGetSymbolAddress may be given to a kernel.
+static __device__ __align__(256) int64_t g_noalloc_deltas[kNoAllocMaxDeltas];
+
+std::mutex g_mu;
+int64_t* g_dev_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_deltas on ctx's device, looked up once per device.
+int64_t* delta_array(fopt_ctx* ctx) {
+  if (ctx->device < 0 || ctx->device >= kMaxDevices) throw Fail{FOPT_ERR_INVALID, "reduce_noalloc: device index"};
+  std::lock_guard<std::mutex> g(g_mu);
+  if (!g_dev_ptr[ctx->device]) {
+    int prev = -1;
+    cuda_check(cudaGetDevice(&prev), "reduce_noalloc: cudaGetDevice");
+    if (prev != ctx->device) cuda_check(cudaSetDevice(ctx->device), "reduce_noalloc: cudaSetDevice");
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_deltas);
+    if (prev != ctx->device) cudaSetDevice(prev);
+    cuda_check(e, "reduce_noalloc: cudaGetSymbolAddress");
+    g_dev_ptr[ctx->device] = (int64_t*)p;
+  }
+  return g_dev_ptr[ctx->device];
+}
+
+std::vector<Mapping> unify2(const Mapping& a, const Mapping& b) {
+  auto table = std::make_shared<AxisTable>();
+  for (auto* m : {&a, &b})
+    for (size_t i = 0; i < m->axes->names.size(); ++i) table->intern(m->axes->names[i], m->axes->sizes[i]);
+  return {parse_mapping(a.to_string(), table), parse_mapping(b.to_string(), table)};
+}
+
+}  // namespace
+}  // namespace fopt
+
+using namespace fopt;
+
+extern "C" fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype,
+                                           fopt_reduce_op op, uint32_t identity_bits, const fopt_mapping* src_map,
+                                           const fopt_mapping* dst_map, int allow_broadcast) {
+  if (!ctx) return FOPT_ERR_INVALID;
+  try {
+    if (!out || !src || !src_map || !dst_map) throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: null argument"};
+    if (!(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16))
+      throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: dtype must be i32, f32 or bf16"};
+    auto u = unify2(src_map->m, dst_map->m);
+    FoldPlan fp;
+    if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
+      throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_reduce_noalloc: mappings are not affine-factorisable"};
+    if ((int)fp.out.wheels.size() > kKWheels || (int)fp.residue.wheels.size() > kKWheels)
+      throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_reduce_noalloc: plan has too many wheels"};
+    FoldKPlan kp;
+    kp.out = to_kwalk(fp.out);
+    kp.residue = to_kwalk(fp.residue);
+    kp.out_positions = fp.out.positions();
+    kp.residue_positions = fp.residue.positions();
+    kp.residue_live = fp.residue.live_positions();
+    if (kp.residue_live > kNoAllocMaxDeltas)
+      throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: the reduce folds " + std::to_string(kp.residue_live) +
+                                       " cells per output, above the fixed maximum of " +
+                                       std::to_string(kNoAllocMaxDeltas) + "; use fopt_reduce"};
+    std::vector<int64_t> d = host_deltas(kp.residue);
+    int64_t* dev = delta_array(ctx);
+    if (!d.empty())
+      cuda_check(cudaMemcpyAsync(dev, d.data(), sizeof(int64_t) * d.size(), cudaMemcpyHostToDevice, ctx->stream),
+                 "reduce_noalloc: delta upload");
+    launch_reduce_cells(ctx, kp, out, src, dtype, op, identity_bits, src_map->m.size(), dev, (int64_t)d.size());
+    return FOPT_OK;
+  } catch (const Fail& f) {
+    ctx->err = f.msg;
+    return f.code;
+  } catch (const std::exception& e) {
+    ctx->err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}

@@ -183,6 +183,18 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
                         uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                         int allow_broadcast);
 
+/* Allocation-free reduce. No counterpart in the reference: it exists for callers that cannot let the
+ * library call cudaMalloc / cudaFree (a host runtime that owns the whole device-memory budget through
+ * its own allocator, or a latency-critical loop that cannot absorb the device synchronisation a
+ * cudaFree implies). Same arguments and results as fopt_reduce with exact fold; its residue table
+ * lives in a fixed 256 KiB device array (at most 32768 folded cells per output, larger reduces are
+ * rejected with FOPT_ERR_INVALID) that every GPU loading the library keeps until exit. The first call
+ * on a device looks the array up; make it before any stream capture. All calls share the array:
+ * calls whose kernels may overlap on the GPU race. */
+fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype, fopt_reduce_op op,
+                                uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                int allow_broadcast);
+
 /* ---- contraction (BufStorage::contraction_in, buf.rs:401-481; Backend::contraction /
  * contraction_prewidened, backend/mod.rs:135-157) ----
  * out[o] = narrow( sum_r widen(lhs[.]) * widen(rhs[.]) ) over the axes of pre_reduce absent from
