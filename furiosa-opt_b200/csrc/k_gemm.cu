@@ -7,8 +7,8 @@
 //     result is bit-identical to the reference's per-cell i32 fold.
 //   * Operands stream HBM -> shared memory through TMA (cp.async.bulk.tensor, 128-byte swizzle) into
 //     a 4-stage ring; one elected thread issues the MMAs; a tcgen05.commit per stage frees the slot.
-//   * Persistent CTAs (one per SM, 192 threads): warp 0 = TMA producer, warp 1 = MMA issuer (and
-//     TMEM owner), warps 2-5 = epilogue. Two TMEM accumulators (2 x BN columns) let the epilogue
+//   * Persistent CTAs (one per SM, 320 threads): warp 0 = TMA producer, warp 1 = MMA issuer (and
+//     TMEM owner), warps 2-9 = epilogue. Two TMEM accumulators (2 x BN columns) let the epilogue
 //     of tile i overlap the MMAs of tile i+1.
 //   * The epilogue fuses the narrow that follows the fold: i32 -> i8 wrap, f32 -> bf16 (RNE, flush,
 //     NaN canonical), or the vector-engine requant chain FxpToFp -> MulF(scale[n]) -> FpToFxp ->
@@ -162,78 +162,104 @@ __device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, flo
   return max(p.clip_lo, min(p.clip_hi, q));
 }
 
+// Epilogue modes, one specialised kernel each so the epilogue code stays small:
+//   EP_I8    i32 accumulator -> i8 (the `as i8` wrap), optional relu
+//   EP_WIDE  raw accumulator (i32 / f32), optional relu
+//   EP_RQ31  requant at int_width 31 with clip bounds exact in f32 (the fast exact form below)
+//   EP_RQ    requant at any int_width (bit-level fixed-point restatement)
+//   EP_BF16  f32 accumulator -> bf16 (RNE, flush, canonical NaN), optional relu (cast_relu)
+enum { EP_I8 = 0, EP_WIDE = 1, EP_RQ31 = 2, EP_RQ = 3, EP_BF16 = 4 };
+
+// float_to_fixedpoint at int_width 31 is round-half-away-from-zero then saturation. With t = trunc(y)
+// and d = y - t (exact), rounding away from zero is needed exactly when |d| >= 0.5. Clip bounds that
+// are exact in f32 let the saturation and the Clip run in f32.
+__device__ __forceinline__ int32_t requant31(int32_t acc, float s, float lo, float hi) {
+  // x86 multiplies (the reference's host) return a NaN operand unchanged, sign included; the GPU
+  // would return a canonical NaN, so a NaN scale is propagated explicitly.
+  float y = s != s ? s : __fmul_rn(__int2float_rn(acc), s);
+  float t = truncf(y);
+  float r = fabsf(__fsub_rn(y, t)) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, y)) : t;
+  if (y != y) r = (__float_as_uint(y) >> 31) ? lo : hi;  // NaN saturates by sign, then clips
+  return (int32_t)fminf(fmaxf(r, lo), hi);
+}
+
 // Epilogue for 32 consecutive columns of one row.
-template <bool IS_F16>
+template <bool IS_F16, int MODE>
 __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col, const uint32_t* r) {
   uint8_t* base = (uint8_t*)p.D;
-  if (!IS_F16) {
-    if (p.ep_kind == 1 || p.out_dt == FOPT_I8) {
-      uint32_t packed[8];
+  const bool relu = p.ep_kind == 2;
+  if constexpr (MODE == EP_I8 || MODE == EP_RQ31 || MODE == EP_RQ) {
+    float sc[32];
+    if constexpr (MODE != EP_I8) {
+      const float4* s4 = (const float4*)(p.scale + col);
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        uint32_t w = 0;
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          int32_t acc = (int32_t)r[j + t];
-          int32_t q;
-          if (p.ep_kind == 1) {
-            q = requant_one(p, acc, __ldg(p.scale + col + j + t));
-          } else {
-            q = p.ep_kind == 2 ? max(acc, 0) : acc;
-          }
-          w |= ((uint32_t)q & 0xffu) << (8 * t);
-        }
-        packed[j / 4] = w;
-      }
-      uint4* dst = (uint4*)(base + (int64_t)row * p.ldd + col);
-      dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    } else {  // wide i32
-      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 4);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        uint32_t v[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) v[t] = p.ep_kind == 2 ? (uint32_t)max((int32_t)r[j + t], 0) : r[j + t];
-        dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
+      for (int q = 0; q < 8; ++q) {
+        float4 v = __ldg(s4 + q);
+        sc[4 * q] = v.x; sc[4 * q + 1] = v.y; sc[4 * q + 2] = v.z; sc[4 * q + 3] = v.w;
       }
     }
-  } else {
-    if (p.out_dt == FOPT_BF16) {
-      uint32_t packed[16];
+    const float flo = (float)p.clip_lo, fhi = (float)p.clip_hi;
+    uint32_t packed[8];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2) {
-        uint32_t lo, hi;
-        if (p.ep_kind == 2) {
-          uint32_t a = r[j], b = r[j + 1];
-          bool na = (a & 0x7fffffffu) > 0x7f800000u, nb = (b & 0x7fffffffu) > 0x7f800000u;
-          lo = (!na && (a >> 31)) ? 0u : f32_to_bf16w(a);
-          hi = (!nb && (b >> 31)) ? 0u : f32_to_bf16w(b);
+    for (int j = 0; j < 32; j += 4) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        int32_t acc = (int32_t)r[j + t];
+        int32_t q;
+        if constexpr (MODE == EP_RQ31) {
+          q = requant31(acc, sc[j + t], flo, fhi);
+        } else if constexpr (MODE == EP_RQ) {
+          float sv = sc[j + t];
+          float y = sv != sv ? sv : __fmul_rn(__uint_as_float(fxp_to_fp_bits(acc, (uint32_t)p.int_width)), sv);
+          q = max(p.clip_lo, min(p.clip_hi, fp_to_fxp(y, (uint32_t)p.int_width)));
         } else {
-          lo = f32_to_bf16w(r[j]);
-          hi = f32_to_bf16w(r[j + 1]);
+          q = relu ? max(acc, 0) : acc;
         }
-        packed[j / 2] = (lo >> 16) | (hi & 0xffff0000u);
+        w |= ((uint32_t)q & 0xffu) << (8 * t);
       }
-      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 2);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-    } else {  // wide f32
-      uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 4);
-#pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        uint32_t v[4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          v[t] = p.ep_kind == 2 ? __float_as_uint(fmaxf(__uint_as_float(r[j + t]), 0.0f)) : r[j + t];
-        dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
-      }
+      packed[j / 4] = w;
     }
+    uint4* dst = (uint4*)(base + (int64_t)row * p.ldd + col);
+    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  } else if constexpr (MODE == EP_WIDE) {
+    uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 4);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      uint32_t v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (!relu) v[t] = r[j + t];
+        else if (IS_F16) v[t] = __float_as_uint(fmaxf(__uint_as_float(r[j + t]), 0.0f));
+        else v[t] = (uint32_t)max((int32_t)r[j + t], 0);
+      }
+      dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
+    }
+  } else {  // EP_BF16
+    uint32_t packed[16];
+#pragma unroll
+    for (int j = 0; j < 32; j += 2) {
+      uint32_t lo, hi;
+      if (relu) {
+        uint32_t a = r[j], b = r[j + 1];
+        bool na = (a & 0x7fffffffu) > 0x7f800000u, nb = (b & 0x7fffffffu) > 0x7f800000u;
+        lo = (!na && (a >> 31)) ? 0u : f32_to_bf16w(a);
+        hi = (!nb && (b >> 31)) ? 0u : f32_to_bf16w(b);
+      } else {
+        lo = f32_to_bf16w(r[j]);
+        hi = f32_to_bf16w(r[j + 1]);
+      }
+      packed[j / 2] = (lo >> 16) | (hi & 0xffff0000u);
+    }
+    uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 2);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
   }
 }
 
-template <bool IS_F16, int BN>
+template <bool IS_F16, int BN, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
   constexpr int A_BYTES = BM * BKB;
@@ -373,7 +399,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
         uint32_t r[32];
         tmem_ld32(tbase + (uint32_t)(c * 32), r);
-        epilogue_store<IS_F16>(p, m0 + row_in_tile, n0 + c * 32, r);
+        epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r);
       }
       fence_before();
       mbar_arrive(smem_u32(&acc_empty[acc]));
@@ -387,6 +413,225 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Paired-SM variant (cta_group::2): a cluster of two CTAs computes a 256 x 256 tile. Each CTA streams
+// its own 128 rows of A and its own 128 rows of B (half of N) into a 6-stage ring of 32 KiB slices;
+// the even CTA issues tcgen05.mma.cta_group::2 (M = 256), which reads both CTAs' shared memory and
+// leaves rows [128 r, 128 r + 128) of the accumulator in CTA r's TMEM. Per SM this halves the B
+// bytes streamed per MMA compared with the single-CTA kernel.
+//   full[s]      (even CTA): both CTAs' TMA bytes land here (cta_group::2 TMA signals the pair's barrier)
+//   empty[s]     (each CTA): arrival from the MMA commit, delivered to both CTAs of the pair
+//   acc_full[a]  (each CTA): MMA commit after the tile's last k-block, delivered to both
+//   acc_empty[a] (even CTA): one arrival per epilogue warp of both CTAs (16)
+// ---------------------------------------------------------------------------------------------
+constexpr int STAGES2 = 6;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
+                                                 int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_i8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma2_f16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Commit the issuing thread's MMAs to the barrier at `bar` in both CTAs of the pair (CTA mask 0b11).
+__device__ __forceinline__ void mma2_commit_both(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          bar)
+      : "memory");
+}
+
+template <bool IS_F16, int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  constexpr int BN = 256;
+  constexpr int A_BYTES = 128 * BKB;
+  constexpr int B_BYTES = (BN / 2) * BKB;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr int KSTEP_BYTES = 32;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + STAGES2 * STAGE_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES2;
+  uint64_t* acc_full = bars + 2 * STAGES2;
+  uint64_t* acc_empty = bars + 2 * STAGES2 + 2;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES2 + 4);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_m = p.M / 256, tiles_n = p.N / BN;
+  const int ntiles = tiles_m * tiles_n;
+  const int kblocks = p.K * (IS_F16 ? 2 : 1) / BKB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&acc_full[a]), 1);
+      mbar_init(smem_u32(&acc_empty[a]), 2 * EPI_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  fence_before();
+  cluster_sync_all();  // both CTAs' barriers initialised before any TMA or remote arrive
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = pair; tile < ntiles; tile += npairs) {
+        const int m0 = (tile % tiles_m) * 256 + (int)rank * 128;
+        const int n0 = (tile / tiles_m) * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 201)) goto done_producer2;
+          const uint32_t fb_local = smem_u32(&full[stage]);
+          const uint32_t fb_pair = map_to_rank(fb_local, 0);
+          if (rank == 0) mbar_expect_tx(fb_local, 2 * STAGE_BYTES);
+          const int kx = kb * (IS_F16 ? BKB / 2 : BKB);
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, fb_pair, kx, m0);
+          tma_load_2d_pair(sa + A_BYTES, &tmB, fb_pair, kx, n0);
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      for (int s = 0; s < STAGES2; ++s) {
+        if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 202)) break;
+        if (++stage == STAGES2) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+  done_producer2:;
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      uint32_t idesc;
+      if (IS_F16)
+        idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+      else
+        idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = pair; tile < ntiles; tile += npairs) {
+        if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, 203)) break;
+        fence_after();
+        const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
+        bool aborted = false;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, 204)) {
+            aborted = true;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t da = smem_desc(sa), db = smem_desc(sa + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BKB / KSTEP_BYTES; ++k) {
+            const uint64_t adv = (uint64_t)((k * KSTEP_BYTES) >> 4);
+            if (IS_F16)
+              mma2_f16(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+            else
+              mma2_i8(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+          }
+          mma2_commit_both(smem_u32(&empty[stage]));
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (aborted) break;
+        mma2_commit_both(smem_u32(&acc_full[acc]));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+    }
+    __syncwarp();
+  } else {
+    const int sub = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in_tile = (int)rank * 128 + sub * 32 + lane;
+    const uint32_t acc_empty_pair = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs) {
+      const int m0 = (tile % tiles_m) * 256, n0 = (tile / tiles_m) * BN;
+      bool ok = mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_flag, p.err, 205);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      fence_after();
+      const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(sub * 32) << 16);
+#pragma unroll 1
+      for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
+        uint32_t r[32];
+        tmem_ld32(tbase + (uint32_t)(c * 32), r);
+        epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_pair + (uint32_t)(acc * sizeof(uint64_t)));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  fence_before();
+  cluster_sync_all();  // no CTA leaves while its pair may still read its smem or signal its barriers
+  fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
   }
 }
 
@@ -420,12 +665,12 @@ CUtensorMap make_map(const void* base, bool f16, int64_t inner, int64_t outer, i
   return m;
 }
 
-template <bool IS_F16, int BN>
+template <bool IS_F16, int BN, int MODE>
 void launch(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Params& p) {
   constexpr int smem = STAGES * (BM * BKB + BN * BKB) + 1024 + 256;
   static bool attr = false;
   if (!attr) {
-    cuda_check(cudaFuncSetAttribute(gemm_tc_kernel<IS_F16, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+    cuda_check(cudaFuncSetAttribute(gemm_tc_kernel<IS_F16, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                "gemm smem attribute");
     attr = true;
   }
@@ -433,8 +678,37 @@ void launch(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Par
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
   int tiles = (p.M / BM) * (p.N / BN);
   int grid = std::min(tiles, sms);
-  gemm_tc_kernel<IS_F16, BN><<<grid, THREADS, smem, ctx->stream>>>(a, b, p);
+  gemm_tc_kernel<IS_F16, BN, MODE><<<grid, THREADS, smem, ctx->stream>>>(a, b, p);
   launched(ctx, "gemm_tc");
+}
+
+template <bool IS_F16, int MODE>
+void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Params& p) {
+  constexpr int smem = STAGES2 * (128 * BKB + 128 * BKB) + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cuda_check(cudaFuncSetAttribute(gemm_tc2_kernel<IS_F16, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "gemm2 smem attribute");
+    attr = true;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
+  int tiles = (p.M / 256) * (p.N / 256);
+  int pairs = std::min(tiles, sms / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  cuda_check(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<IS_F16, MODE>, a, b, p), "gemm_tc2 launch");
+  launched(ctx, "gemm_tc2");
 }
 
 }  // namespace gemm
@@ -470,15 +744,42 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
   p.clip_lo = ep ? ep->clip_lo : INT32_MIN;
   p.clip_hi = ep ? ep->clip_hi : INT32_MAX;
   p.err = ctx->dev_err;
-  CUtensorMap ma = make_map(a, f16, K, M, lda, BM);
-  CUtensorMap mb = make_map(b, f16, K, N, ldb, bn);
+  int mode;
   if (f16) {
-    if (bn == 256) launch<true, 256>(ctx, ma, mb, p);
-    else launch<true, 128>(ctx, ma, mb, p);
+    if (odt == FOPT_BF16) mode = EP_BF16;
+    else if (odt == FOPT_F32) mode = EP_WIDE;
+    else return false;
+  } else if (ep_kind == 1) {
+    if ((uintptr_t)scale % 16) return false;
+    const int64_t lim = 1 << 24;
+    bool fast = p.int_width == 31 && p.clip_lo >= -lim && p.clip_hi <= lim && p.clip_lo <= p.clip_hi;
+    mode = fast ? EP_RQ31 : EP_RQ;
+  } else if (odt == FOPT_I8) {
+    mode = EP_I8;
+  } else if (odt == FOPT_I32) {
+    mode = EP_WIDE;
   } else {
-    if (bn == 256) launch<false, 256>(ctx, ma, mb, p);
-    else launch<false, 128>(ctx, ma, mb, p);
+    return false;
   }
+  const bool pair = M % 256 == 0 && N % 256 == 0 && !getenv("FOPT_GEMM_1SM");
+  CUtensorMap ma = make_map(a, f16, K, M, lda, pair ? 128 : BM);
+  CUtensorMap mb = make_map(b, f16, K, N, ldb, pair ? 128 : bn);
+#define FOPT_GEMM_DISPATCH(F16, MODE)                 \
+  if (pair) launch2<F16, MODE>(ctx, ma, mb, p);       \
+  else if (bn == 256) launch<F16, 256, MODE>(ctx, ma, mb, p); \
+  else launch<F16, 128, MODE>(ctx, ma, mb, p);
+  if (f16) {
+    if (mode == EP_BF16) { FOPT_GEMM_DISPATCH(true, EP_BF16) }
+    else { FOPT_GEMM_DISPATCH(true, EP_WIDE) }
+  } else {
+    switch (mode) {
+      case EP_RQ31: { FOPT_GEMM_DISPATCH(false, EP_RQ31) } break;
+      case EP_RQ: { FOPT_GEMM_DISPATCH(false, EP_RQ) } break;
+      case EP_I8: { FOPT_GEMM_DISPATCH(false, EP_I8) } break;
+      default: { FOPT_GEMM_DISPATCH(false, EP_WIDE) } break;
+    }
+  }
+#undef FOPT_GEMM_DISPATCH
   return true;
 }
 

@@ -440,3 +440,21 @@ def test_gemm_full_size_properties(b200, dtype):
         # f32 accumulation of 4096 N(0,1) products: |err| <= 1e-4 * sqrt(K) * rms
         assert np.max(np.abs(D[rows] - ref)) <= 1e-4 * np.sqrt(K) * 2, np.max(np.abs(D[rows] - ref))
         assert np.allclose(D.sum(1), A @ B.sum(0), rtol=1e-3, atol=1.0)
+
+
+def test_gemm_tc_requant_ties_and_saturation(b200):
+    """Tensor-core requant on values that hit exact .5 ties (round half away from zero), huge and
+    negative scales (saturation into the Clip), and a NaN scale (saturates by sign, then clips)."""
+    ax = dict(M=256, K=256, N=256)
+    (L, rl), (R, rr), (P, rp), (O, ro) = (pair(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
+    lv, rv = rand_vals("i8", L.size), rand_vals("i8", R.size)
+    scale = np.tile(np.array([0.5, 0.25, -0.5, 1e30, -1e30, 0.0078125, 1.5, -0.125], np.float32), 32)
+    scale[7] = np.float32("nan")
+    scale[15] = -np.float32("nan")
+    s = b200.from_vec(fb.Mapping("[N]", dict(N=256)), scale, "f32")
+    for lo, hi in ((-128, 127), (-20, 50)):
+        got = b200.contraction_requant(b200.from_vec(L, lv, "i8"), b200.from_vec(R, rv, "i8"), L, R, P, O, s, "N",
+                                       lo=lo, hi=hi)
+        want = oracle.contract(lv.tobytes(), rv.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
+                               scale_axis="N", clip_lo=lo, clip_hi=hi)
+        assert got.to_bytes() == want
