@@ -59,13 +59,18 @@ class Clocks:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms",
-                                          "200", "-i", str(self.index)], stdout=subprocess.PIPE,
+                                          "50", "-i", str(self.index)], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
             self.proc = None
         return self
+
+    def wait_first_sample(self, timeout=5.0):
+        t0 = time.time()
+        while self.proc and not self.samples and time.time() - t0 < timeout:
+            time.sleep(0.02)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -195,6 +200,56 @@ def wl_relayout(fb, be, R=8192, C=8192):
                 dtype="bf16", config={"R": R, "C": C})
 
 
+def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096):
+    """Config 5: all-reduce of an 8x2048x4096 bf16 activation (N(0,1) per rank) over the Chip axis."""
+    if world > 1:
+        fb.dist.init_comm(be, rank, world)
+    rng = np.random.default_rng(100 + rank)
+    m = fb.Mapping("[E]", dict(E=count))
+    x = be.from_vec(m, fb.dtypes.f32_to_bf16_bits(rng.standard_normal(count).astype(np.float32)), "bf16")
+
+    def step():
+        if world > 1:
+            fb.dist.allreduce(be, x)
+        return x
+
+    nbytes = 2 * count
+    bus = 2.0 * (world - 1) / world * nbytes if world > 1 else 0.0
+    return dict(step=step, units=bus, unit="GB/s", scale=1e9, bound="nvlink", aggregate=False,
+                metric="all-reduce bus bandwidth (8x2048x4096 bf16 per rank)", workload="allreduce_bf16_128MiB",
+                dtype="bf16", config={"elements_per_rank": count, "bytes_per_rank": nbytes,
+                                      "busbw": "bytes * 2(n-1)/n / t"})
+
+
+def allreduce_sweep(fb, be, world, steps=5):
+    """1 KiB .. 1 GiB message sweep (x2 steps), bus bandwidth per size."""
+    import torch
+
+    out = []
+    size = 1024
+    buf = be.zeroed(fb.Mapping("[E]", dict(E=(1 << 30) // 2)), "bf16")
+    lib = fb._lib.lib()
+    st = torch.cuda.current_stream()
+    while size <= (1 << 30):
+        n = size // 2
+        for _ in range(2):
+            lib.fopt_allreduce(be.ctx, buf.ptr, n, fb._lib.DTYPES["bf16"])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            lib.fopt_allreduce(be.ctx, buf.ptr, n, fb._lib.DTYPES["bf16"])
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t[0])
+        out.append({"bytes": size, "us": round(ms * 1e3, 2),
+                    "busbw_gbs": round(2.0 * (world - 1) / world * size / (ms * 1e-3) / 1e9, 1)})
+        size *= 2
+    return out
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -204,8 +259,11 @@ def run_ours(args, rank, world, local):
     stream = torch.cuda.Stream()
     fb._lib.lib().fopt_set_stream(be.ctx, stream.cuda_stream)
     wl = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
-          "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be)}[args.workload]()
+          "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
+          "allreduce": lambda: wl_allreduce(fb, be, rank, world)}[args.workload]()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+    clk = Clocks(local).__enter__()  # sampling runs from before warm-up to the end of the timed steps
+    clk.wait_first_sample()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             wl["step"]()
@@ -215,7 +273,7 @@ def run_ours(args, rank, world, local):
         launches0 = be.launches
         durs = []
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-        with Clocks(local) as clk:
+        if True:
             torch.cuda.synchronize()
             wall0 = time.perf_counter()
             for i in range(args.steps):
@@ -225,7 +283,8 @@ def run_ours(args, rank, world, local):
                 ev[i][1].record(stream)
             torch.cuda.synchronize()
             wall = time.perf_counter() - wall0
-        launches = be.launches - launches0 - 0
+        clk.__exit__()
+        launches = be.launches - launches0
         durs = [a.elapsed_time(b) for a, b in ev]
         e2e = None
         if "e2e_step" in wl:
@@ -245,11 +304,18 @@ def run_ours(args, rank, world, local):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
+    sweep = allreduce_sweep(fb, be, world) if (args.workload == "allreduce" and world > 1 and args.sweep) else None
     if rank != 0:
         return
-    value = world * wl["units"] / (ms * 1e-3) / wl["scale"]
+    agg = world if wl.get("aggregate", True) else 1
+    value = agg * wl["units"] / (ms * 1e-3) / wl["scale"]
     pk = peaks()
-    if wl["bound"] == "hbm":
+    if wl["bound"] == "nvlink":
+        achieved = wl["units"] / (ms * 1e-3) / 1e9
+        roof = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": 770.0, "unit": "GB/s",
+                "frac": round(achieved / 770.0, 3), "traffic": None,
+                "peak_src": "measured peer copy 770 GB/s per direction (pool figure)"}
+    elif wl["bound"] == "hbm":
         achieved = wl["units"] / (ms * 1e-3) / 1e9
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None, "peak_src": pk["src"] + " copy"}
@@ -266,13 +332,16 @@ def run_ours(args, rank, world, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic (seeded)",
             "config": {"workload": wl["workload"], **wl["config"], "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": f"replicas x{world}" if world > 1 else "1 GPU"},
+                       "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
+                                       f"replicas x{world}") if world > 1 else "1 GPU"},
             "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
             "wall_s": round(wall, 4)}
     if e2e_ms:
         line["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
                        "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
                        "ms_per_step": round(e2e_ms, 4)}
+    if args.workload == "allreduce" and world > 1 and args.sweep:
+        line["sweep"] = sweep
     if "cpu" in wl and world == 1 and not args.no_cpu:
         rate, sample = wl["cpu"](args.cpu_rows)
         line["cpu_baseline"] = {"value": round(rate / wl["scale"], 4), "unit": wl["unit"],
@@ -315,6 +384,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="allreduce: add the 1 KiB - 1 GiB size sweep")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
