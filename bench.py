@@ -221,7 +221,7 @@ def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096):
                                       "busbw": "bytes * 2(n-1)/n / t"})
 
 
-def allreduce_sweep(fb, be, world, steps=5):
+def allreduce_sweep(fb, be, world, stream, steps=5):
     """1 KiB .. 1 GiB message sweep (x2 steps), bus bandwidth per size."""
     import torch
 
@@ -229,7 +229,7 @@ def allreduce_sweep(fb, be, world, steps=5):
     size = 1024
     buf = be.zeroed(fb.Mapping("[E]", dict(E=(1 << 30) // 2)), "bf16")
     lib = fb._lib.lib()
-    st = torch.cuda.current_stream()
+    st = stream  # the stream the library launches on
     while size <= (1 << 30):
         n = size // 2
         for _ in range(2):
@@ -304,7 +304,7 @@ def run_ours(args, rank, world, local):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms, e2e_ms = float(t[0]), float(t[1])
-    sweep = allreduce_sweep(fb, be, world) if (args.workload == "allreduce" and world > 1 and args.sweep) else None
+    sweep = allreduce_sweep(fb, be, world, stream) if (args.workload == "allreduce" and world > 1 and args.sweep) else None
     if rank != 0:
         return
     agg = world if wl.get("aggregate", True) else 1
