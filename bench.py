@@ -250,6 +250,40 @@ def allreduce_sweep(fb, be, world, stream, steps=5):
     return out
 
 
+def wl_mnist(fb, be, B=64, I=784, H=128, O=10):
+    """Config 1: MNIST-shaped int8 MLP forward (latency-bound). Unit: images/s."""
+    x, w1, w2, s1 = fb.workloads.mnist_inputs(0, B, I, H, O)
+    ax = dict(B=B, I=I, H=H, O=O)
+    m = lambda e: fb.Mapping(e, ax)
+    X, W1, W2, S1 = (be.from_vec(m("[B, I]"), x, "i8"), be.from_vec(m("[H, I]"), w1, "i8"),
+                     be.from_vec(m("[O, H]"), w2, "i8"), be.from_vec(m("[H]"), s1, "f32"))
+
+    def step():
+        return fb.workloads.mnist_int8_forward(be, X, W1, W2, S1, B, I, H, O)
+
+    return dict(step=step, units=B, unit="images/s", scale=1.0, bound="latency", flops=2.0 * B * (I * H + H * O),
+                metric="MNIST-shaped int8 MLP forward, images/s (64x784 -> 128 -> 10)", workload="mnist_int8_mlp",
+                dtype="i8", config={"B": B, "I": I, "H": H, "O": O})
+
+
+def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
+    """Config 4: W8A8 Llama-3-8B decoder block over 8 x 512 tokens. Unit: tokens/s."""
+    T, H = batch * seq, Hq * 128
+    blk = fb.workloads.DecoderBlockW8A8(be, T, H, Hq, Hkv, F, batch, seq, seed=0)
+    rng = np.random.default_rng(1)
+    X = be.from_vec(blk.m("[T, H]"), fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32)),
+                    "bf16")
+
+    def step():
+        return blk.forward(X)
+
+    return dict(step=step, units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8",
+                flops=blk.gemm_ops() + blk.attention_flops(),
+                metric="W8A8 decoder block tokens/s (Llama-3-8B shape, 8 x 512 tokens)", workload="decoder_w8a8",
+                config={"batch": batch, "seq": seq, "hidden": H, "ffn": F, "heads": Hq, "kv_heads": Hkv,
+                        "gemm_ops": blk.gemm_ops(), "attention_flops": blk.attention_flops()})
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -260,7 +294,8 @@ def run_ours(args, rank, world, local):
     fb._lib.lib().fopt_set_stream(be.ctx, stream.cuda_stream)
     wl = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
           "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
-          "allreduce": lambda: wl_allreduce(fb, be, rank, world)}[args.workload]()
+          "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
+          "decoder": lambda: wl_decoder(fb, be)}[args.workload]()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
     clk = Clocks(local).__enter__()  # sampling runs from before warm-up to the end of the timed steps
     clk.wait_first_sample()
@@ -310,7 +345,11 @@ def run_ours(args, rank, world, local):
     agg = world if wl.get("aggregate", True) else 1
     value = agg * wl["units"] / (ms * 1e-3) / wl["scale"]
     pk = peaks()
-    if wl["bound"] == "nvlink":
+    if wl["bound"] == "latency":
+        achieved = wl["flops"] / (ms * 1e-3) / 1e12
+        roof = {"bound": "latency", "achieved": round(achieved, 4), "peak": None, "unit": "TOPS", "frac": None,
+                "traffic": None, "peak_src": "launch/latency bound (13 M int-ops per forward)"}
+    elif wl["bound"] == "nvlink":
         achieved = wl["units"] / (ms * 1e-3) / 1e9
         roof = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": 770.0, "unit": "GB/s",
                 "frac": round(achieved / 770.0, 3), "traffic": None,

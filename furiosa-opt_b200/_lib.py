@@ -32,7 +32,7 @@ class Program(C.Structure):
 
 class Epilogue(C.Structure):
     _fields_ = [("kind", C.c_int32), ("scale", C.c_void_p), ("scale_axis", C.c_char_p), ("int_width", C.c_int32),
-                ("clip_lo", C.c_int32), ("clip_hi", C.c_int32)]
+                ("clip_lo", C.c_int32), ("clip_hi", C.c_int32), ("row_scale", C.c_void_p)]
 
 
 # (name, restype, argtypes) for every symbol the header declares.
@@ -47,6 +47,7 @@ SIGNATURES = [
     ("fopt_set_exact_fold", _I32, [_VP, C.c_int]),
     ("fopt_launch_count", _I64, [_VP]),
     ("fopt_alloc", _I32, [_VP, _SZ, C.POINTER(_VP)]),
+    ("fopt_alloc_uninit", _I32, [_VP, _SZ, C.POINTER(_VP)]),
     ("fopt_free", _I32, [_VP, _VP]),
     ("fopt_h2d", _I32, [_VP, _VP, _VP, _SZ]),
     ("fopt_d2h", _I32, [_VP, _VP, _VP, _SZ]),

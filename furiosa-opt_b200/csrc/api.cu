@@ -128,6 +128,10 @@ fopt_status fopt_init(int device, fopt_ctx** out) {
     cuda_check(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking), "stream create");
     ctx->stream = ctx->own_stream;
     cuda_check(cudaMalloc(&ctx->dev_err, sizeof(int32_t)), "error word");
+    cudaMemPool_t pool;
+    cuda_check(cudaDeviceGetDefaultMemPool(&pool, device), "default mem pool");
+    uint64_t keep = UINT64_MAX;
+    cuda_check(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep), "mem pool threshold");
     cuda_check(cudaMemset(ctx->dev_err, 0, sizeof(int32_t)), "error word");
   });
   if (st != FOPT_OK) {
@@ -190,17 +194,27 @@ fopt_status fopt_set_exact_fold(fopt_ctx* ctx, int exact) {
 
 int64_t fopt_launch_count(const fopt_ctx* ctx) { return ctx ? ctx->launches : 0; }
 
+// Storages come from the device's stream-ordered memory pool: allocation and release are ordered on
+// the context's stream and never synchronise the device (a plain cudaFree would), and freed blocks
+// stay cached in the pool for the next allocation (the release threshold is raised at fopt_init).
 fopt_status fopt_alloc(fopt_ctx* ctx, size_t bytes, void** dptr) {
   return guarded(ctx, [&] {
     require(dptr != nullptr, "fopt_alloc: null out pointer");
-    cuda_check(cudaMalloc(dptr, std::max<size_t>(bytes, 1)), "cudaMalloc");
+    cuda_check(cudaMallocAsync(dptr, std::max<size_t>(bytes, 1), ctx->stream), "cudaMallocAsync");
     cuda_check(cudaMemsetAsync(*dptr, 0, std::max<size_t>(bytes, 1), ctx->stream), "zero fill");
+  });
+}
+
+fopt_status fopt_alloc_uninit(fopt_ctx* ctx, size_t bytes, void** dptr) {
+  return guarded(ctx, [&] {
+    require(dptr != nullptr, "fopt_alloc_uninit: null out pointer");
+    cuda_check(cudaMallocAsync(dptr, std::max<size_t>(bytes, 1), ctx->stream), "cudaMallocAsync");
   });
 }
 
 fopt_status fopt_free(fopt_ctx* ctx, void* dptr) {
   return guarded(ctx, [&] {
-    if (dptr) cuda_check(cudaFree(dptr), "cudaFree");
+    if (dptr) cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");
   });
 }
 
@@ -423,14 +437,19 @@ fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, con
     int acc;
     require(acc_type_of(in_dtype, &acc), "fopt_contraction: unsupported operand dtype");
     int ep_kind = epilogue ? epilogue->kind : 0;
-    if (ep_kind == 1) {
+    if (ep_kind == 3) {
+      require(acc == FOPT_I32 && out_dtype == FOPT_BF16, "dequant epilogue maps an integer contraction to bf16");
+      require(epilogue->scale && epilogue->scale_axis && epilogue->row_scale,
+              "dequant epilogue needs row and channel scale vectors");
+    } else if (ep_kind == 1) {
       require(acc == FOPT_I32, "requant epilogue needs an integer contraction");
       require(out_dtype == FOPT_I8, "requant epilogue commits i8");
       require(epilogue->scale && epilogue->scale_axis, "requant epilogue needs a scale vector and its axis");
     } else {
       require(out_dtype == in_dtype || out_dtype == acc, "fopt_contraction: out dtype must be the operand or accumulator type");
     }
-    std::string extra_key = ep_kind == 1 ? std::string(epilogue->scale_axis) : "";
+    const bool scaled = ep_kind == 1 || ep_kind == 3;
+    std::string extra_key = scaled ? std::string(epilogue->scale_axis) : "";
     std::string key = "c|" + lhs_map->key + "|" + rhs_map->key + "|" + pre_reduce->key + "|" + out_map->key + "|" + extra_key;
     std::shared_ptr<FoldKPlan> kp;
     {
@@ -440,7 +459,7 @@ fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, con
     }
     if (!kp) {
       FoldPlan fp;
-      bool has_extra = ep_kind == 1;
+      bool has_extra = scaled;
       // The four mappings may come from separate axis tables; re-parse against one shared table.
       auto table = std::make_shared<AxisTable>();
       auto adopt = [&](const Mapping& m) {
@@ -459,11 +478,14 @@ fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, con
     }
     int64_t M, N, K, lda, ldb, ldd;
     int scale_n = 0;
-    if (as_gemm(*kp, &M, &N, &K, &lda, &ldb, &ldd, &scale_n) && (ep_kind != 1 || scale_n)) {
+    if (as_gemm(*kp, &M, &N, &K, &lda, &ldb, &ldd, &scale_n) && (!scaled || scale_n)) {
       if (launch_gemm_tc(ctx, out, out_dtype, lhs, rhs, in_dtype, M, N, K, lda, ldb, ldd, epilogue,
-                         ep_kind == 1 ? epilogue->scale : nullptr, scale_n))
+                         scaled ? epilogue->scale : nullptr, scale_n))
         return;
     }
+    if (ep_kind == 3)
+      throw Fail{FOPT_ERR_UNSUPPORTED, "dequant epilogue needs a GEMM-shaped contraction ([M, K] x [N, K] -> [M, N], "
+                                       "M % 128, K % 128 bytes, N % 128, scales along N)"};
     launch_contraction_generic(ctx, *kp, out, out_dtype, lhs, rhs, in_dtype, lhs_map->m.size(), rhs_map->m.size(),
                                epilogue, nullptr, ep_kind == 1 ? epilogue->scale : nullptr);
   });

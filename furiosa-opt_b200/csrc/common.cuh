@@ -122,16 +122,24 @@ __host__ __device__ inline uint32_t fxp_to_fp_bits(int32_t input, uint32_t iw) {
   return (sign << 31) | ((e & 0xff) << 23) | mant;
 }
 
-// float_to_fixedpoint (float/mod.rs:99-111): f32 -> round-half-away(f64(x) * 2^(31-iw)), clamped.
+// float_to_fixedpoint (float/mod.rs:99-111): round-half-away(f64(x) * 2^(31-iw)), clamped to i32.
+// Computed in f32 with the same result: scaling by 2^(31-iw) (iw <= 31, so a power of two >= 1) is
+// exact unless it overflows, and an overflow saturates either way; with t = trunc(y) and the exact
+// remainder d = y - t, rounding half away from zero steps away exactly when |d| >= 0.5.
 __host__ __device__ inline int32_t fp_to_fxp(float x, uint32_t iw) {
   uint32_t bits;
   memcpy(&bits, &x, 4);
   if ((bits & 0x7fffffffu) > 0x7f800000u) return (bits >> 31) ? INT32_MIN : INT32_MAX;
-  double v = (double)x * ldexp(1.0, (int)(31 - iw));
-  v = round(v);
-  if (v < -2147483648.0) v = -2147483648.0;
-  if (v > 2147483647.0) v = 2147483647.0;
-  return (int32_t)v;
+  const uint32_t sh = 31 - iw;  // 0..31
+  uint32_t pbits = (127u + sh) << 23;
+  float p2;
+  memcpy(&p2, &pbits, 4);
+  const float y = x * p2;
+  const float t = truncf(y);
+  const float r = fabsf(y - t) >= 0.5f ? t + copysignf(1.0f, y) : t;
+  if (r >= 2147483648.0f) return INT32_MAX;
+  if (r <= -2147483648.0f) return INT32_MIN;
+  return (int32_t)r;
 }
 
 // ---------------------------------------------------------------------------------------------

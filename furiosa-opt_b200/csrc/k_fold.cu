@@ -75,7 +75,9 @@ __global__ void reduce_cell_kernel(void* __restrict__ out, const void* __restric
   }
 }
 
-// One warp per output cell; the residue is one unit-stride run of `nd` elements.
+// One warp per output cell; the residue is one unit-stride run of `nd` elements. 32-bit rows whose
+// base is 16-byte aligned are read as uint4 (4 elements per lane per step) into 4 independent
+// partial folds, combined at the end (order-insensitive folds only).
 __global__ void reduce_warp_kernel(void* __restrict__ out, const void* __restrict__ src, int dt, int op, uint32_t ident,
                                    KWalk ow, int64_t out_positions, int64_t nd, int64_t src_elems) {
   const int lane = threadIdx.x & 31;
@@ -85,9 +87,26 @@ __global__ void reduce_warp_kernel(void* __restrict__ out, const void* __restric
     uint32_t acc = ident;
     bool live = walk_offsets<1>(ow, o, &base);
     if (live) {
-      for (int64_t r = lane; r < nd; r += 32) {
-        int64_t p = base + r;
-        if (p < src_elems) acc = combine(op, dt, acc, load_acc(src, dt, p));
+      const bool vec = dtype_bits(dt) == 32 && (base & 3) == 0 && ((uintptr_t)src & 15) == 0 &&
+                       base + nd <= src_elems;
+      if (vec) {
+        uint32_t a0 = ident, a1 = ident, a2 = ident, a3 = ident;
+        const uint4* row = (const uint4*)((const uint32_t*)src + base);
+        const int64_t nv = nd >> 2;
+        for (int64_t r = lane; r < nv; r += 32) {
+          uint4 v = row[r];
+          a0 = combine(op, dt, a0, v.x);
+          a1 = combine(op, dt, a1, v.y);
+          a2 = combine(op, dt, a2, v.z);
+          a3 = combine(op, dt, a3, v.w);
+        }
+        for (int64_t r = (nv << 2) + lane; r < nd; r += 32) a0 = combine(op, dt, a0, load_acc(src, dt, base + r));
+        acc = combine(op, dt, combine(op, dt, a0, a1), combine(op, dt, a2, a3));
+      } else {
+        for (int64_t r = lane; r < nd; r += 32) {
+          int64_t p = base + r;
+          if (p < src_elems) acc = combine(op, dt, acc, load_acc(src, dt, p));
+        }
       }
 #pragma unroll
       for (int s = 16; s > 0; s >>= 1) acc = combine(op, dt, acc, __shfl_xor_sync(0xffffffffu, acc, s));

@@ -139,10 +139,11 @@ struct Params {
   int ep_kind;  // 0 none, 1 requant, 2 relu
   const float* scale;
   int int_width, clip_lo, clip_hi;
+  const float* row_scale;
   int* err;
 };
 
-// Requant of one accumulator (FxpToFp -> MulF -> FpToFxp -> Clip). For int_width 31,
+// (Requant of one accumulator (FxpToFp -> MulF -> FpToFxp -> Clip). For int_width 31,
 // fixedpoint_to_float is exactly IEEE round-to-nearest-even int -> f32 and float_to_fixedpoint is
 // round-half-away-from-zero then saturation, so both collapse to single instructions.
 __device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, float s) {
@@ -168,7 +169,8 @@ __device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, flo
 //   EP_RQ31  requant at int_width 31 with clip bounds exact in f32 (the fast exact form below)
 //   EP_RQ    requant at any int_width (bit-level fixed-point restatement)
 //   EP_BF16  f32 accumulator -> bf16 (RNE, flush, canonical NaN), optional relu (cast_relu)
-enum { EP_I8 = 0, EP_WIDE = 1, EP_RQ31 = 2, EP_RQ = 3, EP_BF16 = 4 };
+//   EP_DQ    dequant: f32(acc) * row_scale[m] * scale[n] -> bf16 (FxpToFp, two MulF, cast)
+enum { EP_I8 = 0, EP_WIDE = 1, EP_RQ31 = 2, EP_RQ = 3, EP_BF16 = 4, EP_DQ = 5 };
 
 // float_to_fixedpoint at int_width 31 is round-half-away-from-zero then saturation. With t = trunc(y)
 // and d = y - t (exact), rounding away from zero is needed exactly when |d| >= 0.5. Clip bounds that
@@ -236,19 +238,37 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col
       }
       dst[j / 4] = make_uint4(v[0], v[1], v[2], v[3]);
     }
-  } else {  // EP_BF16
+  } else {  // EP_BF16, EP_DQ
+    uint32_t rr[32];
+    if constexpr (MODE == EP_DQ) {
+      const float rs = __ldg(p.row_scale + row);
+      const float4* s4 = (const float4*)(p.scale + col);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 v = __ldg(s4 + q);
+        const float sv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          float y = __fmul_rn(__int2float_rn((int32_t)r[4 * q + t]), rs);
+          rr[4 * q + t] = __float_as_uint(__fmul_rn(y, sv[t]));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) rr[j] = r[j];
+    }
     uint32_t packed[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
       uint32_t lo, hi;
       if (relu) {
-        uint32_t a = r[j], b = r[j + 1];
+        uint32_t a = rr[j], b = rr[j + 1];
         bool na = (a & 0x7fffffffu) > 0x7f800000u, nb = (b & 0x7fffffffu) > 0x7f800000u;
         lo = (!na && (a >> 31)) ? 0u : f32_to_bf16w(a);
         hi = (!nb && (b >> 31)) ? 0u : f32_to_bf16w(b);
       } else {
-        lo = f32_to_bf16w(r[j]);
-        hi = f32_to_bf16w(r[j + 1]);
+        lo = f32_to_bf16w(rr[j]);
+        hi = f32_to_bf16w(rr[j + 1]);
       }
       packed[j / 2] = (lo >> 16) | (hi & 0xffff0000u);
     }
@@ -744,11 +764,15 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
   p.clip_lo = ep ? ep->clip_lo : INT32_MIN;
   p.clip_hi = ep ? ep->clip_hi : INT32_MAX;
   p.err = ctx->dev_err;
+  p.row_scale = ep ? ep->row_scale : nullptr;
   int mode;
   if (f16) {
     if (odt == FOPT_BF16) mode = EP_BF16;
     else if (odt == FOPT_F32) mode = EP_WIDE;
     else return false;
+  } else if (ep_kind == 3) {
+    if ((uintptr_t)scale % 16 || !p.row_scale || odt != FOPT_BF16) return false;
+    mode = EP_DQ;
   } else if (ep_kind == 1) {
     if ((uintptr_t)scale % 16) return false;
     const int64_t lim = 1 << 24;
@@ -776,6 +800,7 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
       case EP_RQ31: { FOPT_GEMM_DISPATCH(false, EP_RQ31) } break;
       case EP_RQ: { FOPT_GEMM_DISPATCH(false, EP_RQ) } break;
       case EP_I8: { FOPT_GEMM_DISPATCH(false, EP_I8) } break;
+      case EP_DQ: { FOPT_GEMM_DISPATCH(false, EP_DQ) } break;
       default: { FOPT_GEMM_DISPATCH(false, EP_WIDE) } break;
     }
   }

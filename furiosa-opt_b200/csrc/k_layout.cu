@@ -75,6 +75,25 @@ __global__ void relayout_vec64(V* __restrict__ dst, const V* __restrict__ src, K
   }
 }
 
+// ---- broadcast path: the dst-innermost wheel re-reads one src element (src stride 0) ----
+template <typename T>
+__global__ void relayout_bcast(uint4* __restrict__ dst, const T* __restrict__ src, KWalk outer, int64_t inner_units,
+                               int64_t units, int64_t src_base, int64_t dst_base_v) {
+  constexpr int V = 16 / sizeof(T);
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u < units; u += (int64_t)gridDim.x * blockDim.x) {
+    int64_t off = 0;
+    if (!walk_offsets<1>(outer, u / inner_units, &off)) continue;
+    T v = src[src_base + off];
+    union {
+      uint4 q;
+      T e[V];
+    } pack;
+#pragma unroll
+    for (int k = 0; k < V; ++k) pack.e[k] = v;
+    dst[dst_base_v + u] = pack.q;
+  }
+}
+
 // ---- tile path ----
 // `others` walks every wheel except the dst-innermost (i) and the src-unit-stride (j) ones; memory
 // 0 = src offset, memory 1 = dst position. A (32 V) x (32 V) tile moves through shared memory; each
@@ -222,6 +241,22 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
                                                                    src_base / V, dst_base / V);
     }
     launched(ctx, "relayout_vec");
+    return;
+  }
+  // broadcast path: the innermost wheel is a fully-live stride-0 run of whole 16-byte vectors
+  if (w.n >= 1 && w.stride[0][0] == 0 && w.live[0] == w.extent[0] && w.extent[0] % V == 0 && V > 1 &&
+      dst_base % V == 0 && (uintptr_t)dst % 16 == 0) {
+    KWalk outer{};
+    outer.n = w.n - 1;
+    for (int i = 1; i < w.n; ++i) {
+      outer.extent[i - 1] = w.extent[i];
+      outer.live[i - 1] = w.live[i];
+      outer.stride[0][i - 1] = w.stride[0][i];
+    }
+    int64_t inner_units = w.extent[0] / V, units = p.positions / V;
+    relayout_bcast<T><<<grid_for(units), kThreads, 0, st>>>((uint4*)d, s, outer, inner_units, units, src_base,
+                                                           dst_base / V);
+    launched(ctx, "relayout_bcast");
     return;
   }
   // tile path: dst-innermost wheel strided in src, some other fully-live wheel unit-stride in src.

@@ -1,0 +1,197 @@
+"""The BASELINE configs as op sequences through the `B200` backend (every op is one or more of the
+`Backend` value ops, as the reference's engine stages issue them).
+
+* `mnist_int8_forward` -- config 1: the MNIST-shaped int8 MLP of the reference's mnist example
+  (furiosa-opt-examples/src/mnist/mod.rs:181-192: fc1 matmul -> requant / ReLU -> fc2 matmul -> host
+  argmax), with int8 weights and activations and i32 accumulation.
+* `DecoderBlockW8A8` -- config 4: a Llama-3-8B-shaped decoder block with int8 weights (per-channel
+  scales) and int8 activations (per-token scales): RMSNorm -> QKV -> causal GQA attention -> O-proj
+  -> residual -> RMSNorm -> gate/up -> SwiGLU -> down -> residual. The norm, quantisation and
+  activation steps are vector-engine ops (map / zip / reduce / broadcast relayout); the projections
+  are contractions with the fused dequant epilogue; attention is the fused kernel. Rotary position
+  embedding is not part of the config and is omitted.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import dtypes, ops
+from .backend import B200, Mapping, Storage
+
+
+# ---------------------------------------------------------------------------------------------
+# config 1
+# ---------------------------------------------------------------------------------------------
+def mnist_int8_forward(be: B200, x: Storage, w1: Storage, w2: Storage, s1: Storage, B: int, I: int, H: int,
+                       O: int) -> Storage:
+    """x [B, I] i8, w1 [H, I] i8, w2 [O, H] i8, s1 [H] f32 (per-tensor scale, broadcast along H).
+    Returns the i32 logits [B, O]; the caller takes the argmax on the host, as mnist_tests.rs:40-52."""
+    ax = dict(B=B, I=I, H=H, O=O)
+    m = lambda e: Mapping(e, ax)
+    # fc1 + requant + ReLU (Clip to [0, 127]) fused into the contraction's epilogue
+    h = be.contraction_requant(x, w1, m("[B, I]"), m("[H, I]"), m("[B, H, I]"), m("[B, H]"), s1, "H", lo=0, hi=127)
+    return be.contraction_wide(h, w2, m("[B, H]"), m("[O, H]"), m("[B, O, H]"), m("[B, O]"))
+
+
+def mnist_inputs(seed: int = 0, B: int = 64, I: int = 784, H: int = 128, O: int = 10):
+    """Config 1 inputs: x ~ U[0,1) quantised to i8 (scale 1/127), weights U[-127, 127] from a seed."""
+    rng = np.random.default_rng(seed)
+    x = np.rint(rng.random((B, I), dtype=np.float32) * 127).astype(np.int8)
+    w1 = rng.integers(-127, 128, (H, I)).astype(np.int8)
+    w2 = rng.integers(-127, 128, (O, H)).astype(np.int8)
+    s1 = np.full(H, 2.0 ** -12, np.float32)
+    return x, w1, w2, s1
+
+
+# ---------------------------------------------------------------------------------------------
+# config 4
+# ---------------------------------------------------------------------------------------------
+RMS_EPS = 1e-5
+
+
+def _prog_rinv(hidden: int):
+    # rinv = 1 / sqrt(ss / hidden + eps)
+    p = ops.Prog(1)
+    y = p.emit("MULF", 0, p.const_f32(1.0 / hidden))
+    y = p.emit("ADDF", y, p.const_f32(RMS_EPS))
+    y = p.emit("SQRT", y)
+    y = p.emit("DIVF", p.const_f32(1.0), y)
+    return p.build(y)
+
+
+def _prog_scale3():
+    p = ops.Prog(3)  # x * rinv * g
+    return p.build(p.emit("MULF", p.emit("MULF", 0, 1), 2))
+
+
+def _prog_abs():
+    p = ops.Prog(1)
+    return p.build(p.emit("AND", 0, p.const_i32(0x7FFFFFFF)))
+
+
+def _prog_token_scale():
+    # s = max(amax, tiny) / 127
+    p = ops.Prog(1)
+    y = p.emit("MAXF", 0, p.const_f32(1e-12))
+    return p.build(p.emit("DIVF", y, p.const_f32(127.0)))
+
+
+def _prog_quant():
+    # q = Clip(FpToFxp(x / s, 31), -127, 127) -> i8
+    p = ops.Prog(2)
+    y = p.emit("DIVF", 0, 1)
+    q = p.emit("FP_TO_FXP", y, imm=31)
+    q = p.emit("MAXI", q, p.const_i32(-127))
+    return p.build(p.emit("MINI", q, p.const_i32(127)))
+
+
+def _prog_residual():
+    # bf16 + bf16 -> bf16 (f32 add, RNE narrow)
+    p = ops.Prog(2)
+    return p.build(p.emit("F32_TO_BF16", p.emit("ADDF", 0, 1)))
+
+
+def _prog_swiglu():
+    # silu(g) * u = g * sigmoid(g) * u, in f32
+    p = ops.Prog(2)
+    s = p.emit("SIGMOID", 0)
+    return p.build(p.emit("MULF", p.emit("MULF", 0, s), 1))
+
+
+class DecoderBlockW8A8:
+    """Weights: int8 [N, K] (K-major) with f32 per-channel scales; RMSNorm gains f32."""
+
+    def __init__(self, be: B200, T: int, H: int, Hq: int, Hkv: int, F: int, batch: int, seq: int, seed: int = 0):
+        assert T == batch * seq and H == Hq * 128
+        self.be, self.T, self.H, self.Hq, self.Hkv, self.F = be, T, H, Hq, Hkv, F
+        self.batch, self.seq = batch, seq
+        self.KV = Hkv * 128
+        rng = np.random.default_rng(seed)
+        self.ax = dict(T=T, H=H, Q=H, V=self.KV, F=F)
+        self.host = {}
+
+        def wt(name, n, k):
+            w = rng.integers(-127, 128, (n, k)).astype(np.int8)
+            s = (rng.uniform(0.5, 1.5, n) / (127.0 * np.sqrt(k))).astype(np.float32)
+            self.host[name] = (w, s)
+            return be.from_buf(self.m(f"[{self._ax_n(n)}, {self._ax_k(k)}]"), w.tobytes(), "i8"), \
+                be.from_vec(self.m(f"[{self._ax_n(n)}]"), s, "f32")
+
+        self.wq, self.sq = wt("wq", H, H)
+        self.wk, self.sk = wt("wk", self.KV, H)
+        self.wv, self.sv = wt("wv", self.KV, H)
+        self.wo, self.so = wt("wo", H, H)
+        self.wg, self.sg = wt("wg", F, H)
+        self.wu, self.su = wt("wu", F, H)
+        self.wd, self.sd = wt("wd", H, F)
+        g1 = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        g2 = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        self.host["g1"], self.host["g2"] = g1, g2
+        # the gains broadcast over tokens once, at load time
+        self.g1 = be.relayout(be.from_vec(self.m("[H]"), g1, "f32"), self.m("[H]"), self.m("[T, H]"), True)
+        self.g2 = be.relayout(be.from_vec(self.m("[H]"), g2, "f32"), self.m("[H]"), self.m("[T, H]"), True)
+        self.p_rinv_h = _prog_rinv(H)
+        self.p_rinv_f = _prog_rinv(F)
+
+    # axis naming: H (hidden) doubles as the K of the projections; V the kv width; F the FFN width
+    def _ax_n(self, n):
+        return {self.H: "Q", self.KV: "V", self.F: "F"}[n]
+
+    def _ax_k(self, k):
+        return {self.H: "H", self.F: "F"}[k]
+
+    def m(self, e: str) -> Mapping:
+        return Mapping(e, self.ax)
+
+    # ---- vector-engine steps ----
+    def rmsnorm(self, x_f32: Storage, g: Storage) -> Storage:
+        be, m = self.be, self.m
+        sq = be.zip_with(x_f32, x_f32, ops.fp_binary("MulF"), "f32")
+        ss = be.reduce(sq, "Add", 0.0, m("[T, H]"), m("[T]"))
+        rinv = be.map(ss, self.p_rinv_h, "f32")
+        rb = be.relayout(rinv, m("[T]"), m("[T, H]"), allow_broadcast=True)
+        return be.zip3_with(x_f32, rb, g, _prog_scale3(), "f32")
+
+    def quantize(self, x_f32: Storage, width: str):
+        """Per-token symmetric int8: s[t] = max|x[t, :]| / 127, q = Clip(round(x / s), -127, 127)."""
+        be, m = self.be, self.m
+        a = be.map(x_f32, _prog_abs(), "f32")
+        amax = be.reduce(a, "Max", 0.0, m(f"[T, {width}]"), m("[T]"))
+        s = be.map(amax, _prog_token_scale(), "f32")
+        sb = be.relayout(s, m("[T]"), m(f"[T, {width}]"), allow_broadcast=True)
+        q = be.zip_with(x_f32, sb, _prog_quant(), "i8")
+        return q, s
+
+    def proj(self, q: Storage, s_tok: Storage, w: Storage, s_w: Storage, k_ax: str, n_ax: str) -> Storage:
+        m = self.m
+        return self.be.contraction_dequant(q, w, m(f"[T, {k_ax}]"), m(f"[{n_ax}, {k_ax}]"), m(f"[T, {n_ax}, {k_ax}]"),
+                                           m(f"[T, {n_ax}]"), s_tok, s_w, n_ax)
+
+    def forward(self, x: Storage) -> Storage:
+        """x: bf16 [T, H] -> bf16 [T, H]."""
+        be = self.be
+        xf = be.map(x, ops.cast("bf16", "f32"), "f32")
+        q, s = self.quantize(self.rmsnorm(xf, self.g1), "H")
+        Q = self.proj(q, s, self.wq, self.sq, "H", "Q")
+        K = self.proj(q, s, self.wk, self.sk, "H", "V")
+        V = self.proj(q, s, self.wv, self.sv, "H", "V")
+        att = be.attention(Q, K, V, self.batch, self.seq, self.Hq, self.Hkv, 128, causal=True)
+        qa, sa = self.quantize(be.map(att, ops.cast("bf16", "f32"), "f32"), "H")
+        o = self.proj(qa, sa, self.wo, self.so, "H", "Q")
+        h1 = be.zip_with(x, o, _prog_residual(), "bf16")
+        h1f = be.map(h1, ops.cast("bf16", "f32"), "f32")
+        q2, s2 = self.quantize(self.rmsnorm(h1f, self.g2), "H")
+        g = self.proj(q2, s2, self.wg, self.sg, "H", "F")
+        u = self.proj(q2, s2, self.wu, self.su, "H", "F")
+        act = be.zip_with(g, u, _prog_swiglu(), "f32")
+        q3, s3 = self.quantize(act, "F")
+        d = self.proj(q3, s3, self.wd, self.sd, "F", "Q")
+        return be.zip_with(h1, d, _prog_residual(), "bf16")
+
+    def gemm_ops(self) -> float:
+        """Algorithmic int8 ops of the block's projections."""
+        T, H, KV, F = self.T, self.H, self.KV, self.F
+        return 2.0 * T * H * (H + 2 * KV + H + 3 * F)
+
+    def attention_flops(self) -> float:
+        return 4.0 * self.seq * self.seq * 128 * self.Hq / 2 * self.batch

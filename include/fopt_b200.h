@@ -66,7 +66,11 @@ fopt_status fopt_set_exact_fold(fopt_ctx* ctx, int exact);
 int64_t fopt_launch_count(const fopt_ctx* ctx);
 
 /* ---- memory (BufStorage::zeroed / from_buf / into_buf, buf.rs:83-109,627-629) ---- */
+/* Allocations are stream-ordered (the device's memory pool, on the context's stream): they do not
+ * synchronise the device, and released blocks are reused. */
 fopt_status fopt_alloc(fopt_ctx* ctx, size_t bytes, void** dptr); /* zero-filled */
+/* For outputs an op fully overwrites (map / zip / reduce / contraction results): no zero fill. */
+fopt_status fopt_alloc_uninit(fopt_ctx* ctx, size_t bytes, void** dptr);
 fopt_status fopt_free(fopt_ctx* ctx, void* dptr);
 fopt_status fopt_h2d(fopt_ctx* ctx, void* dst, const void* host, size_t bytes);
 fopt_status fopt_d2h(fopt_ctx* ctx, void* host, const void* src, size_t bytes);
@@ -203,11 +207,14 @@ fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void* src, fopt_
  * keeps the wide sum (the engine's contract_lane output). An optional epilogue fuses the
  * vector-engine requant chain that follows (FxpToFp -> MulF scale -> FpToFxp -> Clip -> commit). */
 typedef struct {
-  int32_t kind;           /* 0 none; 1 requant i32 -> i8 with per-channel scale; 2 relu */
-  const float* scale;     /* kind 1: one f32 per coordinate of `scale_axis` */
-  const char* scale_axis; /* kind 1: axis name the scale vector runs along (e.g. "N") */
+  int32_t kind;           /* 0 none; 1 requant i32 -> i8 with per-channel scale; 2 relu;
+                             3 dequant i32 -> bf16: FxpToFp -> MulF row_scale[m] -> MulF scale[n] -> cast
+                             (per-token x per-channel W8A8; GEMM-shaped contractions only) */
+  const float* scale;     /* kind 1, 3: one f32 per coordinate of `scale_axis` */
+  const char* scale_axis; /* kind 1, 3: axis name the scale vector runs along (e.g. "N") */
   int32_t int_width;      /* FxpToFp / FpToFxp integer width (31 = plain integers) */
   int32_t clip_lo, clip_hi; /* kind 1: Clip bounds before the i8 commit */
+  const float* row_scale; /* kind 3: one f32 per output row (the outer output axis, e.g. the token) */
 } fopt_epilogue;
 fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, const void* lhs, const void* rhs,
                              fopt_dtype in_dtype, const fopt_mapping* lhs_map, const fopt_mapping* rhs_map,

@@ -187,7 +187,7 @@ def reduce(src: bytes, dtype: str, op: int, ident_bits: int, Src: RefMapping, Ds
 
 def contract(lhs: bytes, rhs: bytes, in_dtype: str, out_dtype: str, L: RefMapping, R: RefMapping, P: RefMapping,
              O: RefMapping, ep_kind: int = 0, scale=None, scale_axis: str = None, int_width: int = 31,
-             clip_lo: int = -128, clip_hi: int = 127, out_cells=None) -> bytes:
+             clip_lo: int = -128, clip_hi: int = 127, out_cells=None, row_scale=None, row_axis: str = None) -> bytes:
     """BufStorage::contraction_in. `out_cells` optionally restricts the fold to the first k output
     cells (the bounded CPU-baseline sample); the returned image then covers just those cells."""
     kept = O.idents()
@@ -198,17 +198,22 @@ def contract(lhs: bytes, rhs: bytes, in_dtype: str, out_dtype: str, L: RefMappin
     br, dr = _plan(R, O, res, n_res, n_out)
     sidx = np.zeros(n_out, np.int64)
     sc = np.zeros(1, np.float32)
-    if ep_kind == 1:
+    ridx = np.zeros(n_out, np.int64)
+    rs = np.zeros(1, np.float32)
+    if ep_kind in (1, 3):
         _, oco = O.cells(np.arange(n_out))
         sidx = oco[scale_axis].astype(np.int64)
         sc = np.asarray(scale, np.float32)
+        if ep_kind == 3:
+            ridx = oco[row_axis].astype(np.int64)
+            rs = np.asarray(row_scale, np.float32)
     out = np.zeros(nbytes(out_dtype, n_out) + 4, np.uint8)
     lb, rb = _buf(lhs), _buf(rhs)
     global last_fold_seconds
     t0 = time.perf_counter()
     lib().ref_contract(_p(out), DT[out_dtype], _p(lb), _p(rb), DT[in_dtype], _p(bl), _p(dl), _p(br), _p(dr),
                        C.c_int64(n_out), C.c_int64(n_res), C.c_int64(L.size), C.c_int64(R.size), ep_kind, _p(sc),
-                       _p(sidx), int_width, clip_lo, clip_hi)
+                       _p(sidx), int_width, clip_lo, clip_hi, _p(rs), _p(ridx))
     last_fold_seconds = time.perf_counter() - t0
     return out[: nbytes(out_dtype, n_out)].tobytes()
 

@@ -172,11 +172,13 @@ static float widen_f(const void* p, int dt, int64_t i) {
   return dt == BF16 ? u2f(bf16_to_f32(w)) : u2f(w);
 }
 
-/* ep_kind: 0 none, 1 requant (FxpToFp -> MulF scale[sidx] -> FpToFxp -> Clip), 2 relu */
+/* ep_kind: 0 none, 1 requant (FxpToFp -> MulF scale[sidx] -> FpToFxp -> Clip), 2 relu,
+ * 3 dequant (FxpToFp -> MulF row_scale[ridx] -> MulF scale[sidx] -> bf16) */
 void ref_contract(void* out, int out_dt, const void* lhs, const void* rhs, int in_dt, const int64_t* base_l,
                   const int64_t* delta_l, const int64_t* base_r, const int64_t* delta_r, int64_t n_out,
                   int64_t n_delta, int64_t lhs_len, int64_t rhs_len, int ep_kind, const float* scale,
-                  const int64_t* sidx, int int_width, int clip_lo, int clip_hi) {
+                  const int64_t* sidx, int int_width, int clip_lo, int clip_hi, const float* row_scale,
+                  const int64_t* ridx) {
   int nibble = bits_of(out_dt) == 4;
 #pragma omp parallel for schedule(static) if (!nibble)
   for (int64_t o = 0; o < n_out; ++o) {
@@ -189,7 +191,13 @@ void ref_contract(void* out, int out_dt, const void* lhs, const void* rhs, int i
           if (pl < lhs_len && pr < rhs_len)
             acc = (int32_t)((uint32_t)acc + (uint32_t)((int32_t)ld(lhs, in_dt, pl) * (int32_t)ld(rhs, in_dt, pr)));
         }
-        if (ep_kind == 1) {
+        if (ep_kind == 3) {
+          /* dequant: FxpToFp -> MulF row scale -> MulF channel scale -> bf16 cast */
+          float y = u2f(ref_fxp_to_fp(acc, (uint32_t)int_width));
+          y = y * row_scale[ridx[o]];
+          y = y * scale[sidx[o]];
+          res = f32_to_bf16(f2u(y));
+        } else if (ep_kind == 1) {
           float y = u2f(ref_fxp_to_fp(acc, (uint32_t)int_width));
           y = y * scale[sidx[o]];
           int32_t q = ref_fp_to_fxp(f2u(y), (uint32_t)int_width);

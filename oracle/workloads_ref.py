@@ -1,0 +1,80 @@
+"""ORACLE (test infrastructure only): CPU restatements of the config-1 and config-4 op chains.
+
+Integer projections fold through `ref_contract` (BufStorage::contraction_in, buf.rs:401-447) with
+the vector-engine epilogues; the float steps restate the vector-engine ops in numpy float32 in the
+same order (semantics.rs: MulF, AddF, DivF, Sqrt, Sigmoid; float/mod.rs float_to_fixedpoint);
+attention uses `ref_attention` (attention.rs chain).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import attention, contract
+from .mapping_ref import ref_m
+
+
+def _bf16_bits(x: np.ndarray) -> np.ndarray:
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    sub = ((u >> 23) & 0xFF) == 0
+    hi = (u >> 16) & 0xFFFF
+    up = ((u & 0x8000) != 0) & ((u & 0x17FFF) != 0)
+    out = np.where(nan, 0x7FC0, np.where(sub, hi & 0x8000, hi + up))
+    return (out & 0xFFFF).astype(np.uint16)
+
+
+def _f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def mnist_ref(x, w1, w2, s1, B, I, H, O) -> np.ndarray:
+    ax = dict(B=B, I=I, H=H, O=O)
+    m = lambda e: ref_m(e, **ax)
+    h = contract(x.tobytes(), w1.tobytes(), "i8", "i8", m("[B, I]"), m("[H, I]"), m("[B, H, I]"), m("[B, H]"),
+                 ep_kind=1, scale=s1, scale_axis="H", clip_lo=0, clip_hi=127)
+    logits = contract(h, w2.tobytes(), "i8", "i32", m("[B, H]"), m("[O, H]"), m("[B, O, H]"), m("[B, O]"))
+    return np.frombuffer(logits, np.int32).reshape(B, O)
+
+
+def _round_half_away(y: np.ndarray) -> np.ndarray:
+    y = y.astype(np.float64)
+    return np.sign(y) * np.floor(np.abs(y) + 0.5)
+
+
+def decoder_ref(x_bits: np.ndarray, host: dict, T, H, Hq, Hkv, F, batch, seq, eps=1e-5) -> np.ndarray:
+    KV = Hkv * 128
+
+    def rmsnorm(x, g, width):
+        ss = np.sum(x * x, axis=1, dtype=np.float32)
+        rinv = np.float32(1.0) / np.sqrt(ss * np.float32(1.0 / width) + np.float32(eps))
+        return (x * rinv[:, None]) * g[None, :]
+
+    def quant(x):
+        amax = np.max(np.abs(x), axis=1)
+        s = np.maximum(amax, np.float32(1e-12)) / np.float32(127.0)
+        q = _round_half_away(x / s[:, None])
+        return np.clip(q, -127, 127).astype(np.int8), s.astype(np.float32)
+
+    def proj(q, s, name):
+        w, sw = host[name]
+        n, k = w.shape
+        ax = dict(T=T, N=n, K=k)
+        m = lambda e: ref_m(e, **ax)
+        out = contract(q.tobytes(), w.tobytes(), "i8", "bf16", m("[T, K]"), m("[N, K]"), m("[T, N, K]"), m("[T, N]"),
+                       ep_kind=3, scale=sw, scale_axis="N", row_scale=s, row_axis="T")
+        return np.frombuffer(out, np.uint16).reshape(T, n)
+
+    x = _f32(x_bits).reshape(T, H)
+    q, s = quant(rmsnorm(x, host["g1"], H))
+    Q, K, V = proj(q, s, "wq"), proj(q, s, "wk"), proj(q, s, "wv")
+    att = attention(Q.reshape(-1), K.reshape(-1), V.reshape(-1), batch, seq, Hq, Hkv, 128, 128 ** -0.5, True)
+    qa, sa = quant(_f32(att).reshape(T, H))
+    o = proj(qa, sa, "wo")
+    h1 = _bf16_bits(x + _f32(o))
+    h1f = _f32(h1)
+    q2, s2 = quant(rmsnorm(h1f, host["g2"], H))
+    g, u = _f32(proj(q2, s2, "wg")), _f32(proj(q2, s2, "wu"))
+    act = (g * (np.float32(1.0) / (np.float32(1.0) + np.exp(-g)))) * u
+    q3, s3 = quant(act)
+    d = proj(q3, s3, "wd")
+    return _bf16_bits(h1f + _f32(d))

@@ -119,6 +119,8 @@ RELAYOUTS = [
     ("[A, B]", "[[A, B] # 100]", dict(A=7, B=13), False),
     ("[A / 4 % 4, A % 4, B]", "[A % 4, A / 4 % 4, B]", dict(A=16, B=64), False),
     ("[N, G, T]", "[N, T / 8, G, T % 8]", dict(N=4, G=16, T=128), False),
+    ("[T]", "[T, H]", dict(T=24, H=64), True),  # broadcast along the innermost axis
+    ("[H]", "[T, H]", dict(T=24, H=64), True),
 ]
 
 
@@ -458,3 +460,17 @@ def test_gemm_tc_requant_ties_and_saturation(b200):
         want = oracle.contract(lv.tobytes(), rv.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
                                scale_axis="N", clip_lo=lo, clip_hi=hi)
         assert got.to_bytes() == want
+
+
+@pytest.mark.parametrize("iw", [0, 1, 4, 16, 24, 30, 31])
+def test_fp_to_fxp_edges(b200, iw):
+    """float_to_fixedpoint on ties, near-saturation and tiny values (float/mod.rs:99-111)."""
+    rng = np.random.default_rng(iw)
+    scale = 2.0 ** (31 - iw)
+    ties = ((np.arange(-64, 64) + 0.5) / scale).astype(np.float32)
+    near = (np.array([2 ** 31 - 128, 2 ** 31, 2 ** 31 + 256, -2 ** 31, -2 ** 31 - 256, 2 ** 24 + 1]) / scale)
+    vals = np.concatenate([ties, near.astype(np.float32), rng.standard_normal(3000).astype(np.float32) * 100,
+                           np.array([0.0, -0.0, 1e-30, -1e-30, np.inf, -np.inf, np.nan], np.float32)])
+    vals = vals.astype(np.float32)
+    got, want = _ew_case(b200, ops.fp_to_fxp(iw), ["f32"], "i32", n=len(vals), values=[vals])
+    assert got == want

@@ -1,0 +1,41 @@
+"""Configs 1 and 4 end to end through the backend, against the oracle's restatement of the same op
+chains. Config 1 is integer throughout: logits bit-exact, argmax equal. Config 4 mixes int8
+projections with f32 vector-engine steps whose float rounding can move an int8 quantisation step,
+so its bf16 output is held to a stated tolerance (max abs error <= 3 % of the output's max |value|,
+mean abs error <= 0.3 %), with the error reported."""
+import numpy as np
+import pytest
+
+import furiosa_opt_b200 as fb
+from furiosa_opt_b200 import workloads as W
+from oracle import workloads_ref as R
+
+pytestmark = pytest.mark.gpu
+
+
+def test_mnist_int8_mlp_bit_exact(b200):
+    B, I, H, O = 64, 784, 128, 10
+    x, w1, w2, s1 = W.mnist_inputs(0, B, I, H, O)
+    ax = dict(B=B, I=I, H=H, O=O)
+    m = lambda e: fb.Mapping(e, ax)
+    logits = W.mnist_int8_forward(b200, b200.from_vec(m("[B, I]"), x, "i8"), b200.from_vec(m("[H, I]"), w1, "i8"),
+                                  b200.from_vec(m("[O, H]"), w2, "i8"), b200.from_vec(m("[H]"), s1, "f32"),
+                                  B, I, H, O).to_numpy().reshape(B, O)
+    want = R.mnist_ref(x, w1, w2, s1, B, I, H, O)
+    assert np.array_equal(logits, want)
+    assert np.array_equal(logits.argmax(1), want.argmax(1))
+
+
+def test_decoder_block_w8a8(b200):
+    batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+    T, H = batch * seq, Hq * 128
+    blk = W.DecoderBlockW8A8(b200, T, H, Hq, Hkv, F, batch, seq, seed=3)
+    rng = np.random.default_rng(5)
+    x = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32))
+    got = fb.dtypes.bf16_bits_to_f32(blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_numpy())
+    want = fb.dtypes.bf16_bits_to_f32(R.decoder_ref(x, blk.host, T, H, Hq, Hkv, F, batch, seq)).reshape(-1)
+    err = np.abs(got - want)
+    scale = np.max(np.abs(want))
+    assert np.all(np.isfinite(got))
+    assert err.max() <= 0.03 * scale, f"max abs err {err.max()} vs max |out| {scale}"
+    assert err.mean() <= 0.003 * scale, f"mean abs err {err.mean()}"
