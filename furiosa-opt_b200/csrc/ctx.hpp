@@ -97,6 +97,8 @@ void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, in
 bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const void* b, int in_dt, int64_t M,
                     int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldd, const fopt_epilogue* ep,
                     const float* scale, int scale_along_n);
+bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int B, int S, int Hq,
+                         int Hkv, int D, float scale, int causal, float eps);
 void launch_attention(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int B, int S, int Hq,
                       int Hkv, int D, float scale, int causal, float eps);
 void launch_gather_rows(fopt_ctx* ctx, void* dst, const void* table, const int32_t* idx, int64_t n_idx,

@@ -99,7 +99,7 @@ __global__ void __launch_bounds__(256) attention_rows_kernel(uint16_t* __restric
 
 void launch_attention(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int B, int S, int Hq,
                       int Hkv, int D, float scale, int causal, float eps) {
-  (void)D;
+  if (launch_attention_tc(ctx, o, q, k, v, B, S, Hq, Hkv, D, scale, causal, eps)) return;
   int row_tiles = (S + kRows - 1) / kRows;
   int64_t blocks = (int64_t)B * Hq * row_tiles;
   attention_rows_kernel<<<(unsigned)blocks, 256, 0, ctx->stream>>>((uint16_t*)o, (const uint16_t*)q,

@@ -1,0 +1,434 @@
+// Tensor-core fused attention (tcgen05 + TMEM + TMA), the sm_100a path of fopt_attention:
+// softmax(Q K^T * scale + causal mask) V with the online softmax of the reference's chunked op chain
+// (furiosa-opt-examples/src/transformer/kernel/attention.rs:32-392: qk_scaled, row_max, masked_exp,
+// row_sum + EPS, weighted_sum, online rescale, norm).
+//
+// One CTA per (batch, query head, 128-row query block); 192 threads:
+//   warp 0   TMA producer: Q once, then K and V^T tiles (128 keys) into a 2-stage ring;
+//   warp 1   TMEM owner and single-thread MMA issuer: S_j = Q K_j^T (M=N=K=128, bf16 -> f32) into one of
+//            two TMEM S buffers, then O += P_j V_j into the TMEM O accumulator;
+//   warps 2-5 softmax: one thread per query row reads its 128 scores from TMEM (no cross-thread
+//            reduction), keeps the running max / sum in registers, rescales its O row in TMEM when the
+//            max grows, and writes P_j (bf16) into shared memory in the UMMA K-major 128B-swizzle layout.
+// S_{j+1} is issued before waiting for P_j, so the QK^T of the next block overlaps this block's
+// softmax. V is transposed once per call (V^T [B, Hkv, D, S]) so both MMAs read K-major operands.
+// Every wait is bounded (~2 s of %globaltimer) and reports through the context's device error word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "ctx.hpp"
+
+namespace fopt {
+namespace attn {
+
+constexpr int BQ = 128, BK = 128, D = 128;
+constexpr int STAGES = 2;
+constexpr int THREADS = 192;
+constexpr int TILE = BQ * D * 2;    // one 128 x 128 bf16 tile = 32 KiB (two 128-byte-row chunks)
+constexpr int CHUNK = TILE / 2;     // 128 rows x 128 B
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                          int code) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0 = gtimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try(bar, parity)) return true;
+    if ((it & 255) == 0) {
+      if (*abort_flag) return false;
+      if (gtimer() - t0 > kWaitNs) {
+        *abort_flag = 1;
+        atomicExch(err, code);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::
+          "r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+#define R32(i) "=r"(r[i])
+__device__ __forceinline__ void tld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : R32(0), R32(1), R32(2), R32(3), R32(4), R32(5), R32(6), R32(7), R32(8), R32(9), R32(10), R32(11), R32(12),
+        R32(13), R32(14), R32(15), R32(16), R32(17), R32(18), R32(19), R32(20), R32(21), R32(22), R32(23), R32(24),
+        R32(25), R32(26), R32(27), R32(28), R32(29), R32(30), R32(31)
+      : "r"(taddr));
+}
+#undef R32
+#define S32(i) "r"(r[i])
+__device__ __forceinline__ void tst32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      S32(0), S32(1), S32(2), S32(3), S32(4), S32(5), S32(6), S32(7), S32(8), S32(9), S32(10), S32(11), S32(12),
+      S32(13), S32(14), S32(15), S32(16), S32(17), S32(18), S32(19), S32(20), S32(21), S32(22), S32(23), S32(24),
+      S32(25), S32(26), S32(27), S32(28), S32(29), S32(30), S32(31)
+      : "memory");
+}
+#undef S32
+__device__ __forceinline__ void tld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+struct Params {
+  uint16_t* O;
+  int B, S, Hq, Hkv;
+  int causal;
+  float scale_log2;  // scale * log2(e)
+  float eps;
+  int* err;
+};
+
+// Packs two f32 into bf16x2 with RNE (finite values; the softmax produces no NaN for finite inputs).
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t a = f32_to_bf16w(__float_as_uint(lo)), b = f32_to_bf16w(__float_as_uint(hi));
+  return (a >> 16) | (b & 0xffff0000u);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmVt, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;                       // 32 KiB
+  uint8_t* sP = smem + TILE;                // 32 KiB
+  uint8_t* sKV = smem + 2 * TILE;           // STAGES x (K tile + V^T tile)
+  uint64_t* bars = (uint64_t*)(smem + 2 * TILE + STAGES * 2 * TILE);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 1 + STAGES;
+  uint64_t* s_full = bars + 1 + 2 * STAGES;
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_ready = s_free + 2;
+  uint64_t* o_done = p_ready + 1;
+  uint32_t* tmem_slot = (uint32_t*)(o_done + 1);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = p.S / BQ;
+  // heaviest (last) query blocks first under causal masking
+  const int qb = nqb - 1 - (int)(blockIdx.x % nqb);
+  const int h = (int)((blockIdx.x / nqb) % p.Hq);
+  const int b = (int)(blockIdx.x / (nqb * p.Hq));
+  const int hk = h / (p.Hq / p.Hkv);
+  const int nkb = p.causal ? qb + 1 : p.S / BK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&kv_full[s]), 1);
+      mbar_init(smem_u32(&kv_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&s_full[s]), 1);
+      mbar_init(smem_u32(&s_free[s]), 128);
+    }
+    mbar_init(smem_u32(p_ready), 128);
+    mbar_init(smem_u32(o_done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 128};
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int row0 = b * p.S;  // flattened (batch, seq) row of the tensor maps
+      const uint32_t qb_ = smem_u32(q_full);
+      mbar_expect_tx(qb_, TILE);
+      tma3(smem_u32(sQ), &tmQ, qb_, 0, h, row0 + qb * BQ);
+      tma3(smem_u32(sQ + CHUNK), &tmQ, qb_, 64, h, row0 + qb * BQ);
+      for (int j = 0; j < nkb; ++j) {
+        const int st = j % STAGES;
+        if (!mbar_wait(smem_u32(&kv_empty[st]), ((j / STAGES) & 1) ^ 1, abort_flag, p.err, 301)) break;
+        const uint32_t fb = smem_u32(&kv_full[st]);
+        mbar_expect_tx(fb, 2 * TILE);
+        uint8_t* sK = sKV + st * 2 * TILE;
+        uint8_t* sV = sK + TILE;
+        tma3(smem_u32(sK), &tmK, fb, 0, hk, row0 + j * BK);
+        tma3(smem_u32(sK + CHUNK), &tmK, fb, 64, hk, row0 + j * BK);
+        tma3(smem_u32(sV), &tmVt, fb, j * BK, 0, b * p.Hkv + hk);
+        tma3(smem_u32(sV + CHUNK), &tmVt, fb, j * BK + 64, 0, b * p.Hkv + hk);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, p.err, 302);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % STAGES, buf = j & 1;
+        if (!mbar_wait(smem_u32(&kv_full[st]), (j / STAGES) & 1, abort_flag, p.err, 303)) return false;
+        if (j >= 2 && !mbar_wait(smem_u32(&s_free[buf]), ((j - 2) >> 1) & 1, abort_flag, p.err, 304)) return false;
+        fence_after();
+        const uint32_t sK = smem_u32(sKV + st * 2 * TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+          mma_bf16(tS[buf], sdesc(smem_u32(sQ) + off), sdesc(sK + off), idesc, k != 0);
+        }
+        commit(smem_u32(&s_full[buf]));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < nkb; ++j) {
+        if (j + 1 < nkb && !issue_s(j + 1)) break;
+        if (!mbar_wait(smem_u32(p_ready), j & 1, abort_flag, p.err, 305)) break;
+        fence_after();
+        const int st = j % STAGES;
+        const uint32_t sV = smem_u32(sKV + st * 2 * TILE + TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+          mma_bf16(tO, sdesc(smem_u32(sP) + off), sdesc(sV + off), idesc, (j | k) != 0);
+        }
+        commit(smem_u32(&kv_empty[st]));
+        commit(smem_u32(o_done));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax: one thread per query row ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // row within the block = TMEM lane
+    const int qrow = qb * BQ + r;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkb; ++j) {
+      const int buf = j & 1;
+      ok = mbar_wait(smem_u32(&s_full[buf]), (j >> 1) & 1, abort_flag, p.err, 306);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      fence_after();
+      uint32_t s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tld32(tS[buf] + lane_base + c * 32, s + 32 * c);
+      tld_wait();
+      fence_before();
+      mbar_arrive(smem_u32(&s_free[buf]));
+      // scores in log2 units, causal mask on the diagonal block
+      const bool diag = p.causal && j == qb;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        float v = __uint_as_float(s[c]) * p.scale_log2;
+        if (diag && c > r) v = -INFINITY;
+        s[c] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      const float mnew = fmaxf(m, mx);
+      const float alpha = exp2f(m - mnew);  // m = -inf on the first block -> alpha = 0
+      float sum = 0.0f;
+      uint32_t* pk = s;  // packed bf16 pairs overwrite the scores in place (index c / 2 <= c)
+#pragma unroll
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = exp2f(__uint_as_float(s[c]) - mnew), p1 = exp2f(__uint_as_float(s[c + 1]) - mnew);
+        sum += p0 + p1;
+        pk[c / 2] = pack_bf16(p0, p1);
+      }
+      l = l * alpha + sum;
+      m = mnew;
+      // PV_{j-1} must be complete: P smem is free and the O row is stable
+      if (j > 0) {
+        ok = mbar_wait(smem_u32(o_done), (j - 1) & 1, abort_flag, p.err, 307);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        fence_after();
+        // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp rescales when any row
+        // of it needs to, rows whose max did not move multiply by 1.
+        if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tld32(tO + lane_base + c * 32, o);
+            tld_wait();
+#pragma unroll
+            for (int t = 0; t < 32; ++t) o[t] = __float_as_uint(__uint_as_float(o[t]) * alpha);
+            tst32(tO + lane_base + c * 32, o);
+          }
+          tst_wait();
+        }
+      }
+      // P row -> shared memory, K-major 128B swizzle: chunk = key / 64, 16-byte unit u ^ (row % 8)
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int chunk = u >> 3, unit = u & 7;
+        uint4* dst = (uint4*)(sP + chunk * CHUNK + r * 128 + ((unit ^ (r & 7)) << 4));
+        *dst = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      fence_before();
+      mbar_arrive(smem_u32(p_ready));
+    }
+    if (ok && nkb > 0) {
+      ok = mbar_wait(smem_u32(o_done), (nkb - 1) & 1, abort_flag, p.err, 308);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok && qrow < p.S) {
+      fence_after();
+      const float inv = 1.0f / (l + p.eps);
+      uint16_t* orow = p.O + (((int64_t)b * p.S + qrow) * p.Hq + h) * D;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tld32(tO + lane_base + c * 32, o);
+        tld_wait();
+        uint4* dst = (uint4*)(orow + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          dst[q] = make_uint4(pack_bf16(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                              pack_bf16(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
+// V [B, S, Hkv, D] -> V^T [B, Hkv, D, S] (32 x 32 tiles through shared memory)
+__global__ void transpose_v_kernel(uint16_t* __restrict__ vt, const uint16_t* __restrict__ v, int S, int Hkv) {
+  __shared__ uint16_t tile[32][34];
+  const int bh = blockIdx.z, b = bh / Hkv, hk = bh % Hkv;
+  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  for (int i = threadIdx.y; i < 32; i += 8)
+    tile[i][threadIdx.x] = v[(((int64_t)b * S + s0 + i) * Hkv + hk) * D + d0 + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8)
+    vt[(((int64_t)b * Hkv + hk) * D + d0 + i) * S + s0 + threadIdx.x] = tile[threadIdx.x][i];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  });
+  if (!fn) throw Fail{FOPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable"};
+  return fn;
+}
+
+// A 3-d bf16 tensor map with a 64-element (128-byte) inner box and 128-byte swizzle.
+CUtensorMap map3(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_bytes,
+                 uint64_t stride2_bytes, uint32_t box1, uint32_t box2) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {64, box1, box2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "cuTensorMapEncodeTiled (attention) failed"};
+  return m;
+}
+
+}  // namespace attn
+
+bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, const void* v, int B, int S, int Hq,
+                         int Hkv, int Dh, float scale, int causal, float eps) {
+  using namespace attn;
+  if (Dh != 128 || S % 128 || getenv("FOPT_ATTN_NO_TC")) return false;
+  if ((uintptr_t)q % 16 || (uintptr_t)k % 16 || (uintptr_t)v % 16 || (uintptr_t)o % 16) return false;
+  // V^T into context scratch
+  const size_t vt_bytes = (size_t)B * Hkv * D * S * 2;
+  uint16_t* vt = (uint16_t*)scratch(ctx, vt_bytes);
+  transpose_v_kernel<<<dim3(S / 32, D / 32, B * Hkv), dim3(32, 8), 0, ctx->stream>>>(vt, (const uint16_t*)v, S, Hkv);
+  launched(ctx, "attention_transpose_v");
+  const uint64_t rows = (uint64_t)B * S;
+  CUtensorMap mq = map3(q, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 128);
+  CUtensorMap mk = map3(k, D, Hkv, rows, (uint64_t)D * 2, (uint64_t)Hkv * D * 2, 1, 128);
+  CUtensorMap mv = map3(vt, S, D, (uint64_t)B * Hkv, (uint64_t)S * 2, (uint64_t)D * S * 2, 128, 1);
+  Params p{};
+  p.O = (uint16_t*)o;
+  p.B = B;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.causal = causal;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.eps = eps;
+  p.err = ctx->dev_err;
+  constexpr int smem = 2 * TILE + STAGES * 2 * TILE + 1024 + 256;
+  static bool attr = false;
+  if (!attr) {
+    cuda_check(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "attention smem attribute");
+    attr = true;
+  }
+  const int64_t blocks = (int64_t)B * Hq * (S / 128);
+  attention_tc_kernel<<<(unsigned)blocks, THREADS, smem, ctx->stream>>>(mq, mk, mv, p);
+  launched(ctx, "attention_tc");
+  return true;
+}
+
+}  // namespace fopt

@@ -382,17 +382,20 @@ def test_gather_rejects_negative_index(b200):
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("S,Hq,Hkv,causal", [(128, 4, 2, True), (200, 8, 2, True), (96, 2, 2, False)])
-def test_attention_parity(b200, S, Hq, Hkv, causal):
+@pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 4, 2, True), (1, 200, 8, 2, True), (1, 96, 2, 2, False),
+                                               (1, 512, 8, 2, True), (2, 384, 4, 1, True), (2, 256, 4, 4, False)])
+def test_attention_parity(b200, B, S, Hq, Hkv, causal):
+    """S % 128 == 0 runs the tcgen05 kernel (multi-block online softmax, GQA, batches); other S the
+    CUDA-core kernel."""
     D = 128
-    q = rand_vals("bf16", S * Hq * D)
-    k = rand_vals("bf16", S * Hkv * D)
-    v = rand_vals("bf16", S * Hkv * D)
-    mq = fb.Mapping("[S, H, D]", dict(S=S, H=Hq, D=D))
-    mk = fb.Mapping("[S, H, D]", dict(S=S, H=Hkv, D=D))
-    o = b200.attention(b200.from_vec(mq, q, "bf16"), b200.from_vec(mk, k, "bf16"), b200.from_vec(mk, v, "bf16"), 1, S,
+    q = rand_vals("bf16", B * S * Hq * D)
+    k = rand_vals("bf16", B * S * Hkv * D)
+    v = rand_vals("bf16", B * S * Hkv * D)
+    mq = fb.Mapping("[B, S, H, D]", dict(B=B, S=S, H=Hq, D=D))
+    mk = fb.Mapping("[B, S, H, D]", dict(B=B, S=S, H=Hkv, D=D))
+    o = b200.attention(b200.from_vec(mq, q, "bf16"), b200.from_vec(mk, k, "bf16"), b200.from_vec(mk, v, "bf16"), B, S,
                        Hq, Hkv, D, causal=causal).to_numpy()
-    want = oracle.attention(q, k, v, 1, S, Hq, Hkv, D, D ** -0.5, causal)
+    want = oracle.attention(q, k, v, B, S, Hq, Hkv, D, D ** -0.5, causal)
     g, w = dtypes.bf16_bits_to_f32(o), dtypes.bf16_bits_to_f32(want)
     err = np.abs(g - w)
     # bf16 output: 2 bf16 ulps of the value plus 1e-2 absolute (f32 softmax, different sum order)
