@@ -131,6 +131,18 @@ struct Params {
   int* err;
 };
 
+// 2^x on the special-function unit (relative error ~2^-22; the scores' bf16 rounding dominates).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// Two f32 -> packed bf16x2 with one round-to-nearest-even conversion instruction.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
 // Packs two f32 into bf16x2 with RNE (finite values; the softmax produces no NaN for finite inputs).
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t a = f32_to_bf16w(__float_as_uint(lo)), b = f32_to_bf16w(__float_as_uint(hi));
@@ -268,25 +280,30 @@ __global__ void __launch_bounds__(THREADS, 1)
       tld_wait();
       fence_before();
       mbar_arrive(smem_u32(&s_free[buf]));
-      // scores in log2 units, causal mask on the diagonal block
+      // row max of the raw scores; the causal mask only touches the diagonal block (a CTA-uniform branch)
       const bool diag = p.causal && j == qb;
       float mx = -INFINITY;
+      if (diag) {
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        float v = __uint_as_float(s[c]) * p.scale_log2;
-        if (diag && c > r) v = -INFINITY;
-        s[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int c = 0; c < 128; ++c) {
+          if (c > r) s[c] = __float_as_uint(-INFINITY);
+          mx = fmaxf(mx, __uint_as_float(s[c]));
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
       }
-      const float mnew = fmaxf(m, mx);
-      const float alpha = exp2f(m - mnew);  // m = -inf on the first block -> alpha = 0
+      // p = 2^(s * scale*log2(e) - m), the running max m kept in scaled log2 units
+      const float mnew = fmaxf(m, mx * p.scale_log2);
+      const float alpha = ex2(m - mnew);  // m = -inf on the first block -> alpha = 0
       float sum = 0.0f;
       uint32_t* pk = s;  // packed bf16 pairs overwrite the scores in place (index c / 2 <= c)
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float p0 = exp2f(__uint_as_float(s[c]) - mnew), p1 = exp2f(__uint_as_float(s[c + 1]) - mnew);
+        const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -mnew));
+        const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -mnew));
         sum += p0 + p1;
-        pk[c / 2] = pack_bf16(p0, p1);
+        pk[c / 2] = pack_bf16x2(p0, p1);
       }
       l = l * alpha + sum;
       m = mnew;
