@@ -99,15 +99,21 @@ __global__ void relayout_bcast(uint4* __restrict__ dst, const T* __restrict__ sr
 // 0 = src offset, memory 1 = dst position. A (32 V) x (32 V) tile moves through shared memory; each
 // thread reads V consecutive src elements (a 4-byte word for 1- and 2-byte types) and writes V
 // consecutive dst elements, so both global sides move whole 128-byte lines per warp.
-template <typename T, int V>
+template <typename T, int V, int TT>
 __global__ void __launch_bounds__(256) relayout_tile(T* __restrict__ dst, const T* __restrict__ src, KWalk others,
                                                      int64_t e0, int64_t s0, int64_t ej, int64_t wj, int64_t src_base,
                                                      int64_t dst_base, int64_t nt0, int64_t ntj, int64_t batches) {
-  constexpr int TT = 32 * V;
-  using W = typename std::conditional<V == 4, uint32_t, typename std::conditional<V == 2, uint32_t, T>::type>::type;
-  static_assert(sizeof(T) * V == sizeof(W), "vector width");
-  __shared__ T tile[TT][TT + 2 / sizeof(T) + (sizeof(T) == 4 ? 1 : 0)];
-  const int tx = threadIdx.x, ty = threadIdx.y;
+  // TT x TT tile; a warp covers TT / V columns... each thread moves V-element vectors along both
+  // the read side (src-contiguous) and the write side (dst-contiguous)
+  constexpr int VB = sizeof(T) * V;
+  using W = typename std::conditional<VB == 16, uint4, typename std::conditional<VB == 8, uint2,
+            typename std::conditional<VB == 4, uint32_t, typename std::conditional<VB == 2, uint16_t, uint8_t>::type>::type>::type>::type;
+  constexpr int LANES = TT / V;            // threads across one tile row
+  constexpr int ROWS = 256 / LANES;        // tile rows per pass
+  constexpr int PAD = 1;  // odd row stride: the V-row column gather spreads over the banks
+  __shared__ T tile[TT][TT + PAD];
+  const int tid = threadIdx.x;
+  const int tx = tid % LANES, ty = tid / LANES;
   for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
     int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
     int64_t off[2] = {0, 0};
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(256) relayout_tile(T* __restrict__ dst, const 
     if (live) {
       const int64_t dj = tj * TT + tx * V;
 #pragma unroll 4
-      for (int r = ty; r < TT; r += 8) {
+      for (int r = ty; r < TT; r += ROWS) {
         int64_t d0 = ti * TT + r;
         if (d0 < e0 && dj < ej) {
           W w = *(const W*)(src + src_base + off[0] + d0 * s0 + dj);
@@ -128,7 +134,7 @@ __global__ void __launch_bounds__(256) relayout_tile(T* __restrict__ dst, const 
     if (live) {
       const int64_t d0 = ti * TT + tx * V;
 #pragma unroll 4
-      for (int c = ty; c < TT; c += 8) {
+      for (int c = ty; c < TT; c += ROWS) {
         int64_t dj = tj * TT + c;
         if (d0 < e0 && dj < ej) {
           W w;
@@ -163,6 +169,22 @@ __global__ void relayout_walk64(T* __restrict__ dst, const T* __restrict__ src, 
     if (!walk_offsets<1>(w, q, &off)) continue;
     int64_t s = src_base + off;
     if (s < src_elems) dst[dst_base + q] = src[s];
+  }
+}
+
+// ---- rows path: a warp per row of the innermost wheel (partially live rows, e.g. padded widths) ----
+template <typename T>
+__global__ void relayout_rows(T* __restrict__ dst, const T* __restrict__ src, KWalk32 outer, uint32_t rows, uint32_t e0,
+                              uint32_t l0, int32_t st0, int64_t src_base, int64_t dst_base, int64_t src_elems) {
+  const uint32_t lane = threadIdx.x & 31, warps = (gridDim.x * blockDim.x) >> 5;
+  for (uint32_t row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += warps) {
+    int32_t off = 0;
+    if (!walk_offsets32<1>(outer, row, &off)) continue;
+    const int64_t sb = src_base + off, db = dst_base + (int64_t)row * e0;
+    for (uint32_t d = lane; d < l0; d += 32) {
+      const int64_t si = sb + (int64_t)d * st0;
+      if (si < src_elems) dst[db + d] = src[si];
+    }
   }
 }
 
@@ -284,25 +306,43 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
     }
     int64_t batches = 1;
     for (int k = 0; k < others.n; ++k) batches *= others.extent[k];
-    // Vector width: whole 4-byte words per thread when every offset stays word-aligned.
-    constexpr int VW = sizeof(T) >= 4 ? 1 : 4 / (int)sizeof(T);
-    bool wide = VW > 1 && w.extent[0] % VW == 0 && w.extent[j] % VW == 0 && w.stride[0][0] % VW == 0 &&
-                src_base % VW == 0 && dst_base % VW == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0;
+    // Vector width: 8-byte vectors per thread when every offset stays aligned to them; a 128 x 128
+    // tile for 1- and 2-byte elements, 64 x 64 for 4-byte ones (shared memory stays <= 32 KiB).
+    constexpr int VW = sizeof(T) >= 4 ? 2 : 8 / (int)sizeof(T);
+    bool wide = w.extent[0] % VW == 0 && w.extent[j] % VW == 0 && w.stride[0][0] % VW == 0 && src_base % VW == 0 &&
+                dst_base % VW == 0 && (uintptr_t)src % 8 == 0 && (uintptr_t)dst % 8 == 0;
     for (int k = 0; wide && k < others.n; ++k) wide = others.stride[0][k] % VW == 0;
-    const int TT = wide ? 32 * VW : 32;
+    constexpr int TTW = sizeof(T) >= 4 ? 64 : 128;
+    const int TT = wide ? TTW : 32;
     int64_t nt0 = (w.extent[0] + TT - 1) / TT, ntj = (w.extent[j] + TT - 1) / TT;
     int64_t blocks = nt0 * ntj * batches;
-    int grid = (int)std::min<int64_t>(blocks, 148 * 16);
+    int grid = (int)std::min<int64_t>(blocks, (1ll << 31) - 1);  // one tile per block
     if (wide)
-      relayout_tile<T, VW><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
-                                                         src_base, dst_base, nt0, ntj, batches);
+      relayout_tile<T, VW, TTW><<<grid, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                       src_base, dst_base, nt0, ntj, batches);
     else
-      relayout_tile<T, 1><<<grid, dim3(32, 8), 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
-                                                        src_base, dst_base, nt0, ntj, batches);
+      relayout_tile<T, 1, 32><<<grid, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                     src_base, dst_base, nt0, ntj, batches);
     launched(ctx, "relayout_tile");
     return;
   }
   KWalk32 w32;
+  if (w.n >= 2 && w.extent[0] >= 16 && to_kwalk32(w, w32) && p.positions < (1ll << 31)) {
+    // rows path: the innermost wheel walked by a warp's lanes, the outer wheels decomposed once per row
+    KWalk32 outer{};
+    outer.n = w32.n - 1;
+    for (int i = 1; i < w32.n; ++i) {
+      outer.div[i - 1] = w32.div[i];
+      outer.live[i - 1] = w32.live[i];
+      outer.stride[0][i - 1] = w32.stride[0][i];
+    }
+    const int64_t rows = p.positions / w.extent[0];
+    relayout_rows<T><<<grid_for(rows * 32), kThreads, 0, st>>>(d, s, outer, (uint32_t)rows, (uint32_t)w.extent[0],
+                                                                 (uint32_t)w.live[0], (int32_t)w.stride[0][0],
+                                                                 src_base, dst_base, src_elems);
+    launched(ctx, "relayout_rows");
+    return;
+  }
   if (to_kwalk32(w, w32) && p.positions < (1ll << 31)) {
     relayout_walk32<T><<<grid_for(p.positions), kThreads, 0, st>>>(d, s, w32, (uint32_t)p.positions, src_base,
                                                                   dst_base, src_elems);
