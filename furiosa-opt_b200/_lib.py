@@ -66,6 +66,9 @@ SIGNATURES = [
     ("fopt_scatter", _I32, [_VP, _VP, _VP, _VP, C.c_int, _VP, _VP, _VP, _VP, _VP, C.c_int]),
     ("fopt_elementwise", _I32, [_VP, C.POINTER(Program), _I32, C.POINTER(_VP), C.POINTER(C.c_int), _VP, C.c_int,
                                 _I64]),
+    ("fopt_elementwise_source", _I32, [C.POINTER(Program), _I32, C.POINTER(C.c_int), C.c_int, C.c_char_p, _SZ,
+                                       C.POINTER(_SZ)]),
+    ("fopt_elementwise_jit_launches", C.c_int64, []),
     ("fopt_reduce", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_reduce_noalloc", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_contraction", _I32, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP, _VP, _VP, C.POINTER(Epilogue)]),

@@ -20,7 +20,8 @@ ROOT = os.path.dirname(HERE)
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include"),
+GEN = os.path.join(OBJ, "gen")
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include"), "-I", GEN,
           "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 
@@ -61,8 +62,21 @@ def _compile(src: str, verbose: bool) -> str:
     return obj
 
 
+def _generate():
+    """ew_ops.cuh as a C++ raw string literal: the prelude handed to NVRTC for generated kernels."""
+    os.makedirs(GEN, exist_ok=True)
+    with open(os.path.join(CSRC, "ew_ops.cuh")) as fh:
+        src = fh.read()
+    text = 'R"FOPTSRC(' + src + ')FOPTSRC"\n'
+    out = os.path.join(GEN, "ew_ops_src.inc")
+    if not os.path.exists(out) or open(out).read() != text:
+        with open(out, "w") as fh:
+            fh.write(text)
+
+
 def build(verbose: bool = False) -> str:
     os.makedirs(OBJ, exist_ok=True)
+    _generate()
     srcs = _sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))

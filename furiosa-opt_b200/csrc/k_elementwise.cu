@@ -9,131 +9,12 @@
 #include <algorithm>
 
 #include "ctx.hpp"
+#include "ew_ops.cuh"
 
 namespace fopt {
 namespace {
 
-__device__ __forceinline__ float F(uint32_t w) { return __uint_as_float(w); }
-__device__ __forceinline__ uint32_t W(float f) { return __float_as_uint(f); }
-
-__device__ __forceinline__ int32_t sat_add(int32_t a, int32_t b) {
-  int64_t s = (int64_t)a + b;
-  return (int32_t)max((int64_t)INT32_MIN, min((int64_t)INT32_MAX, s));
-}
-__device__ __forceinline__ int32_t sat_sub(int32_t a, int32_t b) {
-  int64_t s = (int64_t)a - b;
-  return (int32_t)max((int64_t)INT32_MIN, min((int64_t)INT32_MAX, s));
-}
-
-// f32 -> i32 `as` cast: truncation toward zero, saturating, NaN -> 0.
-__device__ __forceinline__ int32_t f2i_as(float x) {
-  if (x != x) return 0;
-  if (x >= 2147483648.0f) return INT32_MAX;
-  if (x <= -2147483904.0f) return INT32_MIN;
-  return (int32_t)x;
-}
-
-// f8 conversions are restated from the OCP 8-bit float definitions (E4M3: bias 7, no infinities,
-// 0x7f/0xff NaN, max 448; E5M2: bias 15, IEEE-like) with round-to-nearest-even on narrowing.
-__device__ __forceinline__ float f8_to_f32(uint32_t code, int ebits) {
-  int mbits = 7 - ebits, bias = (1 << (ebits - 1)) - 1;
-  uint32_t s = code >> 7, e = (code >> mbits) & ((1 << ebits) - 1), m = code & ((1 << mbits) - 1);
-  float v;
-  if (ebits == 4 && e == 15 && m == 7) return __uint_as_float(0x7fc00000u);
-  if (ebits == 5 && e == 31) return m ? __uint_as_float(0x7fc00000u) : (s ? -INFINITY : INFINITY);
-  if (e == 0) v = ldexpf((float)m, 1 - bias - mbits);
-  else v = ldexpf((float)((1 << mbits) | m), (int)e - bias - mbits);
-  return s ? -v : v;
-}
-__device__ __forceinline__ uint32_t f32_to_f8(float x, int ebits) {
-  int mbits = 7 - ebits, bias = (1 << (ebits - 1)) - 1;
-  uint32_t bits = __float_as_uint(x);
-  uint32_t s = (bits >> 31) << 7;
-  if (x != x) return ebits == 4 ? 0x7f : 0x7e;
-  float a = fabsf(x);
-  float maxv = ebits == 4 ? 448.0f : 57344.0f;
-  if (ebits == 5 && isinf(a)) return s | 0x7c;
-  // quantum at this magnitude
-  int e;
-  frexpf(a, &e);  // a = f * 2^e, f in [0.5, 1)
-  int ee = max(e - 1, 1 - bias);
-  float q = ldexpf(1.0f, ee - mbits);
-  float r = rintf(a / q) * q;  // RNE (division by a power of two is exact)
-  if (r > maxv) return ebits == 4 ? (s | 0x7e) /* saturate finite */ : (s | 0x7c);
-  if (r == 0.0f) return s;
-  int re;
-  frexpf(r, &re);
-  int be = re - 1 + bias;
-  uint32_t code;
-  if (be <= 0) code = (uint32_t)(r / ldexpf(1.0f, 1 - bias - mbits));
-  else code = ((uint32_t)be << mbits) | ((uint32_t)(r / ldexpf(1.0f, re - 1 - mbits)) & ((1u << mbits) - 1));
-  return s | code;
-}
-
-// The opcode table: X(code, expression over the operand words a, b, c and the immediate imm).
-// ia / ib are the signed views, fa / fb / fc the f32 views.
-#define FOPT_EW_OPS(X)                                                                                    \
-  X(FOPT_OP_MOV, a)                                                                                       \
-  X(FOPT_OP_BF16_TO_F32, bf16w_to_f32_bits(a & 0xffff0000u))                                              \
-  X(FOPT_OP_F32_TO_BF16, f32_to_bf16w(a))                                                                 \
-  X(FOPT_OP_F32_TO_BF16_RELU, (((a & 0x7fffffffu) <= 0x7f800000u) && (a >> 31)) ? 0u : f32_to_bf16w(a))   \
-  X(FOPT_OP_I32_TO_F32, W(__int2float_rn(ia)))                                                            \
-  X(FOPT_OP_F32_TO_I32, (uint32_t)f2i_as(fa))                                                             \
-  X(FOPT_OP_FXP_TO_FP, fxp_to_fp_bits(ia, (uint32_t)imm))                                                 \
-  X(FOPT_OP_FP_TO_FXP, (uint32_t)fp_to_fxp(fa, (uint32_t)imm))                                            \
-  X(FOPT_OP_F8E4M3_TO_F32, W(f8_to_f32(a & 0xff, 4)))                                                     \
-  X(FOPT_OP_F32_TO_F8E4M3, f32_to_f8(fa, 4))                                                              \
-  X(FOPT_OP_F8E5M2_TO_F32, W(f8_to_f32(a & 0xff, 5)))                                                     \
-  X(FOPT_OP_F32_TO_F8E5M2, f32_to_f8(fa, 5))                                                              \
-  X(FOPT_OP_I4_SEXT, (uint32_t)(((int32_t)(a << 28)) >> 28))                                              \
-  X(FOPT_OP_I5_SEXT, (uint32_t)(((int32_t)(a << 27)) >> 27))                                              \
-  X(FOPT_OP_I9_SEXT, (uint32_t)(((int32_t)(a << 23)) >> 23))                                              \
-  X(FOPT_OP_EXP, W(expf(fa)))                                                                             \
-  X(FOPT_OP_NEGEXP, W(expf(-fa)))                                                                         \
-  X(FOPT_OP_SQRT, W(__fsqrt_rn(fa)))                                                                      \
-  X(FOPT_OP_TANH, W(tanhf(fa)))                                                                           \
-  X(FOPT_OP_SIGMOID, W(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-fa)))))                                      \
-  X(FOPT_OP_LOG, W(logf(fa)))                                                                             \
-  X(FOPT_OP_SIN, W(sinf(fa)))                                                                             \
-  X(FOPT_OP_COS, W(cosf(fa)))                                                                             \
-  X(FOPT_OP_ADDF, W(__fadd_rn(fa, fb)))                                                                   \
-  X(FOPT_OP_SUBF, W(__fsub_rn(fa, fb)))                                                                   \
-  X(FOPT_OP_MULF, W(__fmul_rn(fa, fb)))                                                                   \
-  X(FOPT_OP_DIVF, W(__fdiv_rn(fa, fb)))                                                                   \
-  X(FOPT_OP_FMAF, W(__fmaf_rn(fa, fb, fc)))                                                               \
-  X(FOPT_OP_MINF, W(fminf(fa, fb)))                                                                       \
-  X(FOPT_OP_MAXF, W(fmaxf(fa, fb)))                                                                       \
-  X(FOPT_OP_ABSMINF, fabsf(fa) < fabsf(fb) ? a : b)                                                       \
-  X(FOPT_OP_ABSMAXF, fabsf(fa) > fabsf(fb) ? a : b)                                                       \
-  X(FOPT_OP_ADD_FXP, a + b)                                                                               \
-  X(FOPT_OP_ADD_FXP_SAT, (uint32_t)sat_add(ia, ib))                                                       \
-  X(FOPT_OP_SUB_FXP, a - b)                                                                               \
-  X(FOPT_OP_SUB_FXP_SAT, (uint32_t)sat_sub(ia, ib))                                                       \
-  X(FOPT_OP_SHL, a << (b & 31))                                                                           \
-  X(FOPT_OP_SHL_SAT, shl_sat(ia, b))                                                                      \
-  X(FOPT_OP_MUL_FXP, mul_fxp(ia, ib))                                                                     \
-  X(FOPT_OP_MUL_INT, a * b)                                                                               \
-  X(FOPT_OP_SHR_LOGIC, a >> (b & 31))                                                                     \
-  X(FOPT_OP_SHR_ARITH, (uint32_t)(ia >> (b & 31)))                                                        \
-  X(FOPT_OP_MINI, (uint32_t)min(ia, ib))                                                                  \
-  X(FOPT_OP_MAXI, (uint32_t)max(ia, ib))                                                                  \
-  X(FOPT_OP_ABSMINI, (abs(ia) < abs(ib)) ? a : b)                                                         \
-  X(FOPT_OP_ABSMAXI, (abs(ia) > abs(ib)) ? a : b)                                                         \
-  X(FOPT_OP_AND, a & b)                                                                                   \
-  X(FOPT_OP_OR, a | b)                                                                                    \
-  X(FOPT_OP_XOR, a ^ b)                                                                                   \
-  X(FOPT_OP_SELECT, a ? b : c)                                                                            \
-  X(FOPT_OP_CONST, (uint32_t)imm)
-
-__device__ __forceinline__ uint32_t shl_sat(int32_t ia, uint32_t b) {
-  int64_t m = (int64_t)(int32_t)(1u << (b & 31));
-  int64_t pr = (int64_t)ia * m;
-  return (uint32_t)(int32_t)max((int64_t)INT32_MIN, min((int64_t)INT32_MAX, pr));
-}
-__device__ __forceinline__ uint32_t mul_fxp(int32_t ia, int32_t ib) {
-  if (ia == INT32_MIN && ib == INT32_MIN) return (uint32_t)INT32_MAX;
-  return (uint32_t)(int32_t)((((int64_t)ia * ib) >> 30) + 1 >> 1);
-}
+using namespace ew;
 
 // One opcode applied to EPT independent elements (the switch is uniform across the warp and is
 // taken once per EPT elements).
@@ -412,6 +293,7 @@ void launch_elementwise(fopt_ctx* ctx, const fopt_program* prog, int n_in, const
   a.out_dt = out_dt;
   a.n = n;
   a.vec = vec;
+  if (launch_elementwise_jit(ctx, prog, n_in, in, in_dt, out, out_dt, n)) return;
   fopt_program q = rename_registers(*prog, n_in);
   if (dtype_bits(out_dt) == 4) {
     int64_t bytes = (n + 1) / 2;

@@ -1,0 +1,312 @@
+// Elementwise programs compiled to their own kernels at run time (NVRTC -> sm_100a cubin).
+//
+// The interpreter in k_elementwise.cu dispatches every opcode through switches; a generated kernel
+// instead has the program's expressions inlined with every value in a real register, dtype-specific
+// 16-byte loads and stores, and 8 elements per thread, so a map / zip / zip3 runs at memory speed.
+// The expressions come from the same FOPT_EW_OPS table (stringified) that the interpreter expands,
+// and the same device helpers (ew_ops.cuh, handed to NVRTC verbatim), so both paths compute the
+// identical bit patterns. Kernels are cached per (program, dtypes, device). When NVRTC or the driver
+// entry points are unavailable, or FOPT_EW_NO_JIT is set, the interpreter runs instead.
+#include <cuda.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+
+#include <atomic>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <cstring>
+#include <string>
+
+#include "ctx.hpp"
+#include "ew_ops.cuh"
+
+namespace fopt {
+namespace {
+
+const char* kPrelude =
+#include "ew_ops_src.inc"
+    ;
+
+struct OpText {
+  int code;
+  const char* expr;
+};
+const OpText kOps[] = {
+#define FOPT_EW_TEXT(code, expr) {code, #expr},
+    FOPT_EW_OPS(FOPT_EW_TEXT)
+#undef FOPT_EW_TEXT
+};
+
+const char* op_expr(int op) {
+  for (const auto& o : kOps)
+    if (o.code == op) return o.expr;
+  return nullptr;
+}
+
+struct Jit {
+  bool ok = false;
+  nvrtcResult (*create)(nvrtcProgram*, const char*, const char*, int, const char* const*, const char* const*) = nullptr;
+  nvrtcResult (*compile)(nvrtcProgram, int, const char* const*) = nullptr;
+  nvrtcResult (*cubin_size)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*cubin)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*log_size)(nvrtcProgram, size_t*) = nullptr;
+  nvrtcResult (*log)(nvrtcProgram, char*) = nullptr;
+  nvrtcResult (*destroy)(nvrtcProgram*) = nullptr;
+  CUresult (*load)(CUmodule*, const void*) = nullptr;
+  CUresult (*get_fn)(CUfunction*, CUmodule, const char*) = nullptr;
+  CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
+                     void**, void**) = nullptr;
+};
+
+template <typename T>
+bool driver_sym(const char* name, T* out) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return false;
+  *out = (T)p;
+  return true;
+}
+
+Jit& jit() {
+  static Jit j;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = nullptr;
+    for (const char* n : {"libnvrtc.so.12", "libnvrtc.so"})
+      if ((h = dlopen(n, RTLD_NOW | RTLD_LOCAL))) break;
+    if (!h) return;
+#define SYM(f, s) j.f = (decltype(j.f))dlsym(h, s)
+    SYM(create, "nvrtcCreateProgram");
+    SYM(compile, "nvrtcCompileProgram");
+    SYM(cubin_size, "nvrtcGetCUBINSize");
+    SYM(cubin, "nvrtcGetCUBIN");
+    SYM(log_size, "nvrtcGetProgramLogSize");
+    SYM(log, "nvrtcGetProgramLog");
+    SYM(destroy, "nvrtcDestroyProgram");
+#undef SYM
+    bool drv = driver_sym("cuModuleLoadData", &j.load) && driver_sym("cuModuleGetFunction", &j.get_fn) &&
+               driver_sym("cuLaunchKernel", &j.launch);
+    j.ok = drv && j.create && j.compile && j.cubin_size && j.cubin && j.destroy;
+  });
+  return j;
+}
+
+// ---- code generation ----
+std::string load_vec(int k, int dt) {
+  std::ostringstream o;
+  const std::string in = "in" + std::to_string(k), x = "x" + std::to_string(k);
+  switch (dtype_bits(dt)) {
+    case 32:
+      o << "{ const uint4* q = (const uint4*)" << in << " + (base >> 2); uint4 u0 = q[0], u1 = q[1]; " << x
+        << "[0]=u0.x; " << x << "[1]=u0.y; " << x << "[2]=u0.z; " << x << "[3]=u0.w; " << x << "[4]=u1.x; " << x
+        << "[5]=u1.y; " << x << "[6]=u1.z; " << x << "[7]=u1.w; }\n";
+      break;
+    case 16:
+      o << "{ uint4 u = *((const uint4*)" << in << " + (base >> 3)); const unsigned h[4] = {u.x, u.y, u.z, u.w};\n"
+        << "  for (int j = 0; j < 4; ++j) { ";
+      if (dt == FOPT_BF16)
+        o << x << "[2*j] = h[j] << 16; " << x << "[2*j+1] = h[j] & 0xffff0000u; }";
+      else
+        o << x << "[2*j] = (unsigned)(int)(short)(h[j] & 0xffffu); " << x << "[2*j+1] = (unsigned)((int)h[j] >> 16); }";
+      o << " }\n";
+      break;
+    default: {
+      const bool sgn = dt == FOPT_I8 || dt == FOPT_I5;
+      o << "{ uint2 u = *((const uint2*)" << in << " + (base >> 3)); const unsigned h[2] = {u.x, u.y};\n"
+        << "  for (int j = 0; j < 8; ++j) { unsigned b = (h[j >> 2] >> (8 * (j & 3))) & 0xffu; " << x << "[j] = "
+        << (sgn ? "(unsigned)(int)(signed char)b" : "b") << "; } }\n";
+    }
+  }
+  return o.str();
+}
+
+std::string load_one(int k, int dt, const std::string& i) {
+  const std::string in = "in" + std::to_string(k);
+  switch (dt) {
+    case FOPT_I32: case FOPT_F32: return "((const unsigned*)" + in + ")[" + i + "]";
+    case FOPT_BF16: return "(((unsigned)((const unsigned short*)" + in + ")[" + i + "]) << 16)";
+    case FOPT_I16: case FOPT_I9: return "((unsigned)(int)((const short*)" + in + ")[" + i + "])";
+    case FOPT_I8: case FOPT_I5: return "((unsigned)(int)((const signed char*)" + in + ")[" + i + "])";
+    default: return "((unsigned)((const unsigned char*)" + in + ")[" + i + "])";
+  }
+}
+
+std::string store_vec(int dt) {
+  switch (dtype_bits(dt)) {
+    case 32:
+      return "{ uint4* q = (uint4*)out + (base >> 2); q[0] = make_uint4(r[0], r[1], r[2], r[3]); "
+             "q[1] = make_uint4(r[4], r[5], r[6], r[7]); }\n";
+    case 16:
+      if (dt == FOPT_BF16)
+        return "{ *((uint4*)out + (base >> 3)) = make_uint4((r[0] >> 16) | (r[1] & 0xffff0000u), (r[2] >> 16) | "
+               "(r[3] & 0xffff0000u), (r[4] >> 16) | (r[5] & 0xffff0000u), (r[6] >> 16) | (r[7] & 0xffff0000u)); }\n";
+      return "{ *((uint4*)out + (base >> 3)) = make_uint4((r[0] & 0xffffu) | (r[1] << 16), (r[2] & 0xffffu) | "
+             "(r[3] << 16), (r[4] & 0xffffu) | (r[5] << 16), (r[6] & 0xffffu) | (r[7] << 16)); }\n";
+    default:
+      return "{ unsigned h0 = 0, h1 = 0; for (int j = 0; j < 4; ++j) { h0 |= (r[j] & 0xffu) << (8 * j); "
+             "h1 |= (r[j + 4] & 0xffu) << (8 * j); } *((uint2*)out + (base >> 3)) = make_uint2(h0, h1); }\n";
+  }
+}
+
+std::string store_one(int dt, const std::string& i, const std::string& v) {
+  switch (dtype_bits(dt)) {
+    case 32: return "((unsigned*)out)[" + i + "] = " + v + ";";
+    case 16:
+      return "((unsigned short*)out)[" + i + "] = (unsigned short)(" + (dt == FOPT_BF16 ? v + " >> 16" : v) + ");";
+    default: return "((unsigned char*)out)[" + i + "] = (unsigned char)(" + v + ");";
+  }
+}
+
+int arity_of(int op) {
+  switch (op) {
+    case FOPT_OP_CONST: return 0;
+    case FOPT_OP_FMAF: case FOPT_OP_SELECT: return 3;
+    default: break;
+  }
+  switch (op) {
+    case FOPT_OP_ADDF: case FOPT_OP_SUBF: case FOPT_OP_MULF: case FOPT_OP_DIVF: case FOPT_OP_MINF: case FOPT_OP_MAXF:
+    case FOPT_OP_ABSMINF: case FOPT_OP_ABSMAXF: case FOPT_OP_ADD_FXP: case FOPT_OP_ADD_FXP_SAT: case FOPT_OP_SUB_FXP:
+    case FOPT_OP_SUB_FXP_SAT: case FOPT_OP_SHL: case FOPT_OP_SHL_SAT: case FOPT_OP_MUL_FXP: case FOPT_OP_MUL_INT:
+    case FOPT_OP_SHR_LOGIC: case FOPT_OP_SHR_ARITH: case FOPT_OP_MINI: case FOPT_OP_MAXI: case FOPT_OP_ABSMINI:
+    case FOPT_OP_ABSMAXI: case FOPT_OP_AND: case FOPT_OP_OR: case FOPT_OP_XOR: return 2;
+    default: return 1;
+  }
+}
+
+}  // namespace
+// Returns "" when the program uses an opcode the table lacks (the interpreter then runs it).
+std::string generate(const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt) {
+  std::ostringstream o;
+  o << kPrelude << "\nusing namespace fopt::ew;\n"
+    << "extern \"C\" __global__ void __launch_bounds__(256) fopt_ew_gen(const void* __restrict__ in0, "
+       "const void* __restrict__ in1, const void* __restrict__ in2, void* __restrict__ out, long long n) {\n"
+    << "  const long long stride = (long long)gridDim.x * blockDim.x * 8;\n"
+    << "  for (long long base = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8; base < n; base += stride) {\n"
+    << "    unsigned x0[8], x1[8], x2[8], r[8];\n"
+    << "    const bool full = base + 8 <= n;\n"
+    << "    if (full) {\n";
+  for (int k = 0; k < n_in; ++k) o << "      " << load_vec(k, in_dt[k]);
+  o << "    } else {\n";
+  for (int k = 0; k < n_in; ++k)
+    o << "      for (int e = 0; e < 8; ++e) x" << k << "[e] = base + e < n ? " << load_one(k, in_dt[k], "base + e")
+      << " : 0u;\n";
+  o << "    }\n#pragma unroll\n    for (int e = 0; e < 8; ++e) {\n";
+  std::string name[16];
+  for (int v = 0; v < 16; ++v) name[v] = "0u";
+  for (int k = 0; k < n_in; ++k) name[k] = "x" + std::to_string(k) + "[e]";
+  for (int i = 0; i < p.n_insn; ++i) {
+    const fopt_insn& in = p.insn[i];
+    const char* expr = op_expr(in.op);
+    if (!expr) return "";
+    const int ar = arity_of(in.op);
+    const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
+                      C = ar > 2 ? name[in.c & 15] : "0u";
+    const std::string t = "t" + std::to_string(i);
+    o << "      unsigned " << t << "; { const unsigned a = " << A << ", b = " << B << ", c = " << C
+      << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
+      << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << " = ("
+      << expr << "); }\n";
+    name[in.dst & 15] = t;
+  }
+  o << "      r[e] = " << name[p.ret & 15] << ";\n    }\n"
+    << "    if (full) " << store_vec(out_dt) << "    else for (int e = 0; e < 8; ++e) if (base + e < n) "
+    << store_one(out_dt, "base + e", "r[e]") << "\n  }\n}\n";
+  return o.str();
+}
+
+namespace {
+struct Entry {
+  CUfunction fn = nullptr;
+  bool failed = false;
+};
+std::mutex g_mu;
+std::map<std::string, Entry> g_cache;
+
+CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt) {
+  Jit& j = jit();
+  if (!j.ok) return nullptr;
+  std::string key((const char*)&p, sizeof(int32_t) * 2 + sizeof(fopt_insn) * p.n_insn);
+  key += std::to_string(ctx->device) + ":" + std::to_string(out_dt);
+  for (int k = 0; k < n_in; ++k) key += "," + std::to_string(in_dt[k]);
+  std::lock_guard<std::mutex> g(g_mu);
+  auto it = g_cache.find(key);
+  if (it != g_cache.end()) return it->second.failed ? nullptr : it->second.fn;
+  Entry& e = g_cache[key];
+  e.failed = true;
+  std::string src = generate(p, n_in, in_dt, out_dt);
+  if (src.empty()) return nullptr;
+  nvrtcProgram prog;
+  if (j.create(&prog, src.c_str(), "fopt_ew_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return nullptr;
+  const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "--fmad=false"};
+  nvrtcResult rc = j.compile(prog, 3, opts);
+  if (rc != NVRTC_SUCCESS) {
+    if (getenv("FOPT_EW_JIT_LOG") && j.log_size && j.log) {
+      size_t n = 0;
+      j.log_size(prog, &n);
+      std::string logs(n, '\0');
+      j.log(prog, &logs[0]);
+      fprintf(stderr, "fopt elementwise JIT failed:\n%s\n", logs.c_str());
+    }
+    j.destroy(&prog);
+    return nullptr;
+  }
+  size_t n = 0;
+  j.cubin_size(prog, &n);
+  std::string bin(n, '\0');
+  j.cubin(prog, &bin[0]);
+  j.destroy(&prog);
+  CUmodule mod;
+  if (j.load(&mod, bin.data()) != CUDA_SUCCESS) return nullptr;
+  CUfunction fn;
+  if (j.get_fn(&fn, mod, "fopt_ew_gen") != CUDA_SUCCESS) return nullptr;
+  e.fn = fn;
+  e.failed = false;
+  return fn;
+}
+
+}  // namespace
+
+std::atomic<int64_t> g_jit_launches{0};
+
+// Runs the program as a generated kernel; false when that path does not apply.
+bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
+                            const fopt_dtype* in_dt, void* out, fopt_dtype out_dt, int64_t n) {
+  if (getenv("FOPT_EW_NO_JIT")) return false;
+  if (dtype_bits(out_dt) < 8 || (uintptr_t)out % 16) return false;
+  for (int k = 0; k < n_in; ++k)
+    if (dtype_bits(in_dt[k]) < 8 || (uintptr_t)in[k] % 16) return false;
+  CUfunction fn = kernel_for(ctx, *prog, n_in, in_dt, out_dt);
+  if (!fn) return false;
+  const void* a0 = n_in > 0 ? in[0] : out;
+  const void* a1 = n_in > 1 ? in[1] : a0;
+  const void* a2 = n_in > 2 ? in[2] : a0;
+  long long nn = n;
+  void* args[] = {(void*)&a0, (void*)&a1, (void*)&a2, (void*)&out, (void*)&nn};
+  const int64_t threads = (n + 7) / 8;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((threads + 255) / 256, 148 * 16));
+  CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, args, nullptr);
+  if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "elementwise kernel launch failed"};
+  ctx->launches++;
+  g_jit_launches.fetch_add(1, std::memory_order_relaxed);
+  return true;
+}
+
+}  // namespace fopt
+
+extern "C" int64_t fopt_elementwise_jit_launches(void) { return fopt::g_jit_launches.load(); }
+
+extern "C" fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
+                                               fopt_dtype out_dtype, char* buf, size_t len, size_t* needed) {
+  if (!prog || n_in < 0 || n_in > 3) return FOPT_ERR_INVALID;
+  std::string src = fopt::generate(*prog, n_in, in_dtypes, out_dtype);
+  if (src.empty()) return FOPT_ERR_UNSUPPORTED;
+  if (needed) *needed = src.size() + 1;
+  if (buf && len) {
+    size_t n = std::min(len - 1, src.size());
+    memcpy(buf, src.data(), n);
+    buf[n] = 0;
+  }
+  return FOPT_OK;
+}

@@ -172,6 +172,12 @@ typedef struct {
 
 fopt_status fopt_elementwise(fopt_ctx* ctx, const fopt_program* prog, int32_t n_in, const void* const* inputs,
                              const fopt_dtype* in_dtypes, void* out, fopt_dtype out_dtype, int64_t n);
+/* Diagnostic: the CUDA source of the kernel fopt_elementwise generates (NVRTC, sm_100a) for this
+ * program and these dtypes (byte-multiple types). *needed = bytes including the terminator. */
+fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
+                                    fopt_dtype out_dtype, char* buf, size_t len, size_t* needed);
+/* Diagnostic: how many fopt_elementwise calls (process-wide) ran as a generated kernel. */
+int64_t fopt_elementwise_jit_launches(void);
 
 /* ---- reduce (BufStorage::reduce, buf.rs:331-376; Backend::reduce, backend/mod.rs:128-133) ----
  * Per output cell of dst_map, fold the src cells sharing its kept coordinates, starting from

@@ -9,7 +9,7 @@ import pytest
 
 import furiosa_opt_b200 as fb
 import oracle
-from furiosa_opt_b200 import dtypes, ops
+from furiosa_opt_b200 import _lib, dtypes, ops
 from oracle import ref_m
 
 pytestmark = pytest.mark.gpu
@@ -196,10 +196,28 @@ EXACT = [
 ]
 
 
+@pytest.fixture(params=["generated", "interpreter"])
+def ew_path(request, monkeypatch):
+    """Runs an elementwise test through the NVRTC-generated kernel and through the interpreter."""
+    if request.param == "interpreter":
+        monkeypatch.setenv("FOPT_EW_NO_JIT", "1")
+    else:
+        monkeypatch.delenv("FOPT_EW_NO_JIT", raising=False)
+    return request.param
+
+
+def _check_path(path, before, in_dtypes, out_dtype):
+    n = _lib.lib().fopt_elementwise_jit_launches() - before
+    packed = "i4" in in_dtypes or out_dtype == "i4"
+    assert n == (1 if path == "generated" and not packed else 0)
+
+
 @pytest.mark.parametrize("case", range(len(EXACT)))
-def test_elementwise_exact(b200, case):
+def test_elementwise_exact(b200, ew_path, case):
     prog, ins, out_dt = EXACT[case]
+    before = _lib.lib().fopt_elementwise_jit_launches()
     got, want = _ew_case(b200, prog, ins, out_dt)
+    _check_path(ew_path, before, ins, out_dt)
     if out_dt in ("f32", "bf16"):
         g = np.frombuffer(got, np.uint32 if out_dt == "f32" else np.uint16)
         w = np.frombuffer(want, np.uint32 if out_dt == "f32" else np.uint16)
@@ -212,10 +230,29 @@ def test_elementwise_exact(b200, case):
         assert got == want
 
 
+@pytest.mark.parametrize("n", [1, 7, 8, 9, 4096 * 37 + 3])
+@pytest.mark.parametrize("case", [0, 1, 3, 4])
+def test_elementwise_sizes(b200, ew_path, case, n):
+    """Tails shorter than one 8-element group and grid-stride sizes, in both elementwise paths."""
+    prog, ins, out_dt = EXACT[case]
+    got, want = _ew_case(b200, prog, ins, out_dt, n=n)
+    if out_dt == "f32":
+        g, w = np.frombuffer(got, np.float32), np.frombuffer(want, np.float32)
+        ok = (g.view(np.uint32) == w.view(np.uint32)) | (np.isnan(g) & np.isnan(w))
+        assert ok.all()
+    elif out_dt == "bf16":
+        g, w = dtypes.bf16_bits_to_f32(np.frombuffer(got, np.uint16)), dtypes.bf16_bits_to_f32(np.frombuffer(want, np.uint16))
+        assert ((np.frombuffer(got, np.uint16) == np.frombuffer(want, np.uint16)) | (np.isnan(g) & np.isnan(w))).all()
+    else:
+        assert got == want
+
+
 @pytest.mark.parametrize("name", ["Exp", "NegExp", "Tanh", "Sigmoid", "Log", "Sin", "Cos"])
-def test_elementwise_transcendental(b200, name):
+def test_elementwise_transcendental(b200, ew_path, name):
     # libm vs CUDA: within 2 ulp-ish relative (1e-6) / 1e-6 absolute
+    before = _lib.lib().fopt_elementwise_jit_launches()
     got, want = _ew_case(b200, ops.fp_unary(name), ["f32"], "f32")
+    _check_path(ew_path, before, ["f32"], "f32")
     g, w = np.frombuffer(got, np.float32), np.frombuffer(want, np.float32)
     fin = np.isfinite(w)
     assert np.array_equal(np.isnan(g), np.isnan(w))

@@ -131,3 +131,49 @@ def test_window_base():
     base = fb.Mapping("[A, B # 8]", A=4, B=6)
     assert base.window_base({"A": 2, "B": 3}) == 2 * 8 + 3
     assert base.window_base({}) == 0
+
+
+def _nvrtc():
+    import ctypes as C
+    for n in ("libnvrtc.so.12", "libnvrtc.so"):
+        try:
+            return C.CDLL(n)
+        except OSError:
+            continue
+    pytest.skip("NVRTC not available")
+
+
+@pytest.mark.parametrize("case", ["cast_bf16_f32", "requant", "swiglu", "quant", "zip3_select", "i16_shift"])
+def test_generated_elementwise_kernels_compile(case):
+    """The kernels fopt_elementwise generates compile for sm_100a (NVRTC runs without a GPU)."""
+    import ctypes as C
+    from furiosa_opt_b200 import ops, workloads as W
+    progs = {
+        "cast_bf16_f32": (ops.cast("bf16", "f32"), ["bf16"], "f32"),
+        "requant": (ops.requant_i32_to_i8(0.01, relu=True), ["i32"], "i8"),
+        "swiglu": (W._prog_swiglu(), ["bf16", "bf16"], "f32"),
+        "quant": (W._prog_quant(), ["f32", "f32"], "i8"),
+        "zip3_select": (ops.select(), ["i32", "f32", "f32"], "bf16"),
+        "i16_shift": (ops.fxp_binary("ArithRightShift"), ["i16", "i8"], "i16"),
+    }
+    prog, ins, out = progs[case]
+    lib = _lib.lib()
+    dts = (C.c_int * 3)(*[_lib.DTYPES[d] for d in ins])
+    need = C.c_size_t()
+    assert lib.fopt_elementwise_source(C.byref(prog), len(ins), dts, _lib.DTYPES[out], None, 0, C.byref(need)) == 0
+    buf = C.create_string_buffer(need.value)
+    assert lib.fopt_elementwise_source(C.byref(prog), len(ins), dts, _lib.DTYPES[out], buf, need.value, None) == 0
+    nv = _nvrtc()
+    prog_h = C.c_void_p()
+    assert nv.nvrtcCreateProgram(C.byref(prog_h), buf.value, b"t.cu", 0, None, None) == 0
+    opts = (C.c_char_p * 3)(b"--gpu-architecture=sm_100a", b"--std=c++17", b"--fmad=false")
+    rc = nv.nvrtcCompileProgram(prog_h, 3, opts)
+    if rc != 0:
+        n = C.c_size_t()
+        nv.nvrtcGetProgramLogSize(prog_h, C.byref(n))
+        log = C.create_string_buffer(n.value)
+        nv.nvrtcGetProgramLog(prog_h, log)
+        pytest.fail(log.value.decode()[-3000:])
+    size = C.c_size_t()
+    assert nv.nvrtcGetCUBINSize(prog_h, C.byref(size)) == 0 and size.value > 0
+    nv.nvrtcDestroyProgram(C.byref(prog_h))
