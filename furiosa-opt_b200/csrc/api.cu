@@ -151,6 +151,8 @@ fopt_status fopt_destroy(fopt_ctx* ctx) {
   for (auto& kv : ctx->relayouts)
     if (kv.second->table) cudaFree(kv.second->table);
   if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->gemm_ws) cudaFree(ctx->gemm_ws);
+  if (ctx->gemm_cnt) cudaFree(ctx->gemm_cnt);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   extern fopt_status fopt_comm_destroy(fopt_ctx*);
   fopt_comm_destroy(ctx);
@@ -167,6 +169,7 @@ static void check_device_error(fopt_ctx* ctx) {
   cuda_check(cudaMemcpy(&code, ctx->dev_err, sizeof(code), cudaMemcpyDeviceToHost), "error word read");
   if (code) {
     cuda_check(cudaMemset(ctx->dev_err, 0, sizeof(code)), "error word clear");
+    ctx->gemm_cnt_dirty = true;
     throw Fail{FOPT_ERR_TIMEOUT, "a kernel's bounded wait expired (code " + std::to_string(code) + ")"};
   }
 }

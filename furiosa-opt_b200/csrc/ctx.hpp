@@ -53,6 +53,11 @@ struct fopt_ctx {
   int32_t* dev_err = nullptr;  // device error word: bounded waits that expire write a code here
   void* scratch = nullptr;  // grow-only device scratch for kernels that need it
   size_t scratch_bytes = 0;
+  void* gemm_ws = nullptr;  // split-K partial accumulators of the paired GEMM's last wave
+  size_t gemm_ws_bytes = 0;
+  uint32_t* gemm_cnt = nullptr;  // arrival counters of the split tiles (zero between launches)
+  size_t gemm_cnt_n = 0;
+  bool gemm_cnt_dirty = false;
 };
 
 namespace fopt {

@@ -154,7 +154,10 @@ __device__ __forceinline__ uint32_t contract_cell(const CArgs& a, int64_t bl, in
     if (a.ep_kind == 1) {
       float y = F(fxp_to_fp_bits(acc, (uint32_t)a.int_width));
       const float sv = a.scale[sidx];
-      y = sv != sv ? sv : __fmul_rn(y, sv);  // keep a NaN scale's sign, as the x86 reference does
+      // x86 products (the reference's host) return a NaN operand unchanged and make 0 * inf the
+      // negative default NaN; the GPU would return a positive canonical NaN for both
+      y = __fmul_rn(y, sv);
+      if (y != y) y = sv != sv ? sv : __uint_as_float(0xffc00000u);
       int32_t q = fp_to_fxp(y, (uint32_t)a.int_width);
       q = max(a.clip_lo, min(a.clip_hi, q));
       return (uint32_t)q;

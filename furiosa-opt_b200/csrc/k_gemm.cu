@@ -19,7 +19,9 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "ctx.hpp"
 
@@ -129,6 +131,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+#define W32(i) "r"(r[i])
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      W32(0), W32(1), W32(2), W32(3), W32(4), W32(5), W32(6), W32(7), W32(8), W32(9), W32(10), W32(11), W32(12),
+      W32(13), W32(14), W32(15), W32(16), W32(17), W32(18), W32(19), W32(20), W32(21), W32(22), W32(23), W32(24),
+      W32(25), W32(26), W32(27), W32(28), W32(29), W32(30), W32(31)
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+#undef W32
 #undef R32
 
 struct Params {
@@ -141,26 +155,41 @@ struct Params {
   int int_width, clip_lo, clip_hi;
   const float* row_scale;
   int* err;
+  // split of the last wave (paired kernel): tiles [n_whole, ntiles) each run as `split` K-ranges;
+  // every range leaves its partial accumulator in ws, and the last range to finish adds them up
+  // and runs the epilogue (cnt: one arrival counter per split tile, CTA and epilogue warp)
+  int n_whole, split;
+  uint32_t* ws;
+  uint32_t* cnt;
+  int trace_units;
+  uint64_t* trace;  // diagnostics (FOPT_GEMM_TRACE): per unit {mma start, mma end, epilogue start, end,
+                    // first chunk loaded from TMEM (whole tiles) or SM id (split ranges)}
 };
 
-// (Requant of one accumulator (FxpToFp -> MulF -> FpToFxp -> Clip). For int_width 31,
-// fixedpoint_to_float is exactly IEEE round-to-nearest-even int -> f32 and float_to_fixedpoint is
-// round-half-away-from-zero then saturation, so both collapse to single instructions.
-__device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, float s) {
-  if (p.int_width == 31) {
-    float y = __fmul_rn(__int2float_rn(acc), s);
-    float r = roundf(y);
-    int32_t q;
-    if (r != r) q = (__float_as_uint(r) >> 31) ? INT32_MIN : INT32_MAX;
-    else if (r >= 2147483648.0f) q = INT32_MAX;
-    else if (r <= -2147483648.0f) q = INT32_MIN;
-    else q = (int32_t)r;
-    return max(p.clip_lo, min(p.clip_hi, q));
+// One unit of the paired kernel's persistent loop: a whole tile, or one K-range of a split tile.
+struct Unit {
+  int tile, kb0, kb1, part, sp;  // sp: index among the split tiles (-1 for a whole tile)
+};
+__device__ __forceinline__ Unit unit_of(const Params& p, int u, int kblocks) {
+  Unit w;
+  if (u < p.n_whole) {
+    w.tile = u; w.kb0 = 0; w.kb1 = kblocks; w.part = 0; w.sp = -1;
+  } else {
+    const int v = u - p.n_whole;
+    w.sp = v / p.split;
+    w.part = v - w.sp * p.split;
+    w.tile = p.n_whole + w.sp;
+    // K-range boundaries at (q * (S + q) ) / (2 S^2 ... ) are skewed so that range q ends before q + 1:
+    // the share of range q is proportional to (7 + 2 q), e.g. 7/16 : 9/16 for two ranges.
+    auto edge = [&](int q) {
+      const int64_t num = (int64_t)q * 7 + (int64_t)q * (q - 1);  // sum_{i<q} (7 + 2 i)
+      const int64_t den = (int64_t)p.split * 7 + (int64_t)p.split * (p.split - 1);
+      return (int)((int64_t)kblocks * num / den);
+    };
+    w.kb0 = edge(w.part);
+    w.kb1 = edge(w.part + 1);
   }
-  float y = __uint_as_float(fxp_to_fp_bits(acc, (uint32_t)p.int_width));
-  y = __fmul_rn(y, s);
-  int32_t q = fp_to_fxp(y, (uint32_t)p.int_width);
-  return max(p.clip_lo, min(p.clip_hi, q));
+  return w;
 }
 
 // Epilogue modes, one specialised kernel each so the epilogue code stays small:
@@ -172,31 +201,40 @@ __device__ __forceinline__ int32_t requant_one(const Params& p, int32_t acc, flo
 //   EP_DQ    dequant: f32(acc) * row_scale[m] * scale[n] -> bf16 (FxpToFp, two MulF, cast)
 enum { EP_I8 = 0, EP_WIDE = 1, EP_RQ31 = 2, EP_RQ = 3, EP_BF16 = 4, EP_DQ = 5 };
 
-// float_to_fixedpoint at int_width 31 is round-half-away-from-zero then saturation. With t = trunc(y)
-// and d = y - t (exact), rounding away from zero is needed exactly when |d| >= 0.5. Clip bounds that
-// are exact in f32 let the saturation and the Clip run in f32.
+// The requant chain FxpToFp -> MulF(s) -> FpToFxp -> Clip at int_width 31, for clip bounds exact in
+// f32 (float/mod.rs:22-34 for float_to_fixedpoint):
+//   * FxpToFp(31) is IEEE round-to-nearest int -> f32, and the product is one f32 multiply;
+//   * a NaN saturates by its sign, then clips. A NaN scale is the x86 product itself (the operand
+//     comes back unchanged) and is handled per column by the caller; the only other NaN is 0 * inf,
+//     whose x86 result is the negative default NaN, i.e. the low bound. fmaxf(NaN, lo) = lo gives
+//     exactly that, so clipping in f32 first also covers the saturation;
+//   * round half away from zero of the clipped value y is trunc(RZ(y + copysign(0.5, y))): adding
+//     with round-toward-zero never crosses an integer, and all integers in range are floats.
 __device__ __forceinline__ int32_t requant31(int32_t acc, float s, float lo, float hi) {
-  // x86 multiplies (the reference's host) return a NaN operand unchanged, sign included; the GPU
-  // would return a canonical NaN, so a NaN scale is propagated explicitly.
-  float y = s != s ? s : __fmul_rn(__int2float_rn(acc), s);
-  float t = truncf(y);
-  float r = fabsf(__fsub_rn(y, t)) >= 0.5f ? __fadd_rn(t, copysignf(1.0f, y)) : t;
-  if (y != y) r = (__float_as_uint(y) >> 31) ? lo : hi;  // NaN saturates by sign, then clips
-  return (int32_t)fminf(fmaxf(r, lo), hi);
+  float y = fminf(fmaxf(__fmul_rn(__int2float_rn(acc), s), lo), hi);
+  const float h = __uint_as_float((__float_as_uint(y) & 0x80000000u) | 0x3f000000u);
+  return __float2int_rz(__fadd_rz(y, h));
+}
+// The same chain for a NaN scale: the product is that NaN, which saturates by its sign.
+__device__ __forceinline__ int32_t requant31_nan_scale(float s, int32_t lo, int32_t hi) {
+  return (__float_as_uint(s) >> 31) ? lo : hi;
 }
 
 // Epilogue for 32 consecutive columns of one row.
+// csc: the 32 column scales of this chunk (global or shared memory); rs: the row's scale (EP_DQ).
+// nanmask: bit j set when column j's scale is a NaN (requant modes).
 template <bool IS_F16, int MODE>
-__device__ __forceinline__ void epilogue_store(const Params& p, int row, int col, const uint32_t* r) {
+__device__ __forceinline__ void epilogue_store(const Params& p, int row, int col, const uint32_t* r,
+                                               const float* csc, float rs, uint32_t nanmask) {
   uint8_t* base = (uint8_t*)p.D;
   const bool relu = p.ep_kind == 2;
   if constexpr (MODE == EP_I8 || MODE == EP_RQ31 || MODE == EP_RQ) {
     float sc[32];
     if constexpr (MODE != EP_I8) {
-      const float4* s4 = (const float4*)(p.scale + col);
+      const float4* s4 = (const float4*)csc;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float4 v = __ldg(s4 + q);
+        float4 v = s4[q];
         sc[4 * q] = v.x; sc[4 * q + 1] = v.y; sc[4 * q + 2] = v.z; sc[4 * q + 3] = v.w;
       }
     }
@@ -211,9 +249,12 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col
         int32_t q;
         if constexpr (MODE == EP_RQ31) {
           q = requant31(acc, sc[j + t], flo, fhi);
+          if (nanmask & (1u << (j + t))) q = requant31_nan_scale(sc[j + t], p.clip_lo, p.clip_hi);
         } else if constexpr (MODE == EP_RQ) {
+          // x86 products return a NaN operand unchanged and make 0 * inf the negative default NaN
           float sv = sc[j + t];
-          float y = sv != sv ? sv : __fmul_rn(__uint_as_float(fxp_to_fp_bits(acc, (uint32_t)p.int_width)), sv);
+          float y = __fmul_rn(__uint_as_float(fxp_to_fp_bits(acc, (uint32_t)p.int_width)), sv);
+          if (y != y) y = sv != sv ? sv : __uint_as_float(0xffc00000u);
           q = max(p.clip_lo, min(p.clip_hi, fp_to_fxp(y, (uint32_t)p.int_width)));
         } else {
           q = relu ? max(acc, 0) : acc;
@@ -241,11 +282,10 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col
   } else {  // EP_BF16, EP_DQ
     uint32_t rr[32];
     if constexpr (MODE == EP_DQ) {
-      const float rs = __ldg(p.row_scale + row);
-      const float4* s4 = (const float4*)(p.scale + col);
+      const float4* s4 = (const float4*)csc;
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        float4 v = __ldg(s4 + q);
+        float4 v = s4[q];
         const float sv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
@@ -419,7 +459,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
         uint32_t r[32];
         tmem_ld32(tbase + (uint32_t)(c * 32), r);
-        epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r);
+        const float* csc = p.scale ? p.scale + n0 + c * 32 : nullptr;
+        const uint32_t nanmask = MODE == EP_RQ31 ? __ballot_sync(0xffffffffu, __ldg(csc + lane) != __ldg(csc + lane)) : 0u;
+        epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r, csc,
+                                     MODE == EP_DQ ? __ldg(p.row_scale + m0 + row_in_tile) : 0.0f, nanmask);
       }
       fence_before();
       mbar_arrive(smem_u32(&acc_empty[acc]));
@@ -447,7 +490,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 //   acc_full[a]  (each CTA): MMA commit after the tile's last k-block, delivered to both
 //   acc_empty[a] (even CTA): one arrival per epilogue warp of both CTAs (16)
 // ---------------------------------------------------------------------------------------------
-constexpr int STAGES2 = 6;
+constexpr int RING2_BYTES = 192 * 1024;
+template <int BN>
+constexpr int stages2() {
+  return RING2_BYTES / (128 * BKB + (BN / 2) * BKB);
+}
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -495,10 +542,34 @@ __device__ __forceinline__ void mma2_commit_both(uint32_t bar) {
       : "memory");
 }
 
-template <bool IS_F16, int MODE>
+// r += one parked K-range partial (32 accumulators; f32 adds in range order for the bf16 kernel).
+// Parked K-range partials: each epilogue warp's share of a tile (its 32 rows x BN / 2 columns) is
+// one contiguous slice, chunk-major then column then row, so parking is 128-byte coalesced stores
+// and fetching is one bulk copy.
+template <int BN>
+__device__ __forceinline__ uint32_t* partial_slice(const Params& p, int slot, uint32_t rank, int ew) {
+  return p.ws + ((int64_t)(slot * 2 + (int)rank) * EPI_WARPS + ew) * (BN / 2) * 32;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+// r (chunk i of this warp) += the staged partial in shared memory.
+template <bool IS_F16>
+__device__ __forceinline__ void add_staged(uint32_t* r, const uint32_t* stage, int i, int lane) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const uint32_t x = stage[(i * 32 + j) * 32 + lane];
+    if (IS_F16) r[j] = __float_as_uint(__fadd_rn(__uint_as_float(r[j]), __uint_as_float(x)));
+    else r[j] += x;
+  }
+}
+
+template <bool IS_F16, int BN, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
-  constexpr int BN = 256;
+  constexpr int STAGES2 = stages2<BN>();
   constexpr int A_BYTES = 128 * BKB;
   constexpr int B_BYTES = (BN / 2) * BKB;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -511,15 +582,19 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* empty = bars + STAGES2;
   uint64_t* acc_full = bars + 2 * STAGES2;
   uint64_t* acc_empty = bars + 2 * STAGES2 + 2;
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES2 + 4);
+  uint64_t* xbar = bars + 2 * STAGES2 + 4;  // one per epilogue warp: partial fetches
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES2 + 4 + EPI_WARPS);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  float* sscale = (float*)(smem + STAGES2 * STAGE_BYTES + 256);  // 2 x EPI_WARPS x BN / 2 column scales
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  if (p.trace && threadIdx.x == 0) p.trace[p.trace_units * 5 + blockIdx.x * 3] = globaltimer();
   const int tiles_m = p.M / 256, tiles_n = p.N / BN;
   const int ntiles = tiles_m * tiles_n;
   const int kblocks = p.K * (IS_F16 ? 2 : 1) / BKB;
+  const int nunits = p.n_whole + (ntiles - p.n_whole) * p.split;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES2; ++s) {
@@ -530,6 +605,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(smem_u32(&acc_full[a]), 1);
       mbar_init(smem_u32(&acc_empty[a]), 2 * EPI_WARPS);
     }
+    for (int e = 0; e < EPI_WARPS; ++e) mbar_init(smem_u32(&xbar[e]), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -547,10 +623,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = pair; tile < ntiles; tile += npairs) {
-        const int m0 = (tile % tiles_m) * 256 + (int)rank * 128;
-        const int n0 = (tile / tiles_m) * BN + (int)rank * (BN / 2);
-        for (int kb = 0; kb < kblocks; ++kb) {
+      for (int u = pair; u < nunits; u += npairs) {
+        const Unit w = unit_of(p, u, kblocks);
+        const int m0 = (w.tile % tiles_m) * 256 + (int)rank * 128;
+        const int n0 = (w.tile / tiles_m) * BN + (int)rank * (BN / 2);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 201)) goto done_producer2;
           const uint32_t fb_local = smem_u32(&full[stage]);
           const uint32_t fb_pair = map_to_rank(fb_local, 0);
@@ -585,12 +662,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = pair; tile < ntiles; tile += npairs) {
+      for (int u = pair; u < nunits; u += npairs) {
+        const Unit w = unit_of(p, u, kblocks);
         if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, 203)) break;
         fence_after();
+        if (p.trace) p.trace[u * 5] = globaltimer();
         const uint32_t dcol = tmem_base + (uint32_t)(acc * BN);
         bool aborted = false;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&full[stage]), phase, abort_flag, p.err, 204)) {
             aborted = true;
             break;
@@ -602,9 +681,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < BKB / KSTEP_BYTES; ++k) {
             const uint64_t adv = (uint64_t)((k * KSTEP_BYTES) >> 4);
             if (IS_F16)
-              mma2_f16(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+              mma2_f16(dcol, da + adv, db + adv, idesc, (kb != w.kb0) | (k != 0));
             else
-              mma2_i8(dcol, da + adv, db + adv, idesc, (kb | k) != 0);
+              mma2_i8(dcol, da + adv, db + adv, idesc, (kb != w.kb0) | (k != 0));
           }
           mma2_commit_both(smem_u32(&empty[stage]));
           if (++stage == STAGES2) {
@@ -614,6 +693,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (aborted) break;
         mma2_commit_both(smem_u32(&acc_full[acc]));
+        if (p.trace) p.trace[u * 5 + 1] = globaltimer();
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -623,27 +703,132 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int sub = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in_tile = (int)rank * 128 + sub * 32 + lane;
+    const bool tracer = p.trace && rank == 0 && warp == 2 && lane == 0;
     const uint32_t acc_empty_pair = map_to_rank(smem_u32(&acc_empty[0]), 0);
+    constexpr bool kColScale = MODE == EP_RQ31 || MODE == EP_RQ || MODE == EP_DQ;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < ntiles; tile += npairs) {
-      const int m0 = (tile % tiles_m) * 256, n0 = (tile / tiles_m) * BN;
+    for (int u = pair; u < nunits; u += npairs) {
+      const Unit w = unit_of(p, u, kblocks);
+      const int m0 = (w.tile % tiles_m) * 256, n0 = (w.tile / tiles_m) * BN;
+      // Stage this warp's column scales in shared memory while the MMAs run: its own copy, so
+      // only the warp synchronises (double-buffered by accumulator). Chunk c = half + 2 i has its
+      // 32 scales at wsc + 32 i.
+      float* wsc = sscale + (acc * EPI_WARPS + (warp - 2)) * (BN / 2);
+      float rs = 0.0f;
+      if constexpr (kColScale) {
+#pragma unroll
+        for (int i = 0; i < BN / 64; ++i) wsc[i * 32 + lane] = __ldg(p.scale + n0 + (half + 2 * i) * 32 + lane);
+        if constexpr (MODE == EP_DQ) rs = __ldg(p.row_scale + m0 + row_in_tile);
+        __syncwarp();
+      }
       bool ok = mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_flag, p.err, 205);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       fence_after();
+      if (tracer) p.trace[u * 5 + 2] = globaltimer();
       const uint32_t tbase = tmem_base + (uint32_t)(acc * BN) + ((uint32_t)(sub * 32) << 16);
+      uint32_t* ctr = nullptr;
+      bool finish = w.sp < 0;  // this unit runs the epilogue straight from TMEM
+      if (!finish) {
+        // Have all other K-ranges of this tile already parked their partials? Then this range adds
+        // them to its own accumulator and runs the epilogue without parking its own.
+        ctr = p.cnt + ((int64_t)w.sp * 2 + rank) * EPI_WARPS + (warp - 2);
+        uint32_t seen = 0;
+        if (lane == 0) asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(seen) : "l"(ctr) : "memory");
+        finish = __shfl_sync(0xffffffffu, seen, 0) == (uint32_t)(p.split - 1);
+        if (finish) __threadfence();
+      }
+      // A split unit is always its pair's last unit (the split ranges fill the last wave), so by
+      // now the operand ring is idle: each warp stages fetched partials in its own 16 KiB of it.
+      const int ew = warp - 2;
+      const uint32_t xb = smem_u32(&xbar[ew]);
+      const uint32_t* stage = (const uint32_t*)(smem + ew * (BN / 2) * 32 * 4);
+      uint32_t xphase = 0;
+      // Fetch the partial of range q into this warp's staging slice; false if the wait expired.
+      auto fetch = [&](int q) {
+        constexpr uint32_t bytes = (BN / 2) * 32 * 4;
+        if (lane == 0) {
+          asm volatile("fence.proxy.async;" ::: "memory");
+          mbar_expect_tx(xb, bytes);
+          bulk_g2s(smem_u32(stage), partial_slice<BN>(p, w.sp * p.split + q, rank, ew), bytes, xb);
+        }
+        __syncwarp();
+        const bool got = __all_sync(0xffffffffu, mbar_wait(xb, xphase, abort_flag, p.err, 206));
+        xphase ^= 1;
+        return got;
+      };
+      // After reading a staged slice: order those reads before the next bulk write into it.
+      auto release_stage = [&]() {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+      };
+      if (w.sp >= 0 && !finish) {
+        // park this range's partial, then count this warp's arrival: every lane's partial is
+        // visible device-wide before the count, so the range that counts last sees all of them
+        uint32_t* mine = partial_slice<BN>(p, w.sp * p.split + w.part, rank, ew);
 #pragma unroll 1
-      for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
-        uint32_t r[32];
-        tmem_ld32(tbase + (uint32_t)(c * 32), r);
-        epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r);
+        for (int i = 0; i < BN / 64; ++i) {
+          uint32_t r[32];
+          tmem_ld32(tbase + (uint32_t)((half + 2 * i) * 32), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) __stcg(mine + (i * 32 + j) * 32 + lane, r[j]);
+        }
+        __threadfence();
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) last = atomicAdd(ctr, 1u) == (uint32_t)(p.split - 1);
+        finish = __shfl_sync(0xffffffffu, last, 0) != 0;
+        if (finish) __threadfence();
+      }
+      if (finish) {
+        bool good = true;
+        int q_last = p.split - 1;
+        if (w.sp >= 0 && q_last == w.part) --q_last;
+        // Split unit: add the other ranges' partials (ascending range order) to this range's
+        // accumulator, through TMEM for all but the last one.
+        for (int q = 0; w.sp >= 0 && q < q_last && good; ++q) {
+          if (q == w.part) continue;
+          good = fetch(q);
+#pragma unroll 1
+          for (int i = 0; i < BN / 64 && good; ++i) {
+            uint32_t r[32];
+            const uint32_t ta = tbase + (uint32_t)((half + 2 * i) * 32);
+            tmem_ld32(ta, r);
+            add_staged<IS_F16>(r, stage, i, lane);
+            tmem_st32(ta, r);
+          }
+          release_stage();
+        }
+        if (w.sp >= 0 && good) good = fetch(q_last);
+        if (good) {
+#pragma unroll 1
+          for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
+            uint32_t r[32];
+            tmem_ld32(tbase + (uint32_t)(c * 32), r);
+            if (tracer && w.sp < 0 && c == half) p.trace[u * 5 + 4] = globaltimer();
+            if (w.sp >= 0) add_staged<IS_F16>(r, stage, (c - half) >> 1, lane);
+            const float* csc = wsc + (c - half) * 16;
+            const uint32_t nanmask = MODE == EP_RQ31 ? __ballot_sync(0xffffffffu, csc[lane] != csc[lane]) : 0u;
+            epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r, csc, rs, nanmask);
+          }
+        }
+        if (w.sp >= 0) {
+          release_stage();
+          if (lane == 0) atomicExch(ctr, 0u);  // every other range has counted: reset for the next launch
+        }
       }
       fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_pair + (uint32_t)(acc * sizeof(uint64_t)));
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
+      if (tracer) {
+        uint32_t smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        p.trace[u * 5 + 3] = globaltimer();
+        if (w.sp >= 0) p.trace[u * 5 + 4] = smid;
+      }
     }
   }
 
@@ -652,7 +837,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+    if (p.trace && lane == 0) p.trace[p.trace_units * 5 + blockIdx.x * 3 + 2] = globaltimer();
   }
+  if (p.trace && threadIdx.x == 0) p.trace[p.trace_units * 5 + blockIdx.x * 3 + 1] = globaltimer();
 }
 
 // ---- host side ----
@@ -702,19 +889,66 @@ void launch(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Par
   launched(ctx, "gemm_tc");
 }
 
-template <bool IS_F16, int MODE>
-void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Params& p) {
-  constexpr int smem = STAGES2 * (128 * BKB + 128 * BKB) + 1024 + 256;
+// Split of the last wave: when the tiles leave the last round over the SM pairs less than half
+// full, its tiles run as `split` K-ranges each on the idle pairs. Returns the number of ranges
+// (1 = no split) and sizes the workspace and counters.
+int plan_split(fopt_ctx* ctx, Params& p, int ntiles, int pairs, int kblocks, int bn, bool f32_acc) {
+  p.n_whole = ntiles;
+  p.split = 1;
+  p.ws = nullptr;
+  p.cnt = nullptr;
+  if (getenv("FOPT_GEMM_NO_SPLIT")) return 1;
+  const int rem = ntiles % pairs;
+  if (rem == 0) return 1;
+  // Parking and fetching a partial costs about one epilogue (a few microseconds), so the split pays
+  // when the ranges it shortens are long: a single part-filled wave, or a long K.
+  if (!(ntiles < pairs ? kblocks >= 16 : kblocks >= 96)) return 1;
+  // f32 partials: two ranges only, whose sum is the same whichever range finishes last
+  const int split = std::min({pairs / rem, kblocks / 4, f32_acc ? 2 : 4});
+  if (split < 2) return 1;
+  const size_t ws_bytes = (size_t)rem * split * 256 * bn * 4;
+  const size_t n_cnt = (size_t)rem * 2 * EPI_WARPS;
+  if (ws_bytes > ctx->gemm_ws_bytes) {
+    if (ctx->gemm_ws) cuda_check(cudaFree(ctx->gemm_ws), "gemm workspace free");
+    cuda_check(cudaMalloc(&ctx->gemm_ws, ws_bytes), "gemm workspace alloc");
+    ctx->gemm_ws_bytes = ws_bytes;
+  }
+  if (n_cnt > ctx->gemm_cnt_n) {
+    if (ctx->gemm_cnt) cuda_check(cudaFree(ctx->gemm_cnt), "gemm counters free");
+    cuda_check(cudaMalloc(&ctx->gemm_cnt, n_cnt * 4), "gemm counters alloc");
+    ctx->gemm_cnt_n = n_cnt;
+    ctx->gemm_cnt_dirty = true;
+  }
+  if (ctx->gemm_cnt_dirty) {  // fresh, or a launch may have left mid-count after a timeout
+    cuda_check(cudaMemsetAsync(ctx->gemm_cnt, 0, ctx->gemm_cnt_n * 4, ctx->stream), "gemm counters clear");
+    ctx->gemm_cnt_dirty = false;
+  }
+  p.n_whole = ntiles - rem;
+  p.split = split;
+  p.ws = (uint32_t*)ctx->gemm_ws;
+  p.cnt = ctx->gemm_cnt;
+  return split;
+}
+
+template <bool IS_F16, int BN, int MODE>
+void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, Params p) {
+  constexpr int smem = stages2<BN>() * (128 * BKB + (BN / 2) * BKB) + 1024 + 256 + 2 * EPI_WARPS * (BN / 2) * 4;
   static bool attr = false;
   if (!attr) {
-    cuda_check(cudaFuncSetAttribute(gemm_tc2_kernel<IS_F16, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+    cuda_check(cudaFuncSetAttribute(gemm_tc2_kernel<IS_F16, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                "gemm2 smem attribute");
     attr = true;
   }
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
-  int tiles = (p.M / 256) * (p.N / 256);
-  int pairs = std::min(tiles, sms / 2);
+  const int tiles = (p.M / 256) * (p.N / BN);
+  const int split = plan_split(ctx, p, tiles, sms / 2, p.K * (IS_F16 ? 2 : 1) / BKB, BN, IS_F16);
+  const int units = p.n_whole + (tiles - p.n_whole) * split;
+  const int pairs = std::min(units, sms / 2);
+  const char* trace_path = getenv("FOPT_GEMM_TRACE");
+  p.trace = nullptr;
+  p.trace_units = units;
+  if (trace_path) cuda_check(cudaMallocAsync((void**)&p.trace, units * 40 + 2 * pairs * 24, ctx->stream), "trace alloc");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(THREADS);
@@ -727,8 +961,43 @@ void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Pa
   attrs[0].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cuda_check(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<IS_F16, MODE>, a, b, p), "gemm_tc2 launch");
+  cuda_check(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<IS_F16, BN, MODE>, a, b, p), "gemm_tc2 launch");
   launched(ctx, "gemm_tc2");
+  if (trace_path) {  // diagnostics only: append "unit mma0 mma1 epi0 epi1 sm" lines (ns from the first start)
+    std::vector<uint64_t> t((size_t)units * 5 + 2 * pairs * 3);
+    cuda_check(cudaMemcpyAsync(t.data(), p.trace, t.size() * 8, cudaMemcpyDeviceToHost, ctx->stream), "trace copy");
+    cuda_check(cudaStreamSynchronize(ctx->stream), "trace sync");
+    cudaFreeAsync(p.trace, ctx->stream);
+    uint64_t t0 = ~0ull;
+    for (int u = 0; u < units; ++u) t0 = std::min(t0, t[u * 5]);
+    if (FILE* f = fopen(trace_path, "a")) {
+      uint64_t e0 = ~0ull, e1 = 0, x1 = 0;
+      for (int b = 0; b < 2 * pairs; ++b) {
+        e0 = std::min(e0, t[units * 5 + b * 3]);
+        e1 = std::max(e1, t[units * 5 + b * 3]);
+        x1 = std::max(x1, t[units * 5 + b * 3 + 1]);
+      }
+      fprintf(f, "# M=%d N=%d K=%d units=%d whole=%d split=%d entry_first=%lld entry_last=%lld exit_last=%lld\n", p.M,
+              p.N, p.K, units, p.n_whole, p.split, (long long)(e0 - t0), (long long)(e1 - t0), (long long)(x1 - t0));
+      for (int u = 0; u < units; ++u)
+        fprintf(f, "%d %llu %llu %llu %llu %llu\n", u, (unsigned long long)(t[u * 5] - t0),
+                (unsigned long long)(t[u * 5 + 1] - t0), (unsigned long long)(t[u * 5 + 2] - t0),
+                (unsigned long long)(t[u * 5 + 3] - t0),
+                (unsigned long long)(t[u * 5 + 4] > t0 ? t[u * 5 + 4] - t0 : t[u * 5 + 4]));
+      fclose(f);
+    }
+  }
+}
+
+// Tile width of the paired kernel: 256 whenever N allows. The narrower tile streams 1.5x the
+// L2 -> shared-memory bytes per MMA (96 vs 64 bytes per SM-cycle at the full int8 rate), which on
+// B200 costs more than its fuller last wave gains; the last wave is evened out by the K split.
+int pair_tile_n(int max_bn) {
+  if (const char* e = getenv("FOPT_GEMM_BN")) {
+    int v = atoi(e);
+    if ((v == 128 || v == 256) && v <= max_bn) return v;
+  }
+  return max_bn;
 }
 
 }  // namespace gemm
@@ -785,12 +1054,14 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
   } else {
     return false;
   }
-  const bool pair = M % 256 == 0 && N % 256 == 0 && !getenv("FOPT_GEMM_1SM");
+  const bool pair = M % 256 == 0 && bn && !getenv("FOPT_GEMM_1SM");
+  if (pair) bn = pair_tile_n(bn);
   CUtensorMap ma = make_map(a, f16, K, M, lda, pair ? 128 : BM);
-  CUtensorMap mb = make_map(b, f16, K, N, ldb, pair ? 128 : bn);
-#define FOPT_GEMM_DISPATCH(F16, MODE)                 \
-  if (pair) launch2<F16, MODE>(ctx, ma, mb, p);       \
-  else if (bn == 256) launch<F16, 256, MODE>(ctx, ma, mb, p); \
+  CUtensorMap mb = make_map(b, f16, K, N, ldb, pair ? bn / 2 : bn);
+#define FOPT_GEMM_DISPATCH(F16, MODE)                                \
+  if (pair && bn == 256) launch2<F16, 256, MODE>(ctx, ma, mb, p);    \
+  else if (pair) launch2<F16, 128, MODE>(ctx, ma, mb, p);            \
+  else if (bn == 256) launch<F16, 256, MODE>(ctx, ma, mb, p);        \
   else launch<F16, 128, MODE>(ctx, ma, mb, p);
   if (f16) {
     if (mode == EP_BF16) { FOPT_GEMM_DISPATCH(true, EP_BF16) }

@@ -318,6 +318,8 @@ CONTRACTIONS = [
     # tensor-core shapes (M % 128, N % 128, K % 128 bytes): several tiles per CTA ring
     ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]", dict(M=256, K=512, N=512)),
     ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]", dict(M=384, K=1024, N=384)),
+    # fewer tiles than SM pairs and a long K: the paired kernel splits each tile into K-ranges
+    ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]", dict(M=256, K=2048, N=512)),
 ]
 
 
@@ -439,24 +441,42 @@ def test_attention_parity(b200, B, S, Hq, Hkv, causal):
     assert np.all(err <= 2 ** -7 * np.abs(w) + 1e-2), f"max abs err {err.max()}"
 
 
-def test_gemm_tc_requant_large_grid(b200):
-    # more tiles than SMs: exercises the persistent tile loop and both TMEM accumulators
-    ax = dict(M=2048, K=256, N=2560)
+@pytest.fixture(params=["pair256", "pair128", "single"])
+def gemm_tile(request, monkeypatch):
+    """Runs a tensor-core GEMM test through each kernel shape: CTA pairs on 256 x 256 or 256 x 128
+    tiles, and the single-CTA kernel."""
+    monkeypatch.delenv("FOPT_GEMM_1SM", raising=False)
+    monkeypatch.delenv("FOPT_GEMM_BN", raising=False)
+    if request.param == "single":
+        monkeypatch.setenv("FOPT_GEMM_1SM", "1")
+    else:
+        monkeypatch.setenv("FOPT_GEMM_BN", request.param[4:])
+    return request.param
+
+
+@pytest.mark.parametrize("shape", [(2048, 256, 2560), (512, 384, 384), (512, 2048, 2560), (256, 2048, 256)])
+def test_gemm_tc_requant_large_grid(b200, gemm_tile, shape):
+    # more tiles than SMs: exercises the persistent tile loop and both TMEM accumulators; the second
+    # shape has N % 256 != 0, so the paired kernel runs 256 x 128 tiles whatever is asked; the last
+    # two fill less than one wave over the SM pairs with K long enough, so their tiles run split into K-ranges
+    M, K, N = shape
+    ax = dict(M=M, K=K, N=N)
     (L, rl), (R, rr), (P, rp), (O, ro) = (pair(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
     lv, rv = rand_vals("i8", L.size), rand_vals("i8", R.size)
-    scale = RNG.uniform(0.001, 0.01, 2560).astype(np.float32)
-    s = b200.from_vec(fb.Mapping("[N]", dict(N=2560)), scale, "f32")
+    scale = RNG.uniform(0.001, 0.01, N).astype(np.float32)
+    s = b200.from_vec(fb.Mapping("[N]", dict(N=N)), scale, "f32")
     got = b200.contraction_requant(b200.from_vec(L, lv, "i8"), b200.from_vec(R, rv, "i8"), L, R, P, O, s, "N")
     want = oracle.contract(lv.tobytes(), rv.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
                            scale_axis="N")
     assert got.to_bytes() == want
 
 
-@pytest.mark.parametrize("dtype", ["i8", "bf16"])
-def test_gemm_full_size_properties(b200, dtype):
-    """Config 2 at full size (M=N=K=4096): size-independent checks instead of the slow oracle --
-    exact row / column checksums (linearity) of the i32 result and 8 sampled rows in full."""
-    M = N = K = 4096
+@pytest.mark.parametrize("dtype,K", [("i8", 4096), ("bf16", 4096), ("i8", 16384), ("bf16", 12288)])
+def test_gemm_full_size_properties(b200, gemm_tile, dtype, K):
+    """Config 2 at full size (M=N=K=4096), and long-K shapes whose last wave runs split into K-ranges:
+    size-independent checks instead of the slow oracle -- exact row / column checksums (linearity)
+    of the i32 result and 8 sampled rows in full."""
+    M = N = 4096
     ax = dict(M=M, N=N, K=K)
     L, R, P, O = (fb.Mapping(e, ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
     rng = np.random.default_rng(7)
@@ -479,27 +499,67 @@ def test_gemm_full_size_properties(b200, dtype):
         B = dtypes.bf16_bits_to_f32(b).reshape(N, K).astype(np.float64)
         rows = rng.choice(M, 8, replace=False)
         ref = A[rows] @ B.T
-        # f32 accumulation of 4096 N(0,1) products: |err| <= 1e-4 * sqrt(K) * rms
+        # f32 accumulation of K N(0,1) products: |err| <= 1e-4 * sqrt(K) * rms
         assert np.max(np.abs(D[rows] - ref)) <= 1e-4 * np.sqrt(K) * 2, np.max(np.abs(D[rows] - ref))
-        assert np.allclose(D.sum(1), A @ B.sum(0), rtol=1e-3, atol=1.0)
+        # a row sum adds N such errors, which add up like a random walk
+        assert np.allclose(D.sum(1), A @ B.sum(0), rtol=1e-3, atol=max(1.0, 2e-4 * np.sqrt(K) * np.sqrt(N)))
 
 
-def test_gemm_tc_requant_ties_and_saturation(b200):
-    """Tensor-core requant on values that hit exact .5 ties (round half away from zero), huge and
-    negative scales (saturation into the Clip), and a NaN scale (saturates by sign, then clips)."""
+@pytest.fixture(params=["tensor_core", "generic"])
+def contract_path(request, monkeypatch):
+    """Runs a contraction test through the tensor-core GEMM and through the generic fold kernel."""
+    if request.param == "generic":
+        monkeypatch.setenv("FOPT_DISABLE_TC", "1")
+    else:
+        monkeypatch.delenv("FOPT_DISABLE_TC", raising=False)
+    return request.param
+
+
+@pytest.mark.parametrize("iw", [31, 24])
+def test_gemm_tc_requant_ties_and_saturation(b200, contract_path, iw):
+    """Requant on values that hit exact .5 ties (round half away from zero), huge and negative scales
+    (saturation into the Clip), NaN scales (saturate by sign, then clip) and infinite scales times a
+    zero accumulator (the x86 default NaN, which is negative)."""
     ax = dict(M=256, K=256, N=256)
     (L, rl), (R, rr), (P, rp), (O, ro) = (pair(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
     lv, rv = rand_vals("i8", L.size), rand_vals("i8", R.size)
     scale = np.tile(np.array([0.5, 0.25, -0.5, 1e30, -1e30, 0.0078125, 1.5, -0.125], np.float32), 32)
     scale[7] = np.float32("nan")
     scale[15] = -np.float32("nan")
+    scale[16], scale[17] = np.float32("inf"), -np.float32("inf")  # 0 * inf: the x86 default NaN is negative
+    lv = lv.copy()
+    lv.reshape(256, 256)[::7] = 0  # zero rows: accumulators of exactly 0
     s = b200.from_vec(fb.Mapping("[N]", dict(N=256)), scale, "f32")
     for lo, hi in ((-128, 127), (-20, 50)):
         got = b200.contraction_requant(b200.from_vec(L, lv, "i8"), b200.from_vec(R, rv, "i8"), L, R, P, O, s, "N",
-                                       lo=lo, hi=hi)
+                                       int_width=iw, lo=lo, hi=hi)
         want = oracle.contract(lv.tobytes(), rv.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
-                               scale_axis="N", clip_lo=lo, clip_hi=hi)
+                               scale_axis="N", int_width=iw, clip_lo=lo, clip_hi=hi)
         assert got.to_bytes() == want
+
+
+def test_gemm_tc_requant_near_ties(b200, contract_path):
+    """Round half away from zero next to the ties: accumulators -128 .. 127 (one per row) times
+    scales within an ulp of k + 1/2 over small integers, and of 1/3, 2/3, 1/7."""
+    M, K, N = 256, 128, 256
+    ax = dict(M=M, K=K, N=N)
+    (L, rl), (R, rr), (P, rp), (O, ro) = (pair(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
+    a = np.zeros((M, K), np.int8)
+    a[:, 0] = np.arange(-128, 128)  # acc[m, n] = a[m, 0] * 1
+    b = np.zeros((N, K), np.int8)
+    b[:, 0] = 1
+    base = []
+    for num in (0.5, 1.5, 2.5, 0.25, 0.75, 1 / 3, 2 / 3, 1 / 7, 1.0, 0.1):
+        f = np.float32(num)
+        base += [f, np.nextafter(f, np.float32(0)), np.nextafter(f, np.float32(2))]
+    scale = np.resize(np.array(base, np.float32), N)
+    scale[1::2] *= -1
+    s = b200.from_vec(fb.Mapping("[N]", dict(N=N)), scale, "f32")
+    got = b200.contraction_requant(b200.from_vec(L, a.reshape(-1), "i8"), b200.from_vec(R, b.reshape(-1), "i8"),
+                                   L, R, P, O, s, "N", lo=-128, hi=127)
+    want = oracle.contract(a.tobytes(), b.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
+                           scale_axis="N", clip_lo=-128, clip_hi=127)
+    assert got.to_bytes() == want
 
 
 @pytest.mark.parametrize("iw", [0, 1, 4, 16, 24, 30, 31])
