@@ -43,6 +43,30 @@ def mnist_inputs(seed: int = 0, B: int = 64, I: int = 784, H: int = 128, O: int 
     return x, w1, w2, s1
 
 
+def _prog_bias(relu: bool):
+    # bf16 matmul + bf16 bias in f32 (ClipBinaryOpF32::Add), optional Max 0, narrowed to bf16
+    p = ops.Prog(2)
+    y = p.emit("ADDF", p.emit("BF16_TO_F32", 0), p.emit("BF16_TO_F32", 1))
+    if relu:
+        y = p.emit("MAXF", y, p.const_f32(0.0))
+    return p.build(p.emit("F32_TO_BF16", y))
+
+
+MNIST_BF16_AXES = dict(X=800, H=256, C=16)
+
+
+def mnist_bf16_forward(be: B200, x: Storage, w1: Storage, b1: Storage, w2: Storage, b2: Storage) -> Storage:
+    """The reference's own bf16 MNIST forward (furiosa-opt-examples/src/mnist/mod.rs:1-192), one
+    image: fc1 contraction (bf16 x bf16, f32 accumulation, narrowed to bf16: `fc1_matmul`), bias add
+    and ReLU in f32 narrowed to bf16 (`fc1_relu`), fc2 contraction and bias add (`fc2`). Shapes
+    x [X=800], w1 [H=256, X], b1 [H], w2 [C=16, H], b2 [C]; returns the bf16 logits [C]."""
+    m = lambda e: Mapping(e, MNIST_BF16_AXES)
+    h = be._contract(w1, x, m("[H, X]"), m("[X]"), m("[H, X]"), m("[H]"), "bf16")
+    h = be.zip_with(h, b1, _prog_bias(True), "bf16")
+    o = be._contract(w2, h, m("[C, H]"), m("[H]"), m("[C, H]"), m("[C]"), "bf16")
+    return be.zip_with(o, b2, _prog_bias(False), "bf16")
+
+
 # ---------------------------------------------------------------------------------------------
 # config 4
 # ---------------------------------------------------------------------------------------------

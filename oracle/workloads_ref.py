@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import attention, contract
+from . import attention, contract, elementwise
 from .mapping_ref import ref_m
 
 
@@ -34,6 +34,29 @@ def mnist_ref(x, w1, w2, s1, B, I, H, O) -> np.ndarray:
                  ep_kind=1, scale=s1, scale_axis="H", clip_lo=0, clip_hi=127)
     logits = contract(h, w2.tobytes(), "i8", "i32", m("[B, H]"), m("[O, H]"), m("[B, O, H]"), m("[B, O]"))
     return np.frombuffer(logits, np.int32).reshape(B, O)
+
+
+def _bias_insns(relu: bool):
+    # the register program of the bias step: r2 = bf16->f32(r0), r3 = bf16->f32(r1), r4 = r2 + r3,
+    # [r6 = max(r4, 0.0)], narrowed to bf16 (opcode numbers of the C ABI)
+    ins = [(1, 2, 0, 0, 0, 0), (1, 3, 1, 0, 0, 0), (30, 4, 2, 3, 0, 0)]
+    if relu:
+        ins += [(71, 5, 0, 0, 0, 0), (36, 6, 4, 5, 0, 0)]
+    ins += [(2, 7, 6 if relu else 4, 0, 0, 0)]
+    return ins, 7
+
+
+def mnist_bf16_ref(x: bytes, w1: bytes, b1: bytes, w2: bytes, b2: bytes) -> bytes:
+    """bf16 MNIST forward of mnist/mod.rs (one image): fc1 = bf16(sum_x w1[h, x] * x[x]) with the f32
+    fold in x order, bias + ReLU in f32 -> bf16, fc2 likewise, bias -> bf16. Returns logits [16] bf16."""
+    ax = dict(X=800, H=256, C=16)
+    m = lambda e: ref_m(e, **ax)
+    h = contract(w1, x, "bf16", "bf16", m("[H, X]"), m("[X]"), m("[H, X]"), m("[H]"))
+    ins, ret = _bias_insns(True)
+    h = elementwise(ins, ret, [h, b1], ["bf16", "bf16"], "bf16", 256)
+    o = contract(w2, h, "bf16", "bf16", m("[C, H]"), m("[H]"), m("[C, H]"), m("[C]"))
+    ins, ret = _bias_insns(False)
+    return elementwise(ins, ret, [o, b2], ["bf16", "bf16"], "bf16", 16)
 
 
 def _round_half_away(y: np.ndarray) -> np.ndarray:

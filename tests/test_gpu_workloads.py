@@ -26,6 +26,24 @@ def test_mnist_int8_mlp_bit_exact(b200):
     assert np.array_equal(logits.argmax(1), want.argmax(1))
 
 
+def test_mnist_bf16_reference_forward_bit_exact(b200):
+    """The reference's own bf16 MNIST forward (mnist/mod.rs), whose restatement reproduces the
+    reference test's labels on its weights (test_oracle.py), on seeded weights of the same shapes:
+    logits bit-exact against the oracle, ten images."""
+    rng = np.random.default_rng(11)
+    bf = lambda a: fb.dtypes.f32_to_bf16_bits(a.astype(np.float32))
+    X, H, C = 800, 256, 16
+    w1, b1 = bf(rng.standard_normal((H, X)) * 0.05), bf(rng.standard_normal(H) * 0.1)
+    w2, b2 = bf(rng.standard_normal((C, H)) * 0.1), bf(rng.standard_normal(C) * 0.1)
+    m = lambda e: fb.Mapping(e, W.MNIST_BF16_AXES)
+    dev = [b200.from_vec(m(e), v, "bf16") for e, v in (("[H, X]", w1), ("[H]", b1), ("[C, H]", w2), ("[C]", b2))]
+    for i in range(10):
+        x = bf(np.clip(rng.random(X), 0, 1) * (rng.random(X) < 0.3))
+        got = W.mnist_bf16_forward(b200, b200.from_vec(m("[X]"), x, "bf16"), *dev).to_bytes()
+        want = R.mnist_bf16_ref(x.tobytes(), w1.tobytes(), b1.tobytes(), w2.tobytes(), b2.tobytes())
+        assert got == want, i
+
+
 def test_decoder_block_w8a8(b200):
     batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
     T, H = batch * seq, Hq * 128

@@ -3,6 +3,7 @@
 Every expected value below is transcribed from the reference test it cites; the oracle must
 reproduce each one before it is trusted as the parity checker for the CUDA kernels.
 """
+import os
 import struct
 
 import numpy as np
@@ -290,3 +291,31 @@ def test_fxp_to_fp_iw31_is_ieee_rne():
     for v in vals:
         got = lib.ref_fxp_to_fp(int(v), 31)
         assert got == int(np.float32(np.int32(v)).view(np.uint32)), int(v)
+
+
+MNIST_DATA = "/root/reference/furiosa-opt-examples/data/mnist/mnist.safetensors"
+
+
+def _safetensors(path):
+    import json
+    import struct
+    with open(path, "rb") as fh:
+        raw = fh.read()
+    n = struct.unpack("<Q", raw[:8])[0]
+    head = json.loads(raw[8:8 + n])
+    body = raw[8 + n:]
+    return {k: body[v["data_offsets"][0]:v["data_offsets"][1]] for k, v in head.items() if k != "__metadata__"}
+
+
+@pytest.mark.skipif(not os.path.exists(MNIST_DATA), reason="reference tree not present")
+def test_mnist_bf16_reference_known_answers():
+    """The reference's own end-to-end known answers (furiosa-opt-examples/tests/mnist_tests.rs:7-53):
+    with its bf16 weights, the restated forward classifies all ten test images as labelled (the
+    argmax over the first ten logits, as the test takes)."""
+    from oracle.workloads_ref import mnist_bf16_ref
+    t = _safetensors(MNIST_DATA)
+    for i in range(10):
+        logits = mnist_bf16_ref(t[f"hw.image_{i}"], t["hw.fc1.weight"], t["fc1.bias"], t["hw.fc2.weight"],
+                                t["hw.fc2.bias"])
+        f = (np.frombuffer(logits, np.uint16).astype(np.uint32) << 16).view(np.float32)[:10]
+        assert int(np.argmax(f)) == int(np.frombuffer(t[f"label_{i}"], np.int32)[0]), i
