@@ -16,7 +16,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "ctx.hpp"
 
@@ -45,19 +47,32 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// The same test, but a thread whose phase has not completed sleeps until it does (or for at most
+// the hint, 20 us) instead of returning at once: waiting warps then leave the issue slots to the
+// warps doing work.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(20000)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int code) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = gtimer();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try(bar, parity)) return true;
-    if ((it & 255) == 0) {
-      if (*abort_flag) return false;
-      if (gtimer() - t0 > kWaitNs) {
-        *abort_flag = 1;
-        atomicExch(err, code);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_sleep(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (gtimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(err, code);
+      return false;
     }
   }
 }
@@ -77,6 +92,14 @@ __device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap* map, uint3
       "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// Tiled TMA store shared -> global (bulk async group of the issuing thread).
+__device__ __forceinline__ void tma3_store(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"((uint64_t)map),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
   uint64_t d = (uint64_t)((addr & 0x3FFFF) >> 4);
   d |= (uint64_t)1 << 16;
@@ -119,6 +142,28 @@ __device__ __forceinline__ void tst32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 #undef S32
+#define S16(i) "r"(r[i])
+__device__ __forceinline__ void tst16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      S16(0), S16(1), S16(2), S16(3), S16(4), S16(5), S16(6), S16(7), S16(8), S16(9), S16(10), S16(11), S16(12),
+      S16(13), S16(14), S16(15)
+      : "memory");
+}
+#undef S16
+// tcgen05.wait::ld that also ties the 32 destination registers of the loads it completes, so the
+// compiler cannot move their uses above it.
+#define T32(i) "+r"(r[i])
+__device__ __forceinline__ void tld_wait_regs(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : T32(0), T32(1), T32(2), T32(3), T32(4), T32(5), T32(6), T32(7), T32(8), T32(9), T32(10), T32(11),
+                 T32(12), T32(13), T32(14), T32(15), T32(16), T32(17), T32(18), T32(19), T32(20), T32(21), T32(22),
+                 T32(23), T32(24), T32(25), T32(26), T32(27), T32(28), T32(29), T32(30), T32(31)
+               :
+               : "memory");
+}
+#undef T32
 __device__ __forceinline__ void tld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tst_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -129,6 +174,7 @@ struct Params {
   float scale_log2;  // scale * log2(e)
   float eps;
   int* err;
+  uint64_t* trace;  // diagnostics (FOPT_ATTN_TRACE): per CTA 40 stamps, see attention_tc2_kernel
 };
 
 // 2^x on the special-function unit (relative error ~2^-22; the scores' bf16 rounding dominates).
@@ -143,11 +189,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-// Packs two f32 into bf16x2 with RNE (finite values; the softmax produces no NaN for finite inputs).
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  uint32_t a = f32_to_bf16w(__float_as_uint(lo)), b = f32_to_bf16w(__float_as_uint(hi));
-  return (a >> 16) | (b & 0xffff0000u);
-}
+// Packs two f32 into bf16x2 under the reference's conversion rule.
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) { return bf16x2_rule(lo, hi); }
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -368,6 +411,298 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
+// ---------------------------------------------------------------------------------------------
+// Two query tiles per CTA (ping-pong), P kept in tensor memory.
+//
+// One CTA per (batch, query head, pair of adjacent 128-row query blocks); 320 threads:
+//   warp 0     TMA producer: both Q tiles once, then K and V^T tiles into a 2-stage ring that both
+//              query tiles read;
+//   warp 1     TMEM owner and MMA issuer, in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) ...:
+//              S_t = Q_t K^T into TMEM, and O_t += P_t V with P_t read from TMEM (the A operand);
+//   warps 2-5  softmax of query tile 0, warps 6-9 of tile 1: one thread per row reads its scores from
+//              TMEM, keeps the running max / sum, rescales its O row when the max grows, and writes
+//              the bf16 probabilities back over the first 64 columns of its S row (tcgen05.st).
+// While one tile's softmax runs, the tensor cores work on the other tile. P_t shares S_t's columns,
+// so S_t(j+1) is issued only after PV_t(j) has completed.
+// TMEM columns: S0 [0, 128), S1 [128, 256), O0 [256, 384), O1 [384, 512).
+// ---------------------------------------------------------------------------------------------
+constexpr int THREADS2 = 320;
+
+__device__ __forceinline__ void mma_bf16_ta(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__global__ void __launch_bounds__(THREADS2, 1)
+    attention_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmVt, const __grid_constant__ CUtensorMap tmO, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;               // 2 x 32 KiB (tile t at sQ + t * TILE)
+  uint8_t* sKV = smem + 2 * TILE;   // STAGES x (K tile + V^T tile)
+  uint64_t* bars = (uint64_t*)(smem + 2 * TILE + STAGES * 2 * TILE);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;  // K and V of a stage are released separately: K after both S MMAs
+  uint64_t* k_empty = k_full + STAGES;
+  uint64_t* v_full = k_empty + STAGES;
+  uint64_t* v_empty = v_full + STAGES;
+  uint64_t* s_full = v_empty + STAGES;  // [2] per tile
+  uint64_t* p_ready = s_full + 2;        // [2]
+  uint64_t* pv_done = p_ready + 2;       // [2]
+  uint32_t* tmem_slot = (uint32_t*)(pv_done + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npair = p.S / (2 * BQ);
+  // heaviest (last) query blocks first under causal masking
+  const int qp = npair - 1 - (int)(blockIdx.x % npair);
+  const int h = (int)((blockIdx.x / npair) % p.Hq);
+  const int b = (int)(blockIdx.x / (npair * p.Hq));
+  const int hk = h / (p.Hq / p.Hkv);
+  const int qb0 = 2 * qp;  // tile t covers query block qb0 + t
+  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 40 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = gtimer();
+  // last key block of each tile (inclusive)
+  const int last0 = p.causal ? qb0 : p.S / BK - 1;
+  const int last1 = p.causal ? qb0 + 1 : p.S / BK - 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 2);
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 2);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&s_full[t]), 1);
+      mbar_init(smem_u32(&p_ready[t]), 128);
+      mbar_init(smem_u32(&pv_done[t]), 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int row0 = b * p.S;  // flattened (batch, seq) row of the tensor maps
+      const uint32_t qf = smem_u32(q_full);
+      mbar_expect_tx(qf, 2 * TILE);
+      for (int t = 0; t < 2; ++t) {
+        tma3(smem_u32(sQ + t * TILE), &tmQ, qf, 0, h, row0 + (qb0 + t) * BQ);
+        tma3(smem_u32(sQ + t * TILE + CHUNK), &tmQ, qf, 64, h, row0 + (qb0 + t) * BQ);
+      }
+      for (int j = 0; j <= last1; ++j) {
+        const int st = j % STAGES;
+        const uint32_t ph = ((j / STAGES) & 1) ^ 1;
+        uint8_t* sK = sKV + st * 2 * TILE;
+        uint8_t* sV = sK + TILE;
+        if (!mbar_wait(smem_u32(&k_empty[st]), ph, abort_flag, p.err, 311)) break;
+        const uint32_t kb = smem_u32(&k_full[st]);
+        mbar_expect_tx(kb, TILE);
+        tma3(smem_u32(sK), &tmK, kb, 0, hk, row0 + j * BK);
+        tma3(smem_u32(sK + CHUNK), &tmK, kb, 64, hk, row0 + j * BK);
+        if (!mbar_wait(smem_u32(&v_empty[st]), ph, abort_flag, p.err, 319)) break;
+        const uint32_t vb = smem_u32(&v_full[st]);
+        mbar_expect_tx(vb, TILE);
+        tma3(smem_u32(sV), &tmVt, vb, j * BK, 0, b * p.Hkv + hk);
+        tma3(smem_u32(sV + CHUNK), &tmVt, vb, j * BK + 64, 0, b * p.Hkv + hk);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+      const uint32_t sQ0 = smem_u32(sQ);
+      auto issue_s = [&](int t, int j) {  // S_t = Q_t K_j^T
+        const uint32_t sK = smem_u32(sKV + (j % STAGES) * 2 * TILE);
+        const uint32_t sq = sQ0 + t * TILE;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+          mma_bf16(tmem + t * 128, sdesc(sq + off), sdesc(sK + off), idesc, k != 0);
+        }
+        commit(smem_u32(&s_full[t]));
+      };
+      auto issue_pv = [&](int t, int j) {  // O_t += P_t V_j, P_t in TMEM columns [128 t, 128 t + 64)
+        const uint32_t sV = smem_u32(sKV + (j % STAGES) * 2 * TILE + TILE);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
+          mma_bf16_ta(tmem + 256 + t * 128, tmem + t * 128 + 8 * k, sdesc(sV + off), idesc, (j | k) != 0);
+        }
+        commit(smem_u32(&pv_done[t]));
+      };
+      bool ok = mbar_wait(smem_u32(q_full), 0, abort_flag, p.err, 312) &&
+                mbar_wait(smem_u32(&k_full[0]), 0, abort_flag, p.err, 313);
+      if (ok) {
+        fence_after();
+        issue_s(0, 0);
+        commit(smem_u32(&k_empty[0]));
+        issue_s(1, 0);
+        commit(smem_u32(&k_empty[0]));
+      }
+      for (int j = 0; ok && j <= last1; ++j) {
+        for (int t = 0; t < 2 && ok; ++t) {
+          const int last = t ? last1 : last0;
+          if (j > last) continue;
+          const bool solo = t == 1 && j > last0;  // tile 0 does not use this block
+          ok = mbar_wait(smem_u32(&p_ready[t]), j & 1, abort_flag, p.err, 314) &&
+               mbar_wait(smem_u32(&v_full[j % STAGES]), (j / STAGES) & 1, abort_flag, p.err, 320);
+          if (!ok) break;
+          fence_after();
+          issue_pv(t, j);
+          // the K and V "empty" barriers take one commit per tile per block (two from tile 1 for the
+          // block tile 0 does not use)
+          commit(smem_u32(&v_empty[j % STAGES]));
+          if (solo) commit(smem_u32(&v_empty[j % STAGES]));
+          if (j + 1 <= last) {
+            // S_t(j+1) overwrites the columns PV_t(j) reads P_t from: wait for it, and for K_{j+1}
+            ok = mbar_wait(smem_u32(&pv_done[t]), j & 1, abort_flag, p.err, 315) &&
+                 mbar_wait(smem_u32(&k_full[(j + 1) % STAGES]), ((j + 1) / STAGES) & 1, abort_flag, p.err, 316);
+            if (!ok) break;
+            fence_after();
+            issue_s(t, j + 1);
+            commit(smem_u32(&k_empty[(j + 1) % STAGES]));
+            if (t == 1 && j + 1 > last0) commit(smem_u32(&k_empty[(j + 1) % STAGES]));
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax: one thread per query row of tile t ----------------
+    const int t = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // row within the tile = TMEM lane
+    const int qb = qb0 + t;
+    const int qrow = qb * BQ + r;
+    const int last = t ? last1 : last0;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_base, tO = tmem + 256 + t * 128 + lane_base;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j <= last; ++j) {
+      ok = mbar_wait(smem_u32(&s_full[t]), j & 1, abort_flag, p.err, 317);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      fence_after();
+      const bool tracer = tr && t == 0 && r == 0 && j < 17;
+      if (tracer) tr[1 + 2 * j] = gtimer();
+      uint32_t s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tld32(tS + c * 32, s + 32 * c);
+      tld_wait();
+      const bool diag = p.causal && j == qb;
+      if (diag) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c > r) s[c] = __float_as_uint(-INFINITY);
+      }
+      // row max and sum as 8 independent chains
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(s[k]);
+#pragma unroll
+      for (int c = 8; c < 128; c += 8)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(s[c + k]));
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
+      // Lazy rescaling: the exponent base m moves only when the block max exceeds it by more than
+      // 8 (log2 units), so probabilities stay below 2^8 and O and l share one base; the normalised
+      // result is unchanged and the O rescale below becomes rare.
+      const float mnew = mx > m + 8.0f ? mx : m;
+      const float alpha = ex2(m - mnew);
+      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t* pk = s;  // packed bf16 pairs overwrite the scores in place (index c / 2 <= c)
+#pragma unroll
+      for (int c = 0; c < 128; c += 2) {
+        const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -mnew));
+        const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -mnew));
+        sum8[(c >> 1) & 7] += p0 + p1;
+        pk[c / 2] = pack_bf16x2(p0, p1);
+      }
+      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      l = l * alpha + sum;
+      m = mnew;
+      // S_t(j) was issued after PV_t(j - 1) completed, so the O row is stable here
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tld32(tO + c * 32, o);
+          tld_wait_regs(o);
+#pragma unroll
+          for (int q = 0; q < 32; ++q) o[q] = __float_as_uint(__uint_as_float(o[q]) * alpha);
+          tst32(tO + c * 32, o);
+        }
+      }
+      tst32(tS, pk);
+      tst32(tS + 32, pk + 32);
+      tst_wait();
+      fence_before();
+      mbar_arrive(smem_u32(&p_ready[t]));
+      if (tracer) tr[2 + 2 * j] = gtimer();
+    }
+    if (tr && t == 0 && r == 0) tr[35] = gtimer();
+    if (ok) {
+      ok = mbar_wait(smem_u32(&pv_done[t]), last & 1, abort_flag, p.err, 318);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (tr && t == 0 && r == 0) tr[37] = gtimer();
+    if (ok) {
+      fence_after();
+      // O row -> this tile's (now idle) Q buffer in the 128-byte-swizzled TMA layout, then each warp
+      // stores its 32 rows with two tensor stores: whole 128-byte lines instead of one 16-byte piece
+      // per row per lane.
+      const float inv = 1.0f / (l + p.eps);
+      uint8_t* stage = sQ + t * TILE;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tld32(tO + c * 32, o);
+        tld_wait();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int u = c * 4 + q;  // 16-byte unit of the row: columns 8 u .. 8 u + 7
+          uint4* dst = (uint4*)(stage + (u >> 3) * CHUNK + r * 128 + (((u & 7) ^ (r & 7)) << 4));
+          *dst = make_uint4(pack_bf16(__uint_as_float(o[8 * q]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        const int grow = b * p.S + qb * BQ + quarter * 32;
+        tma3_store(&tmO, smem_u32(stage + quarter * 32 * 128), 0, h, grow);
+        tma3_store(&tmO, smem_u32(stage + CHUNK + quarter * 32 * 128), 64, h, grow);
+        bulk_commit();
+        bulk_wait_read0();
+      }
+      __syncwarp();
+      if (tr && t == 0 && r == 0) tr[36] = gtimer();
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
 // V [B, S, Hkv, D] -> V^T [B, Hkv, D, S] (32 x 32 tiles through shared memory)
 __global__ void transpose_v_kernel(uint16_t* __restrict__ vt, const uint16_t* __restrict__ v, int S, int Hkv) {
   __shared__ uint16_t tile[32][34];
@@ -440,7 +775,38 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
   if (!attr) {
     cuda_check(cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                "attention smem attribute");
+    cuda_check(cudaFuncSetAttribute(attention_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "attention smem attribute");
     attr = true;
+  }
+  if ((S / 128) % 2 == 0 && !getenv("FOPT_ATTN_ONE_TILE")) {
+    const int64_t blocks = (int64_t)B * Hq * (S / 256);
+    const char* trace_path = getenv("FOPT_ATTN_TRACE");
+    if (trace_path) {
+      cuda_check(cudaMallocAsync((void**)&p.trace, blocks * 40 * 8, ctx->stream), "trace alloc");
+      cuda_check(cudaMemsetAsync(p.trace, 0, blocks * 40 * 8, ctx->stream), "trace clear");
+    }
+    CUtensorMap mo = map3(o, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 32);
+    attention_tc2_kernel<<<(unsigned)blocks, THREADS2, smem, ctx->stream>>>(mq, mk, mv, mo, p);
+    launched(ctx, "attention_tc2");
+    if (trace_path) {  // diagnostics only: one line per CTA, stamps in ns from the earliest entry
+      std::vector<uint64_t> t((size_t)blocks * 40);
+      cuda_check(cudaMemcpyAsync(t.data(), p.trace, t.size() * 8, cudaMemcpyDeviceToHost, ctx->stream), "trace copy");
+      cuda_check(cudaStreamSynchronize(ctx->stream), "trace sync");
+      cudaFreeAsync(p.trace, ctx->stream);
+      uint64_t t0 = ~0ull;
+      for (int64_t c = 0; c < blocks; ++c) t0 = std::min(t0, t[c * 40]);
+      if (FILE* f = fopen(trace_path, "a")) {
+        fprintf(f, "# blocks=%lld S=%d\n", (long long)blocks, S);
+        for (int64_t c = 0; c < blocks; ++c) {
+          fprintf(f, "%lld", (long long)c);
+          for (int k = 0; k < 40; ++k) fprintf(f, " %lld", t[c * 40 + k] ? (long long)(t[c * 40 + k] - t0) : -1LL);
+          fprintf(f, "\n");
+        }
+        fclose(f);
+      }
+    }
+    return true;
   }
   const int64_t blocks = (int64_t)B * Hq * (S / 128);
   attention_tc_kernel<<<(unsigned)blocks, THREADS, smem, ctx->stream>>>(mq, mk, mv, p);

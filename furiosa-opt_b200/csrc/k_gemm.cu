@@ -55,20 +55,33 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// The same test, but a thread whose phase has not completed sleeps until it does (or for at most
+// the hint, 20 us) instead of returning at once: waiting warps then leave the issue slots to the
+// warps doing work.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(20000)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait: returns false (and raises the shared abort flag) after ~kWaitNs.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                                           int code) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try(bar, parity)) return true;
-    if ((it & 255) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitNs) {
-        *abort_flag = 1;
-        atomicExch(err, code);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_sleep(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitNs) {
+      *abort_flag = 1;
+      atomicExch(err, code);
+      return false;
     }
   }
 }
@@ -300,17 +313,12 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col
     uint32_t packed[16];
 #pragma unroll
     for (int j = 0; j < 32; j += 2) {
-      uint32_t lo, hi;
-      if (relu) {
-        uint32_t a = rr[j], b = rr[j + 1];
-        bool na = (a & 0x7fffffffu) > 0x7f800000u, nb = (b & 0x7fffffffu) > 0x7f800000u;
-        lo = (!na && (a >> 31)) ? 0u : f32_to_bf16w(a);
-        hi = (!nb && (b >> 31)) ? 0u : f32_to_bf16w(b);
-      } else {
-        lo = f32_to_bf16w(rr[j]);
-        hi = f32_to_bf16w(rr[j + 1]);
+      uint32_t a = rr[j], b = rr[j + 1];
+      if (relu) {  // commit_cast_relu: negative non-NaN values become +0
+        if ((a & 0x7fffffffu) <= 0x7f800000u && (a >> 31)) a = 0u;
+        if ((b & 0x7fffffffu) <= 0x7f800000u && (b >> 31)) b = 0u;
       }
-      packed[j / 2] = (lo >> 16) | (hi & 0xffff0000u);
+      packed[j / 2] = bf16x2_rule(__uint_as_float(a), __uint_as_float(b));
     }
     uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 2);
 #pragma unroll
