@@ -421,15 +421,18 @@ def test_gather_rejects_negative_index(b200):
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 4, 2, True), (1, 200, 8, 2, True), (1, 96, 2, 2, False),
-                                               (1, 512, 8, 2, True), (2, 384, 4, 1, True), (2, 256, 4, 4, False)])
-def test_attention_parity(b200, B, S, Hq, Hkv, causal):
-    """S % 128 == 0 runs the tcgen05 kernel (multi-block online softmax, GQA, batches); other S the
-    CUDA-core kernel."""
-    D = 128
-    q = rand_vals("bf16", B * S * Hq * D)
-    k = rand_vals("bf16", B * S * Hkv * D)
-    v = rand_vals("bf16", B * S * Hkv * D)
+@pytest.fixture(params=["paired", "one_tile"])
+def attn_kernel(request, monkeypatch):
+    """S % 256 == 0 runs the two-query-tile tcgen05 kernel, or with FOPT_ATTN_ONE_TILE the one-tile
+    kernel (which also serves odd block counts)."""
+    if request.param == "one_tile":
+        monkeypatch.setenv("FOPT_ATTN_ONE_TILE", "1")
+    else:
+        monkeypatch.delenv("FOPT_ATTN_ONE_TILE", raising=False)
+    return request.param
+
+
+def _attention_check(b200, q, k, v, B, S, Hq, Hkv, causal, D=128):
     mq = fb.Mapping("[B, S, H, D]", dict(B=B, S=S, H=Hq, D=D))
     mk = fb.Mapping("[B, S, H, D]", dict(B=B, S=S, H=Hkv, D=D))
     o = b200.attention(b200.from_vec(mq, q, "bf16"), b200.from_vec(mk, k, "bf16"), b200.from_vec(mk, v, "bf16"), B, S,
@@ -439,6 +442,31 @@ def test_attention_parity(b200, B, S, Hq, Hkv, causal):
     err = np.abs(g - w)
     # bf16 output: 2 bf16 ulps of the value plus 1e-2 absolute (f32 softmax, different sum order)
     assert np.all(err <= 2 ** -7 * np.abs(w) + 1e-2), f"max abs err {err.max()}"
+
+
+def test_attention_growing_scores(b200, attn_kernel):
+    """Keys whose magnitude grows along the sequence, so a row's running max keeps rising by more
+    than 2^8 between key blocks: every rescaling path of the online softmax runs."""
+    B, S, Hq, Hkv, D = 1, 1024, 4, 2, 128
+    rng = np.random.default_rng(21)
+    q = dtypes.f32_to_bf16_bits(rng.standard_normal(B * S * Hq * D).astype(np.float32))
+    grow = (1.0 + np.arange(S, dtype=np.float32) / 32.0)[None, :, None, None]
+    k = dtypes.f32_to_bf16_bits((rng.standard_normal((B, S, Hkv, D)).astype(np.float32) * grow).reshape(-1))
+    v = dtypes.f32_to_bf16_bits(rng.standard_normal(B * S * Hkv * D).astype(np.float32))
+    _attention_check(b200, q, k, v, B, S, Hq, Hkv, True)
+
+
+@pytest.mark.parametrize("B,S,Hq,Hkv,causal", [(1, 128, 4, 2, True), (1, 200, 8, 2, True), (1, 96, 2, 2, False),
+                                               (1, 512, 8, 2, True), (2, 384, 4, 1, True), (2, 256, 4, 4, False),
+                                               (1, 1024, 8, 2, False)])
+def test_attention_parity(b200, attn_kernel, B, S, Hq, Hkv, causal):
+    """S % 128 == 0 runs a tcgen05 kernel (multi-block online softmax, GQA, batches); other S the
+    CUDA-core kernel."""
+    D = 128
+    q = rand_vals("bf16", B * S * Hq * D)
+    k = rand_vals("bf16", B * S * Hkv * D)
+    v = rand_vals("bf16", B * S * Hkv * D)
+    _attention_check(b200, q, k, v, B, S, Hq, Hkv, causal, D)
 
 
 @pytest.fixture(params=["pair256", "pair128", "single"])
