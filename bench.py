@@ -100,6 +100,14 @@ class Clocks:
 # ---------------------------------------------------------------------------------------------
 # workloads: each returns a dict with step(), per-step units, and metadata
 # ---------------------------------------------------------------------------------------------
+# DRAM bytes per launch of the step's dominant kernel, read + write, from one ncu capture of this
+# workload (the summaries under profiles/ give the command); None where no capture was taken.
+TRAFFIC = {
+    "gemm_i8_4096x4096x4096": (33.6e6, "profiles/gemm_tc_i8_4096.md"),
+    "attention_s2048": (25.2e6, "profiles/attention_tc2_s2048.md"),
+}
+
+
 def wl_gemm(fb, be, dtype: str, M=4096, N=4096, K=4096):
     rng = np.random.default_rng(42)
     ax = dict(M=M, N=N, K=K)
@@ -367,6 +375,9 @@ def run_ours(args, rank, world, local):
             peak, src = pk["bf16_tflops"], f"{pk['src']} bf16 cuBLAS burst"
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 3), "traffic": None, "peak_src": src}
+    tr = TRAFFIC.get(wl["workload"])
+    if tr:
+        roof["traffic"], roof["traffic_unit"], roof["traffic_src"] = tr[0], "bytes per launch (ncu)", tr[1]
     line = {"metric": wl["metric"], "value": round(value, 2), "unit": wl["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic (seeded)",
