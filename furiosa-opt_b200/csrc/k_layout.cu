@@ -148,6 +148,74 @@ __global__ void __launch_bounds__(256) relayout_tile(T* __restrict__ dst, const 
   }
 }
 
+// Tile path on 32-bit words (E = 4 / sizeof(T) elements per word; the launcher uses it for 1-byte
+// elements). A
+// tile is 32 E x 32 E elements: 128-byte rows on both sides. An E x E element block moves as E
+// words: a lane loads one word from each of E consecutive source rows (a warp instruction reads a
+// whole 128-byte line), transposes the block in registers with byte permutes, and stores the E
+// words into the transposed shared tile. The shared column is XOR-swizzled by the block's source
+// word (word a of tile row c sits at column a ^ (c / E)), so the stores and the row reads both hit
+// 32 distinct banks; each warp then writes whole 128-byte dst lines. Tile base pointers are formed
+// once per tile in 64 bits; in-tile offsets stay 32-bit.
+template <int E>
+__device__ __forceinline__ void transpose_block(const uint32_t* r, uint32_t* o) {
+  if constexpr (E == 1) {
+    o[0] = r[0];
+  } else if constexpr (E == 2) {
+    o[0] = __byte_perm(r[0], r[1], 0x5410);
+    o[1] = __byte_perm(r[0], r[1], 0x7632);
+  } else {
+    const uint32_t t0 = __byte_perm(r[0], r[1], 0x5140), t1 = __byte_perm(r[0], r[1], 0x7362);
+    const uint32_t t2 = __byte_perm(r[2], r[3], 0x5140), t3 = __byte_perm(r[2], r[3], 0x7362);
+    o[0] = __byte_perm(t0, t2, 0x5410);
+    o[1] = __byte_perm(t0, t2, 0x7632);
+    o[2] = __byte_perm(t1, t3, 0x5410);
+    o[3] = __byte_perm(t1, t3, 0x7632);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) relayout_tile_w(T* __restrict__ dst, const T* __restrict__ src, KWalk others,
+                                                       int64_t e0, int64_t s0, int64_t ej, int64_t wj,
+                                                       int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
+                                                       int64_t batches) {
+  constexpr int E = 4 / (int)sizeof(T), TT = 32 * E;
+  __shared__ uint32_t tile[TT][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
+    const int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
+    int64_t off[2] = {0, 0};
+    const bool live = walk_offsets<2>(others, b, off);
+    // rows / columns of this tile that exist (extents are multiples of E)
+    const int64_t r0 = e0 - ti * TT, rj = ej - tj * TT;
+    const int n0 = r0 < TT ? (int)r0 : TT, nj = rj < TT ? (int)rj : TT;
+    if (live) {
+      const T* sT = src + src_base + off[0] + ti * TT * s0 + tj * TT;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int a = warp + 8 * q;  // source rows E a .. E a + E - 1 of the tile
+        uint32_t r[E], o[E];
+#pragma unroll
+        for (int i = 0; i < E; ++i) r[i] = 0;
+        if (E * a < n0 && E * lane < nj) {
+#pragma unroll
+          for (int i = 0; i < E; ++i) r[i] = *(const uint32_t*)(sT + (int64_t)(E * a + i) * s0 + E * lane);
+        }
+        transpose_block<E>(r, o);
+#pragma unroll
+        for (int k = 0; k < E; ++k) tile[E * lane + k][a ^ lane] = o[k];
+      }
+    }
+    __syncthreads();
+    if (live && E * lane < n0) {
+      T* dT = dst + dst_base + off[1] + ti * TT + tj * TT * wj + E * lane;
+#pragma unroll 4
+      for (int c = warp; c < nj; c += 8) *(uint32_t*)(dT + (int64_t)c * wj) = tile[c][lane ^ (c / E)];
+    }
+    __syncthreads();
+  }
+}
+
 // ---- walk path ----
 template <typename T>
 __global__ void relayout_walk32(T* __restrict__ dst, const T* __restrict__ src, KWalk32 w, uint32_t positions,
@@ -185,6 +253,70 @@ __global__ void relayout_rows(T* __restrict__ dst, const T* __restrict__ src, KW
       const int64_t si = sb + (int64_t)d * st0;
       if (si < src_elems) dst[db + d] = src[si];
     }
+  }
+}
+
+// Rows path, vectorised: one thread per 16-byte dst vector of a row whose innermost wheel is only
+// partly live (e.g. a padded width). The dst row pitch is a whole number of vectors, so every
+// vector lies in one row; fully live vectors gather their V elements and store once, the vector
+// that straddles the live width reads the dst first so that the dead slots keep their contents
+// (the reference skips them), and fully dead vectors are not touched.
+template <typename T>
+__global__ void relayout_rows_vec(T* __restrict__ dst, const T* __restrict__ src, KWalk32 outer, FastDiv lvec_div,
+                                  uint32_t total, uint32_t e0, uint32_t l0, int32_t st0, int64_t src_base,
+                                  int64_t dst_base, int64_t src_elems, int64_t src_bytes) {
+  constexpr int V = 16 / sizeof(T);
+  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const uint32_t row = fdiv(lvec_div, t);
+    const uint32_t c0 = (t - row * lvec_div.d) * V;
+    int32_t off = 0;
+    if (!walk_offsets32<1>(outer, row, &off)) continue;
+    const int64_t sb = src_base + off + (int64_t)c0 * st0;
+    uint4* dp = (uint4*)(dst + dst_base + (int64_t)row * e0 + c0);
+    uint4 w;
+    T* e = (T*)&w;
+    if (c0 + V <= l0 && st0 == 1 && sb >= 0 && (sb * (int64_t)sizeof(T) & ~(int64_t)15) + 32 <= src_bytes) {
+      // contiguous source window at any element alignment: two aligned 16-byte loads and a
+      // funnel shift by the window's byte offset
+      const int64_t byte = sb * (int64_t)sizeof(T);
+      const uint4* a = (const uint4*)((const uint8_t*)src + (byte & ~(int64_t)15));
+      const uint4 lo = a[0], hi = a[1];
+      const uint32_t x[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      const int o = (int)(byte & 15), ow = o >> 2, sh = (o & 3) * 8;
+      uint32_t r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t w0 = x[0], w1 = x[1];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (ow == q) {
+            w0 = x[i + q];
+            w1 = x[i + q + 1];
+          }
+        r[i] = __funnelshift_r(w0, w1, sh);
+      }
+      w = make_uint4(r[0], r[1], r[2], r[3]);
+    } else if (c0 + V <= l0) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int64_t si = sb + (int64_t)k * st0;
+        e[k] = si < src_elems ? src[si] : T(0);
+      }
+      if (sb + (int64_t)(V - 1) * st0 >= src_elems) {  // rare: the window runs past the source
+        const uint4 old = *dp;
+#pragma unroll
+        for (int k = 0; k < V; ++k)
+          if (sb + (int64_t)k * st0 >= src_elems) e[k] = ((const T*)&old)[k];
+      }
+    } else {
+      w = *dp;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int64_t si = sb + (int64_t)k * st0;
+        if (c0 + k < l0 && si < src_elems) e[k] = src[si];
+      }
+    }
+    *dp = w;
   }
 }
 
@@ -317,6 +449,25 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
     int64_t nt0 = (w.extent[0] + TT - 1) / TT, ntj = (w.extent[j] + TT - 1) / TT;
     int64_t blocks = nt0 * ntj * batches;
     int grid = (int)std::min<int64_t>(blocks, (1ll << 31) - 1);  // one tile per block
+    // word tiles: element counts, strides and bases that keep every word aligned
+    // (1-byte elements only: for 2- and 4-byte elements the 64 x 64 and 32 x 32 element word tiles are
+    // too small, and the vector tile below is faster: 61 vs 84 us and 103 vs 178 us at 8192^2)
+    constexpr int EW = sizeof(T) == 1 ? 4 : 0;
+    bool words = EW > 0 && w.extent[0] % EW == 0 && w.extent[j] % EW == 0 && w.stride[0][0] % EW == 0 &&
+                 src_base % EW == 0 && dst_base % EW == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0 &&
+                 !getenv("FOPT_RELAYOUT_NO_WORDTILE");
+    for (int k = 0; words && k < others.n; ++k) words = others.stride[0][k] % EW == 0;
+    if constexpr (sizeof(T) <= 4) {
+      if (words) {
+        constexpr int TW = 32 * (4 / (int)sizeof(T));
+        const int64_t n0 = (w.extent[0] + TW - 1) / TW, nj = (w.extent[j] + TW - 1) / TW;
+        const int gw = (int)std::min<int64_t>(n0 * nj * batches, (1ll << 31) - 1);
+        relayout_tile_w<T><<<gw, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj, src_base,
+                                               dst_base, n0, nj, batches);
+        launched(ctx, "relayout_tile_w");
+        return;
+      }
+    }
     if (wide)
       relayout_tile<T, VW, TTW><<<grid, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
                                                        src_base, dst_base, nt0, ntj, batches);
@@ -337,6 +488,17 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
       outer.stride[0][i - 1] = w32.stride[0][i];
     }
     const int64_t rows = p.positions / w.extent[0];
+    constexpr int V = 16 / sizeof(T);
+    const int64_t lvec = (w.live[0] + V - 1) / V;
+    if (sizeof(T) <= 4 && w.extent[0] % V == 0 && dst_base % V == 0 && (uintptr_t)d % 16 == 0 &&
+        rows * lvec < (1ll << 31) && !getenv("FOPT_RELAYOUT_NO_ROWVEC")) {
+      relayout_rows_vec<T><<<grid_for(rows * lvec), kThreads, 0, st>>>(
+          d, s, outer, make_fastdiv((uint32_t)lvec), (uint32_t)(rows * lvec), (uint32_t)w.extent[0],
+          (uint32_t)w.live[0], (int32_t)w.stride[0][0], src_base, dst_base, src_elems,
+          (uintptr_t)s % 16 == 0 ? src_elems * (int64_t)sizeof(T) : 0);
+      launched(ctx, "relayout_rows_vec");
+      return;
+    }
     relayout_rows<T><<<grid_for(rows * 32), kThreads, 0, st>>>(d, s, outer, (uint32_t)rows, (uint32_t)w.extent[0],
                                                                  (uint32_t)w.live[0], (int32_t)w.stride[0][0],
                                                                  src_base, dst_base, src_elems);

@@ -109,9 +109,15 @@ RELAYOUTS = [
     ("[R, C]", "[C, R]", dict(R=512, C=384), False),
     ("[A, B, C]", "[C, A, B]", dict(A=3, B=5, C=7), False),
     ("[A, B, C]", "[B, A, C]", dict(A=16, B=24, C=64), False),
+    ("[A, B, C]", "[A, C, B]", dict(A=3, B=36, C=20), False),  # batched tiles, extents not multiples of 128
     ("[A]", "[B, A # 6]", dict(A=4, B=3), True),
     ("[C, D]", "[C, D # 64]", dict(C=13, D=61), False),
     ("[C, D # 64]", "[D, C]", dict(C=13, D=61), False),
+    # partly live destination rows (vectorised rows path): live widths not a multiple of the vector,
+    # permuted outer wheels, a strided innermost source wheel
+    ("[C, D]", "[C, D # 48]", dict(C=37, D=33), False),
+    ("[A, B, D]", "[B, A, D # 32]", dict(A=5, B=7, D=29), False),
+    ("[D, C]", "[C, D # 32]", dict(C=9, D=20), False),
     ("[B]", "[B / 64, B % 32, B / 32 % 2]", dict(B=512), False),
     ("[A, B]", "[A / 4, B, A % 4]", dict(A=16, B=12), False),
     ("[H, X]", "[X / 8, H, X % 8]", dict(H=10, X=64), False),
