@@ -13,6 +13,7 @@ Closures become opcodes: `map` / `zip_with` / `zip3_with` / `reduce` take a prog
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import Optional, Sequence
 
 import numpy as np
@@ -74,17 +75,38 @@ def m(expr: str, **axes) -> Mapping:
 
 
 class Storage:
-    """`B200::Storage<D>`: one owned device allocation holding the packed image of `n` elements."""
+    """`B200::Storage<D>`: one owned device allocation holding the packed image of `n` elements.
 
-    def __init__(self, backend: "B200", dtype: str, n: int, zero: bool = True):
+    A storage made by `B200.relayout` as a plain broadcast (one value per row, or one row repeated)
+    is lazy: it holds only the small source until something needs its bytes. Elementwise ops read
+    the source directly with the broadcast index; any other use (its device pointer) writes the
+    broadcast out first, so the observable image is always the relayout's."""
+
+    def __init__(self, backend: "B200", dtype: str, n: int, zero: bool = True, lazy=None):
         self.backend = backend
         self.dtype = dtype
         self.n = n
         self.nbytes = dtypes.nbytes(dtype, n)
+        self._ptr = C.c_void_p()
+        self.lazy = lazy  # (src Storage, Src Mapping, Dst Mapping, bcast code for fopt_elementwise_bcast)
+        if lazy is None:
+            self._alloc(zero)
+
+    def _alloc(self, zero: bool):
         p = C.c_void_p()
         alloc = _lib.lib().fopt_alloc if zero else _lib.lib().fopt_alloc_uninit
-        check(alloc(backend.ctx, self.nbytes, C.byref(p)), backend.ctx)
-        self.ptr = p
+        check(alloc(self.backend.ctx, self.nbytes, C.byref(p)), self.backend.ctx)
+        self._ptr = p
+
+    @property
+    def ptr(self) -> C.c_void_p:
+        if self.lazy is not None:
+            src, Src, Dst, _ = self.lazy
+            self._alloc(True)
+            self.lazy = None
+            check(_lib.lib().fopt_transpose(self.backend.ctx, self._ptr, src.ptr, _lib.DTYPES[src.dtype], Src.handle,
+                                            Dst.handle, 0, 0, 1), self.backend.ctx)
+        return self._ptr
 
     @property
     def addr(self) -> int:
@@ -115,9 +137,9 @@ class Storage:
 
     def __del__(self):
         try:
-            if self.ptr:
-                _lib.lib().fopt_free(self.backend.ctx, self.ptr)
-                self.ptr = C.c_void_p()
+            if self._ptr:
+                _lib.lib().fopt_free(self.backend.ctx, self._ptr)
+                self._ptr = C.c_void_p()
         except Exception:
             pass
 
@@ -140,6 +162,8 @@ class B200:
         check(_lib.lib().fopt_init(device, C.byref(ctx)))
         self.ctx = ctx
         self.device = device
+        # write broadcasts out at relayout time instead of reading them lazily (for comparison)
+        self.eager_broadcast = bool(os.environ.get("FOPT_EAGER_BROADCAST"))
 
     # ---- lifecycle (backend/mod.rs:45-90) ----
     def from_vec(self, mapping: Mapping, data, dtype: str) -> Storage:
@@ -183,8 +207,18 @@ class B200:
             if s.n != n:
                 raise ValueError("zip: operands must have the same element count")
         out = Storage(self, out_dtype, n, zero=dtypes.BITS[out_dtype] == 4)
-        ptrs = (C.c_void_p * len(inputs))(*[s.addr for s in inputs])
         dts = (C.c_int * len(inputs))(*[_lib.DTYPES[s.dtype] for s in inputs])
+        if any(s.lazy is not None for s in inputs):
+            # read lazy broadcasts from their sources; write them out only if no generated kernel applies
+            bc = (C.c_int64 * len(inputs))(*[s.lazy[3] if s.lazy is not None else 0 for s in inputs])
+            ptrs = (C.c_void_p * len(inputs))(*[(s.lazy[0] if s.lazy is not None else s).addr for s in inputs])
+            st = _lib.lib().fopt_elementwise_bcast(self.ctx, C.byref(prog), len(inputs), ptrs, dts, bc, out.ptr,
+                                                   _lib.DTYPES[out_dtype], n)
+            if st == 0:
+                return out
+            if st != _lib.FOPT_ERR_UNSUPPORTED:
+                check(st, self.ctx)
+        ptrs = (C.c_void_p * len(inputs))(*[s.addr for s in inputs])
         check(_lib.lib().fopt_elementwise(self.ctx, C.byref(prog), len(inputs), ptrs, dts, out.ptr,
                                           _lib.DTYPES[out_dtype], n), self.ctx)
         return out
@@ -210,7 +244,14 @@ class B200:
                                         src_base, dst_base, int(allow_broadcast)), self.ctx)
 
     def relayout(self, src: Storage, Src: Mapping, Dst: Mapping, allow_broadcast: bool = False) -> Storage:
-        """A fresh Dst-laid-out copy (`Tensor::transpose(true)` on a zeroed destination)."""
+        """A fresh Dst-laid-out copy (`Tensor::transpose(true)` on a zeroed destination). A plain
+        broadcast of a byte-multiple type comes back lazy (see `Storage`)."""
+        if allow_broadcast and dtypes.BITS[src.dtype] >= 8 and not self.eager_broadcast:
+            kind, inner = C.c_int32(), C.c_int64()
+            check(_lib.lib().fopt_broadcast_kind(Src.handle, Dst.handle, C.byref(kind), C.byref(inner)), None)
+            if kind.value and inner.value % 8 == 0:
+                code = inner.value if kind.value == 1 else -inner.value
+                return Storage(self, src.dtype, Dst.size, lazy=(src, Src, Dst, code))
         dst = Storage(self, src.dtype, Dst.size)
         self.transpose(dst, src, Src, Dst, allow_broadcast=allow_broadcast)
         return dst

@@ -374,6 +374,51 @@ fopt_status fopt_elementwise(fopt_ctx* ctx, const fopt_program* prog, int32_t n_
   });
 }
 
+fopt_status fopt_elementwise_bcast(fopt_ctx* ctx, const fopt_program* prog, int32_t n_in, const void* const* inputs,
+                                   const fopt_dtype* in_dtypes, const int64_t* bcast, void* out, fopt_dtype out_dtype,
+                                   int64_t n) {
+  fopt_status st = FOPT_OK;
+  bool ran = false;
+  st = guarded(ctx, [&] {
+    require(prog && out && bcast && n_in >= 0 && n_in <= 3, "fopt_elementwise_bcast: bad arguments");
+    require(prog->n_insn >= 0 && prog->n_insn <= 32, "fopt_elementwise_bcast: program too long");
+    for (int i = 0; i < n_in; ++i) require(inputs[i] != nullptr, "fopt_elementwise_bcast: null input");
+    ran = launch_elementwise_jit_ex(ctx, prog, n_in, inputs, in_dtypes, bcast, out, out_dtype, n);
+  });
+  if (st == FOPT_OK && !ran) {
+    ctx->err = "fopt_elementwise_bcast: no generated kernel for these operands";
+    return FOPT_ERR_UNSUPPORTED;
+  }
+  return st;
+}
+
+fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst, int32_t* kind, int64_t* inner) {
+  try {
+    require(src && dst && kind && inner, "fopt_broadcast_kind: null argument");
+    *kind = 0;
+    *inner = 0;
+    Walk w;
+    auto u = unify({&src->m, &dst->m});
+    if (!plan_relayout(u[0], u[1], true, w) || w.wheels.size() != 2) return FOPT_OK;
+    const Wheel &a = w.wheels[0], &b = w.wheels[1];
+    if (a.live != a.extent || b.live != b.extent) return FOPT_OK;
+    if (a.stride[0] == 0 && b.stride[0] == 1 && src->m.size() == b.extent) {
+      *kind = 1;  // dst[i] = src[i / inner]
+      *inner = a.extent;
+    } else if (a.stride[0] == 1 && b.stride[0] == 0 && src->m.size() == a.extent) {
+      *kind = 2;  // dst[i] = src[i % inner]
+      *inner = a.extent;
+    }
+    return FOPT_OK;
+  } catch (const Fail& f) {
+    g_noctx_err = f.msg;
+    return f.code;
+  } catch (const std::exception& e) {
+    g_noctx_err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}
+
 // ---- reduce ----
 fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype, fopt_reduce_op op,
                         uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,

@@ -94,17 +94,17 @@ Jit& jit() {
 }
 
 // ---- code generation ----
-std::string load_vec(int k, int dt) {
+std::string load_vec(int k, int dt, const std::string& idx = "base") {
   std::ostringstream o;
   const std::string in = "in" + std::to_string(k), x = "x" + std::to_string(k);
   switch (dtype_bits(dt)) {
     case 32:
-      o << "{ const uint4* q = (const uint4*)" << in << " + (base >> 2); uint4 u0 = q[0], u1 = q[1]; " << x
+      o << "{ const uint4* q = (const uint4*)" << in << " + ((" << idx << ") >> 2); uint4 u0 = q[0], u1 = q[1]; " << x
         << "[0]=u0.x; " << x << "[1]=u0.y; " << x << "[2]=u0.z; " << x << "[3]=u0.w; " << x << "[4]=u1.x; " << x
         << "[5]=u1.y; " << x << "[6]=u1.z; " << x << "[7]=u1.w; }\n";
       break;
     case 16:
-      o << "{ uint4 u = *((const uint4*)" << in << " + (base >> 3)); const unsigned h[4] = {u.x, u.y, u.z, u.w};\n"
+      o << "{ uint4 u = *((const uint4*)" << in << " + ((" << idx << ") >> 3)); const unsigned h[4] = {u.x, u.y, u.z, u.w};\n"
         << "  for (int j = 0; j < 4; ++j) { ";
       if (dt == FOPT_BF16)
         o << x << "[2*j] = h[j] << 16; " << x << "[2*j+1] = h[j] & 0xffff0000u; }";
@@ -114,7 +114,7 @@ std::string load_vec(int k, int dt) {
       break;
     default: {
       const bool sgn = dt == FOPT_I8 || dt == FOPT_I5;
-      o << "{ uint2 u = *((const uint2*)" << in << " + (base >> 3)); const unsigned h[2] = {u.x, u.y};\n"
+      o << "{ uint2 u = *((const uint2*)" << in << " + ((" << idx << ") >> 3)); const unsigned h[2] = {u.x, u.y};\n"
         << "  for (int j = 0; j < 8; ++j) { unsigned b = (h[j >> 2] >> (8 * (j & 3))) & 0xffu; " << x << "[j] = "
         << (sgn ? "(unsigned)(int)(signed char)b" : "b") << "; } }\n";
     }
@@ -177,21 +177,35 @@ int arity_of(int op) {
 
 }  // namespace
 // Returns "" when the program uses an opcode the table lacks (the interpreter then runs it).
-std::string generate(const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt) {
+// modes[k]: 0 input k is read at the element index i, 1 at i / b_k (a per-row value broadcast along
+// rows of b_k elements), 2 at i % b_k (a row of b_k values repeated); b_k is a multiple of 8, so an
+// 8-element group never straddles a row.
+std::string generate(const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt, const int* modes) {
   std::ostringstream o;
   o << kPrelude << "\nusing namespace fopt::ew;\n"
     << "extern \"C\" __global__ void __launch_bounds__(256) fopt_ew_gen(const void* __restrict__ in0, "
-       "const void* __restrict__ in1, const void* __restrict__ in2, void* __restrict__ out, long long n) {\n"
+       "const void* __restrict__ in1, const void* __restrict__ in2, void* __restrict__ out, long long n, "
+       "long long b0, long long b1, long long b2) {\n"
     << "  const long long stride = (long long)gridDim.x * blockDim.x * 8;\n"
     << "  for (long long base = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8; base < n; base += stride) {\n"
     << "    unsigned x0[8], x1[8], x2[8], r[8];\n"
     << "    const bool full = base + 8 <= n;\n"
     << "    if (full) {\n";
-  for (int k = 0; k < n_in; ++k) o << "      " << load_vec(k, in_dt[k]);
+  for (int k = 0; k < n_in; ++k) {
+    const std::string bk = "b" + std::to_string(k), xk = "x" + std::to_string(k);
+    if (modes[k] == 1)
+      o << "      { const unsigned v = " << load_one(k, in_dt[k], "base / " + bk) << "; for (int e = 0; e < 8; ++e) " << xk
+        << "[e] = v; }\n";
+    else
+      o << "      " << load_vec(k, in_dt[k], modes[k] == 2 ? "base % " + bk : "base");
+  }
   o << "    } else {\n";
-  for (int k = 0; k < n_in; ++k)
-    o << "      for (int e = 0; e < 8; ++e) x" << k << "[e] = base + e < n ? " << load_one(k, in_dt[k], "base + e")
+  for (int k = 0; k < n_in; ++k) {
+    const std::string bk = "b" + std::to_string(k);
+    const std::string idx = modes[k] == 1 ? "(base + e) / " + bk : modes[k] == 2 ? "(base + e) % " + bk : "base + e";
+    o << "      for (int e = 0; e < 8; ++e) x" << k << "[e] = base + e < n ? " << load_one(k, in_dt[k], idx)
       << " : 0u;\n";
+  }
   o << "    }\n#pragma unroll\n    for (int e = 0; e < 8; ++e) {\n";
   std::string name[16];
   for (int v = 0; v < 16; ++v) name[v] = "0u";
@@ -224,18 +238,19 @@ struct Entry {
 std::mutex g_mu;
 std::map<std::string, Entry> g_cache;
 
-CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt) {
+CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt,
+                      const int* modes) {
   Jit& j = jit();
   if (!j.ok) return nullptr;
   std::string key((const char*)&p, sizeof(int32_t) * 2 + sizeof(fopt_insn) * p.n_insn);
   key += std::to_string(ctx->device) + ":" + std::to_string(out_dt);
-  for (int k = 0; k < n_in; ++k) key += "," + std::to_string(in_dt[k]);
+  for (int k = 0; k < n_in; ++k) key += "," + std::to_string(in_dt[k]) + "/" + std::to_string(modes[k]);
   std::lock_guard<std::mutex> g(g_mu);
   auto it = g_cache.find(key);
   if (it != g_cache.end()) return it->second.failed ? nullptr : it->second.fn;
   Entry& e = g_cache[key];
   e.failed = true;
-  std::string src = generate(p, n_in, in_dt, out_dt);
+  std::string src = generate(p, n_in, in_dt, out_dt, modes);
   if (src.empty()) return nullptr;
   nvrtcProgram prog;
   if (j.create(&prog, src.c_str(), "fopt_ew_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return nullptr;
@@ -270,20 +285,31 @@ CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt
 
 std::atomic<int64_t> g_jit_launches{0};
 
-// Runs the program as a generated kernel; false when that path does not apply.
-bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
-                            const fopt_dtype* in_dt, void* out, fopt_dtype out_dt, int64_t n) {
+// Runs the program as a generated kernel; false when that path does not apply. bcast (optional):
+// per input 0 (read at i), > 0 (read at i / bcast[k]) or < 0 (read at i % -bcast[k]).
+bool launch_elementwise_jit_ex(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
+                               const fopt_dtype* in_dt, const int64_t* bcast, void* out, fopt_dtype out_dt, int64_t n) {
   if (getenv("FOPT_EW_NO_JIT")) return false;
   if (dtype_bits(out_dt) < 8 || (uintptr_t)out % 16) return false;
-  for (int k = 0; k < n_in; ++k)
+  int modes[3] = {0, 0, 0};
+  long long inner[3] = {1, 1, 1};
+  for (int k = 0; k < n_in; ++k) {
     if (dtype_bits(in_dt[k]) < 8 || (uintptr_t)in[k] % 16) return false;
-  CUfunction fn = kernel_for(ctx, *prog, n_in, in_dt, out_dt);
+    if (bcast && bcast[k]) {
+      const int64_t b = bcast[k] > 0 ? bcast[k] : -bcast[k];
+      if (b % 8 || n % b) return false;
+      modes[k] = bcast[k] > 0 ? 1 : 2;
+      inner[k] = b;
+    }
+  }
+  CUfunction fn = kernel_for(ctx, *prog, n_in, in_dt, out_dt, modes);
   if (!fn) return false;
   const void* a0 = n_in > 0 ? in[0] : out;
   const void* a1 = n_in > 1 ? in[1] : a0;
   const void* a2 = n_in > 2 ? in[2] : a0;
   long long nn = n;
-  void* args[] = {(void*)&a0, (void*)&a1, (void*)&a2, (void*)&out, (void*)&nn};
+  void* args[] = {(void*)&a0, (void*)&a1, (void*)&a2, (void*)&out, (void*)&nn, (void*)&inner[0], (void*)&inner[1],
+                  (void*)&inner[2]};
   const int64_t threads = (n + 7) / 8;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((threads + 255) / 256, 148 * 16));
   CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, args, nullptr);
@@ -293,6 +319,11 @@ bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, c
   return true;
 }
 
+bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
+                            const fopt_dtype* in_dt, void* out, fopt_dtype out_dt, int64_t n) {
+  return launch_elementwise_jit_ex(ctx, prog, n_in, in, in_dt, nullptr, out, out_dt, n);
+}
+
 }  // namespace fopt
 
 extern "C" int64_t fopt_elementwise_jit_launches(void) { return fopt::g_jit_launches.load(); }
@@ -300,7 +331,8 @@ extern "C" int64_t fopt_elementwise_jit_launches(void) { return fopt::g_jit_laun
 extern "C" fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
                                                fopt_dtype out_dtype, char* buf, size_t len, size_t* needed) {
   if (!prog || n_in < 0 || n_in > 3) return FOPT_ERR_INVALID;
-  std::string src = fopt::generate(*prog, n_in, in_dtypes, out_dtype);
+  const int modes[3] = {0, 0, 0};
+  std::string src = fopt::generate(*prog, n_in, in_dtypes, out_dtype, modes);
   if (src.empty()) return FOPT_ERR_UNSUPPORTED;
   if (needed) *needed = src.size() + 1;
   if (buf && len) {

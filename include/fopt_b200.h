@@ -172,6 +172,18 @@ typedef struct {
 
 fopt_status fopt_elementwise(fopt_ctx* ctx, const fopt_program* prog, int32_t n_in, const void* const* inputs,
                              const fopt_dtype* in_dtypes, void* out, fopt_dtype out_dtype, int64_t n);
+/* fopt_elementwise where an input is a broadcast that was never written out: bcast[k] = 0 reads
+ * input k at the element index i, bcast[k] > 0 at i / bcast[k] (one value per row of bcast[k]
+ * elements), bcast[k] < 0 at i % -bcast[k] (one row of -bcast[k] values repeated). Row lengths must be
+ * multiples of 8 and divide n. Returns FOPT_ERR_UNSUPPORTED when no generated kernel applies (NVRTC
+ * absent, 4-bit types, misalignment); the caller then materialises the broadcast and calls
+ * fopt_elementwise. Same results as materialising first. */
+fopt_status fopt_elementwise_bcast(fopt_ctx* ctx, const fopt_program* prog, int32_t n_in, const void* const* inputs,
+                                   const fopt_dtype* in_dtypes, const int64_t* bcast, void* out, fopt_dtype out_dtype,
+                                   int64_t n);
+/* Whether relayouting src into dst with broadcasting is a plain row broadcast (*kind = 1: dst[i] =
+ * src[i / *inner]) or a repeated row (*kind = 2: dst[i] = src[i % *inner]); *kind = 0 otherwise. */
+fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst, int32_t* kind, int64_t* inner);
 /* Diagnostic: the CUDA source of the kernel fopt_elementwise generates (NVRTC, sm_100a) for this
  * program and these dtypes (byte-multiple types). *needed = bytes including the terminator. */
 fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,

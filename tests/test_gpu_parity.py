@@ -236,6 +236,38 @@ def test_elementwise_exact(b200, ew_path, case):
         assert got == want
 
 
+@pytest.mark.parametrize("path", ["generated", "interpreter"])
+def test_lazy_broadcast_elementwise(b200, monkeypatch, path):
+    """A broadcast made by relayout stays unwritten when only elementwise ops read it: a per-row
+    value ([T] -> [T, W]) and a repeated row ([W] -> [T, W]) read through the broadcast index give
+    the same bits as the written-out broadcast; without generated kernels the broadcast is written
+    out first, with the same result; and its bytes, when asked for, are the relayout's."""
+    if path == "interpreter":
+        monkeypatch.setenv("FOPT_EW_NO_JIT", "1")
+    else:
+        monkeypatch.delenv("FOPT_EW_NO_JIT", raising=False)
+    T, W = 24, 72
+    ax = dict(T=T, W=W)
+    big, rows, cols = fb.Mapping("[T, W]", ax), fb.Mapping("[T]", ax), fb.Mapping("[W]", ax)
+    x = rand_vals("f32", T * W)
+    r = rand_vals("f32", T)
+    c = rand_vals("f32", W)
+    X = b200.from_vec(big, x, "f32")
+    R = b200.relayout(b200.from_vec(rows, r, "f32"), rows, big, allow_broadcast=True)
+    Cb = b200.relayout(b200.from_vec(cols, c, "f32"), cols, big, allow_broadcast=True)
+    assert R.lazy is not None and Cb.lazy is not None
+    got = b200.zip3_with(X, R, Cb, ops.fp_ternary("FmaF"), "f32").to_numpy().reshape(T, W)
+    # FmaF(a, b, c) = fma(a, b, c) on the written-out operands
+    want = np.frombuffer(oracle.elementwise([(34, 3, 0, 1, 2, 0)], 3, [x.tobytes(), np.repeat(r, W).tobytes(),
+                                                                      np.tile(c, T).tobytes()],
+                                            ["f32", "f32", "f32"], "f32", T * W), np.float32).reshape(T, W)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    if path == "generated":
+        assert R.lazy is not None and Cb.lazy is not None  # read through, never written out
+    assert np.array_equal(R.to_numpy().reshape(T, W), np.repeat(r, W).reshape(T, W))
+    assert np.array_equal(Cb.to_numpy().reshape(T, W), np.tile(c, T).reshape(T, W))
+
+
 @pytest.mark.parametrize("n", [1, 7, 8, 9, 4096 * 37 + 3])
 @pytest.mark.parametrize("case", [0, 1, 3, 4])
 def test_elementwise_sizes(b200, ew_path, case, n):
