@@ -69,8 +69,13 @@ SIGNATURES = [
     ("fopt_elementwise_source", _I32, [C.POINTER(Program), _I32, C.POINTER(C.c_int), C.c_int, C.c_char_p, _SZ,
                                        C.POINTER(_SZ)]),
     ("fopt_elementwise_jit_launches", C.c_int64, []),
+    ("fopt_reduce_map_source", _I32, [C.POINTER(Program), _I32, C.POINTER(C.c_int), _I32, C.c_char_p, _SZ,
+                                      C.POINTER(_SZ)]),
     ("fopt_elementwise_bcast", _I32, [C.c_void_p, C.POINTER(Program), _I32, C.POINTER(C.c_void_p), C.POINTER(C.c_int),
                                       C.POINTER(C.c_int64), C.c_void_p, C.c_int, C.c_int64]),
+    ("fopt_reduce_map", _I32, [C.c_void_p, C.c_void_p, C.POINTER(Program), _I32, C.POINTER(C.c_void_p),
+                               C.POINTER(C.c_int), C.POINTER(C.c_int64), C.c_int, C.c_int, C.c_uint32, C.c_void_p,
+                               C.c_void_p]),
     ("fopt_broadcast_kind", _I32, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int64)]),
     ("fopt_reduce", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_reduce_noalloc", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),

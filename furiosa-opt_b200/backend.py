@@ -14,6 +14,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 from typing import Optional, Sequence
 
 import numpy as np
@@ -88,9 +89,27 @@ class Storage:
         self.n = n
         self.nbytes = dtypes.nbytes(dtype, n)
         self._ptr = C.c_void_p()
-        self.lazy = lazy  # (src Storage, Src Mapping, Dst Mapping, bcast code for fopt_elementwise_bcast)
+        # lazy: ("bcast", src Storage, Src Mapping, Dst Mapping, bcast code of fopt_elementwise_bcast)
+        #    or ("ew", program, leaf inputs): values not yet written (leaves may be lazy broadcasts)
+        self.lazy = lazy
+        self._dependents = weakref.WeakSet()  # lazy storages that read this one
         if lazy is None:
             self._alloc(zero)
+        else:
+            for src in self._lazy_sources():
+                src._dependents.add(self)
+
+    def _lazy_sources(self):
+        if self.lazy is None:
+            return []
+        return [self.lazy[1]] if self.lazy[0] == "bcast" else list(self.lazy[2])
+
+    def _will_write(self) -> None:
+        """Called before anything writes into this storage in place: lazy storages that read it
+        take their values now."""
+        for d in list(self._dependents):
+            d.ptr  # noqa: B018 (materialises)
+        self._dependents = weakref.WeakSet()
 
     def _alloc(self, zero: bool):
         p = C.c_void_p()
@@ -101,11 +120,16 @@ class Storage:
     @property
     def ptr(self) -> C.c_void_p:
         if self.lazy is not None:
-            src, Src, Dst, _ = self.lazy
-            self._alloc(True)
-            self.lazy = None
-            check(_lib.lib().fopt_transpose(self.backend.ctx, self._ptr, src.ptr, _lib.DTYPES[src.dtype], Src.handle,
-                                            Dst.handle, 0, 0, 1), self.backend.ctx)
+            lazy, self.lazy = self.lazy, None
+            if lazy[0] == "bcast":
+                _, src, Src, Dst, _ = lazy
+                self._alloc(True)
+                check(_lib.lib().fopt_transpose(self.backend.ctx, self._ptr, src.ptr, _lib.DTYPES[src.dtype],
+                                                Src.handle, Dst.handle, 0, 0, 1), self.backend.ctx)
+            else:
+                _, prog, leaves = lazy
+                self._alloc(dtypes.BITS[self.dtype] == 4)
+                self.backend._run_ew(prog, leaves, self)
         return self._ptr
 
     @property
@@ -134,6 +158,8 @@ class Storage:
 
     def __len__(self):
         return self.n
+
+    __hash__ = object.__hash__  # identity: storages are tracked in sets of dependents
 
     def __del__(self):
         try:
@@ -164,6 +190,8 @@ class B200:
         self.device = device
         # write broadcasts out at relayout time instead of reading them lazily (for comparison)
         self.eager_broadcast = bool(os.environ.get("FOPT_EAGER_BROADCAST"))
+        # engine-chain fusion of elementwise results (off: every op writes its result)
+        self.fuse = not os.environ.get("FOPT_NO_FUSION")
 
     # ---- lifecycle (backend/mod.rs:45-90) ----
     def from_vec(self, mapping: Mapping, data, dtype: str) -> Storage:
@@ -201,27 +229,90 @@ class B200:
         return int(_lib.lib().fopt_launch_count(self.ctx))
 
     # ---- elementwise (backend/mod.rs:92-116) ----
+    # Elementwise results of f32 / i32 type are deferred (engine-chain fusion): a deferred storage
+    # keeps its program and leaf inputs; an elementwise consumer composes the program into its own,
+    # a fused row reduction (`reduce`) folds the values without writing them, and any other use
+    # writes them out first. Leaf inputs are ordinary storages or lazy broadcasts.
+    DEFER = ("f32", "i32")
+
+    @staticmethod
+    def _leaf_args(leaves):
+        """ctypes arrays (pointers, dtypes, bcast codes) for leaf inputs: a still-lazy broadcast is
+        passed as its source with its code, anything else as itself."""
+        srcs, codes = [], []
+        for s in leaves:
+            if s.lazy is not None and s.lazy[0] == "bcast":
+                srcs.append(s.lazy[1])
+                codes.append(s.lazy[4])
+            else:
+                srcs.append(s)
+                codes.append(0)
+        ptrs = (C.c_void_p * len(leaves))(*[s.addr for s in srcs])
+        dts = (C.c_int * len(leaves))(*[_lib.DTYPES[s.dtype] for s in leaves])
+        return ptrs, dts, (C.c_int64 * len(leaves))(*codes), any(codes)
+
+    def _compose(self, prog, inputs: Sequence[Storage]):
+        """Returns (program, leaves) with deferred elementwise inputs folded in, or None when the
+        result would need more than 3 leaves, 32 instructions or 16 registers."""
+        leaves, keymap = [], {}
+
+        def leaf_reg(st):
+            if id(st) not in keymap:
+                keymap[id(st)] = len(leaves)
+                leaves.append(st)
+            return keymap[id(st)]
+
+        parts = []  # per consumer input: ("leaf", reg) or ("prog", program, [leaf regs])
+        for s in inputs:
+            if s.lazy is not None and s.lazy[0] == "ew":
+                _, q, qleaves = s.lazy
+                parts.append(("prog", q, [leaf_reg(l) for l in qleaves]))
+            else:
+                parts.append(("leaf", leaf_reg(s)))
+        if len(leaves) > 3:
+            return None
+        out = ops.Prog(len(leaves))
+        regs = []
+        try:
+            for part in parts:
+                regs.append(part[1] if part[0] == "leaf" else ops.inline(out, part[1], part[2]))
+            return out.build(ops.inline(out, prog, regs)), leaves
+        except ValueError:
+            return None
+
+    def _run_ew(self, prog, leaves, out: Storage) -> None:
+        ptrs, dts, codes, any_bcast = self._leaf_args(leaves)
+        if any_bcast:
+            st = _lib.lib().fopt_elementwise_bcast(self.ctx, C.byref(prog), len(leaves), ptrs, dts, codes, out._ptr,
+                                                   _lib.DTYPES[out.dtype], out.n)
+            if st == 0:
+                return
+            if st != _lib.FOPT_ERR_UNSUPPORTED:
+                check(st, self.ctx)
+            ptrs = (C.c_void_p * len(leaves))(*[s.addr for s in leaves])  # writes the broadcasts out
+        check(_lib.lib().fopt_elementwise(self.ctx, C.byref(prog), len(leaves), ptrs, dts, out._ptr,
+                                          _lib.DTYPES[out.dtype], out.n), self.ctx)
+
     def _ew(self, prog, inputs: Sequence[Storage], out_dtype: str) -> Storage:
         n = inputs[0].n
         for s in inputs:
             if s.n != n:
                 raise ValueError("zip: operands must have the same element count")
+        composed = self._compose(prog, inputs)
+        if composed is None:  # evaluate the deferred inputs and run on their values
+            composed = self._compose(prog, [self._force(s) if s.lazy is not None and s.lazy[0] == "ew" else s
+                                            for s in inputs])
+        cprog, leaves = composed
+        if self.fuse and out_dtype in self.DEFER:
+            return Storage(self, out_dtype, n, lazy=("ew", cprog, leaves))
         out = Storage(self, out_dtype, n, zero=dtypes.BITS[out_dtype] == 4)
-        dts = (C.c_int * len(inputs))(*[_lib.DTYPES[s.dtype] for s in inputs])
-        if any(s.lazy is not None for s in inputs):
-            # read lazy broadcasts from their sources; write them out only if no generated kernel applies
-            bc = (C.c_int64 * len(inputs))(*[s.lazy[3] if s.lazy is not None else 0 for s in inputs])
-            ptrs = (C.c_void_p * len(inputs))(*[(s.lazy[0] if s.lazy is not None else s).addr for s in inputs])
-            st = _lib.lib().fopt_elementwise_bcast(self.ctx, C.byref(prog), len(inputs), ptrs, dts, bc, out.ptr,
-                                                   _lib.DTYPES[out_dtype], n)
-            if st == 0:
-                return out
-            if st != _lib.FOPT_ERR_UNSUPPORTED:
-                check(st, self.ctx)
-        ptrs = (C.c_void_p * len(inputs))(*[s.addr for s in inputs])
-        check(_lib.lib().fopt_elementwise(self.ctx, C.byref(prog), len(inputs), ptrs, dts, out.ptr,
-                                          _lib.DTYPES[out_dtype], n), self.ctx)
+        self._run_ew(cprog, leaves, out)
         return out
+
+    @staticmethod
+    def _force(s: Storage) -> Storage:
+        s.ptr  # noqa: B018 (materialises)
+        return s
 
     def map(self, src: Storage, prog, out_dtype: str) -> Storage:
         return self._ew(prog, [src], out_dtype)
@@ -240,6 +331,7 @@ class B200:
             raise ValueError("transpose: dtype mismatch")
         src_base = (src_map or Src).window_base(src_offset) if src_offset else 0
         dst_base = (dst_map or Dst).window_base(dst_offset) if dst_offset else 0
+        dst._will_write()
         check(_lib.lib().fopt_transpose(self.ctx, dst.ptr, src.ptr, _lib.DTYPES[src.dtype], Src.handle, Dst.handle,
                                         src_base, dst_base, int(allow_broadcast)), self.ctx)
 
@@ -251,7 +343,7 @@ class B200:
             check(_lib.lib().fopt_broadcast_kind(Src.handle, Dst.handle, C.byref(kind), C.byref(inner)), None)
             if kind.value and inner.value % 8 == 0:
                 code = inner.value if kind.value == 1 else -inner.value
-                return Storage(self, src.dtype, Dst.size, lazy=(src, Src, Dst, code))
+                return Storage(self, src.dtype, Dst.size, lazy=("bcast", src, Src, Dst, code))
         dst = Storage(self, src.dtype, Dst.size)
         self.transpose(dst, src, Src, Dst, allow_broadcast=allow_broadcast)
         return dst
@@ -284,6 +376,15 @@ class B200:
             bits = int(np.uint32(dtypes.f32_to_bf16_bits(np.float32(identity))) << 16)
         else:
             bits = int(np.float32(identity).view(np.uint32))
+        if src.lazy is not None and src.lazy[0] == "ew" and not allow_broadcast:
+            _, prog, leaves = src.lazy
+            ptrs, dts, codes, _ = self._leaf_args(leaves)
+            st = _lib.lib().fopt_reduce_map(self.ctx, out.ptr, C.byref(prog), len(leaves), ptrs, dts, codes,
+                                            _lib.DTYPES[src.dtype], REDUCE_OPS[op], bits, Src.handle, Dst.handle)
+            if st == 0:
+                return out
+            if st != _lib.FOPT_ERR_UNSUPPORTED:
+                check(st, self.ctx)
         check(_lib.lib().fopt_reduce(self.ctx, out.ptr, src.ptr, _lib.DTYPES[src.dtype], REDUCE_OPS[op], bits,
                                      Src.handle, Dst.handle, int(allow_broadcast)), self.ctx)
         return out
@@ -294,6 +395,8 @@ class B200:
     def _contract(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, out_dtype, ep=None, out=None) -> Storage:
         if lhs.dtype != rhs.dtype:
             raise ValueError("contraction: operand dtypes differ")
+        if out is not None:
+            out._will_write()
         if out is None:
             out = Storage(self, out_dtype, out_map.size, zero=False)
         elif out.dtype != out_dtype or out.n != out_map.size:
@@ -334,11 +437,13 @@ class B200:
     # ---- gather / scatter (backend/mod.rs:159-206) ----
     def gather(self, src: Storage, dst: Storage, index: Storage, Src: Mapping, Dst: Mapping, payload: Mapping,
                axis: Mapping, Idx: Mapping, scaled: bool = False) -> None:
+        dst._will_write()
         check(_lib.lib().fopt_gather(self.ctx, dst.ptr, src.ptr, index.ptr, _lib.DTYPES[src.dtype], Src.handle,
                                      Dst.handle, payload.handle, axis.handle, Idx.handle, int(scaled)), self.ctx)
 
     def scatter(self, src: Storage, dst: Storage, index: Storage, Src: Mapping, Dst: Mapping, payload: Mapping,
                 key: Mapping, axis: Mapping, scaled: bool = False) -> None:
+        dst._will_write()
         check(_lib.lib().fopt_scatter(self.ctx, dst.ptr, src.ptr, index.ptr, _lib.DTYPES[src.dtype], Src.handle,
                                       Dst.handle, payload.handle, key.handle, axis.handle, int(scaled)), self.ctx)
 
@@ -347,6 +452,7 @@ class B200:
                   head_dim: int = 128, scale: Optional[float] = None, causal: bool = True,
                   eps: float = 6.25e-8, out=None) -> Storage:
         o = out if out is not None else Storage(self, "bf16", q.n, zero=False)
+        o._will_write()
         sc = scale if scale is not None else head_dim ** -0.5
         check(_lib.lib().fopt_attention(self.ctx, o.ptr, q.ptr, k.ptr, v.ptr, batch, seq, hq, hkv, head_dim,
                                         C.c_float(sc), int(causal), C.c_float(eps)), self.ctx)

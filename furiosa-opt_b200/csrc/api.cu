@@ -420,30 +420,71 @@ fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst
 }
 
 // ---- reduce ----
+static std::shared_ptr<FoldKPlan> reduce_plan(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                              int allow_broadcast) {
+  std::string key = "r|" + src_map->key + "|" + dst_map->key + "|" + std::to_string(allow_broadcast);
+  {
+    std::lock_guard<std::mutex> g(ctx->mu);
+    auto it = ctx->folds.find(key);
+    if (it != ctx->folds.end()) return it->second;
+  }
+  FoldPlan fp;
+  auto u = unify({&src_map->m, &dst_map->m});
+  if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
+    throw Fail{FOPT_ERR_UNSUPPORTED, "reduce: mappings are not affine-factorisable"};
+  auto kp = std::make_shared<FoldKPlan>(to_kfold(fp));
+  std::lock_guard<std::mutex> g(ctx->mu);
+  ctx->folds[key] = kp;
+  return kp;
+}
+
 fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype, fopt_reduce_op op,
                         uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                         int allow_broadcast) {
   return guarded(ctx, [&] {
     require(out && src && src_map && dst_map, "fopt_reduce: null argument");
     require(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16, "fopt_reduce: dtype must be i32, f32 or bf16");
-    std::string key = "r|" + src_map->key + "|" + dst_map->key + "|" + std::to_string(allow_broadcast);
-    std::shared_ptr<FoldKPlan> kp;
-    {
-      std::lock_guard<std::mutex> g(ctx->mu);
-      auto it = ctx->folds.find(key);
-      if (it != ctx->folds.end()) kp = it->second;
-    }
-    if (!kp) {
-      FoldPlan fp;
-      auto u = unify({&src_map->m, &dst_map->m});
-      if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
-        throw Fail{FOPT_ERR_UNSUPPORTED, "reduce: mappings are not affine-factorisable"};
-      kp = std::make_shared<FoldKPlan>(to_kfold(fp));
-      std::lock_guard<std::mutex> g(ctx->mu);
-      ctx->folds[key] = kp;
-    }
+    auto kp = reduce_plan(ctx, src_map, dst_map, allow_broadcast);
     launch_reduce(ctx, *kp, out, src, dtype, op, identity_bits, src_map->m.size());
   });
+}
+
+fopt_status fopt_reduce_map(fopt_ctx* ctx, void* out, const fopt_program* prog, int32_t n_in, const void* const* inputs,
+                            const fopt_dtype* in_dtypes, const int64_t* bcast, fopt_dtype dtype, fopt_reduce_op op,
+                            uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map) {
+  bool ran = false;
+  fopt_status st = guarded(ctx, [&] {
+    require(out && prog && src_map && dst_map && n_in >= 0 && n_in <= 3, "fopt_reduce_map: bad arguments");
+    require(prog->n_insn >= 0 && prog->n_insn <= 32, "fopt_reduce_map: program too long");
+    for (int i = 0; i < n_in; ++i) require(inputs[i] != nullptr, "fopt_reduce_map: null input");
+    // folds whose result does not depend on the order (or f32 sums outside exact-fold mode)
+    int fold = -1;
+    if (dtype == FOPT_F32) {
+      if (op == FOPT_RED_MAX) fold = 2;
+      else if (op == FOPT_RED_MIN) fold = 3;
+      else if (!ctx->exact_fold && op == FOPT_RED_ADD) fold = 0;
+      else if (!ctx->exact_fold && op == FOPT_RED_MUL) fold = 4;
+    } else if (dtype == FOPT_I32) {
+      if (op == FOPT_RED_ADD) fold = 10;
+      else if (op == FOPT_RED_MAX) fold = 12;
+      else if (op == FOPT_RED_MIN) fold = 13;
+    }
+    if (fold < 0) return;
+    // a plain row reduction: dst cell t folds src cells t * W .. t * W + W - 1
+    auto kp = reduce_plan(ctx, src_map, dst_map, 0);
+    const KWalk &o = kp->out, &r = kp->residue;
+    if (o.n != 1 || r.n != 1 || o.live[0] != o.extent[0] || r.live[0] != r.extent[0] || r.stride[0][0] != 1 ||
+        o.stride[0][0] != r.extent[0] || kp->out_positions != o.extent[0] ||
+        src_map->m.size() != o.extent[0] * r.extent[0])
+      return;
+    ran = launch_reduce_map_jit(ctx, prog, n_in, inputs, in_dtypes, bcast, fold, identity_bits, out, o.extent[0],
+                                r.extent[0]);
+  });
+  if (st == FOPT_OK && !ran) {
+    ctx->err = "fopt_reduce_map: no fused kernel for this reduction";
+    return FOPT_ERR_UNSUPPORTED;
+  }
+  return st;
 }
 
 // ---- contraction ----

@@ -89,6 +89,9 @@ void launch_relayout(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void
 void launch_transmute(fopt_ctx* ctx, const RankWalk& src, const RankWalk& dst, void* out, const void* in, int dtype);
 bool launch_elementwise_jit_ex(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                                const fopt_dtype* in_dt, const int64_t* bcast, void* out, fopt_dtype out_dt, int64_t n);
+bool launch_reduce_map_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
+                           const fopt_dtype* in_dt, const int64_t* bcast, int fold, uint32_t ident, void* out,
+                           int64_t rows, int64_t W);
 bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                             const fopt_dtype* in_dt, void* out, fopt_dtype out_dt, int64_t n);
 void launch_elementwise(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in, const fopt_dtype* in_dt,

@@ -175,6 +175,43 @@ int arity_of(int op) {
   }
 }
 
+// Emits the program's instructions for element e of inputs x0..x2 (one scoped block per
+// instruction, every value in a named register); *ret names the result. False for an opcode the
+// table lacks.
+bool emit_program(std::ostringstream& o, const fopt_program& p, int n_in, std::string* ret) {
+  std::string name[16];
+  for (int v = 0; v < 16; ++v) name[v] = "0u";
+  for (int k = 0; k < n_in; ++k) name[k] = "x" + std::to_string(k) + "[e]";
+  for (int i = 0; i < p.n_insn; ++i) {
+    const fopt_insn& in = p.insn[i];
+    const char* expr = op_expr(in.op);
+    if (!expr) return false;
+    const int ar = arity_of(in.op);
+    const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
+                      C = ar > 2 ? name[in.c & 15] : "0u";
+    const std::string t = "t" + std::to_string(i);
+    o << "      unsigned " << t << "; { const unsigned a = " << A << ", b = " << B << ", c = " << C
+      << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
+      << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << " = ("
+      << expr << "); }\n";
+    name[in.dst & 15] = t;
+  }
+  *ret = name[p.ret & 15];
+  return true;
+}
+
+// Loads the 8 elements at `base` of every input into x0..x2 (modes as for generate below).
+void emit_loads(std::ostringstream& o, int n_in, const fopt_dtype* in_dt, const int* modes) {
+  for (int k = 0; k < n_in; ++k) {
+    const std::string bk = "b" + std::to_string(k), xk = "x" + std::to_string(k);
+    if (modes[k] == 1)
+      o << "      { const unsigned v = " << load_one(k, in_dt[k], "base / " + bk) << "; for (int e = 0; e < 8; ++e) " << xk
+        << "[e] = v; }\n";
+    else
+      o << "      " << load_vec(k, in_dt[k], modes[k] == 2 ? "base % " + bk : "base");
+  }
+}
+
 }  // namespace
 // Returns "" when the program uses an opcode the table lacks (the interpreter then runs it).
 // modes[k]: 0 input k is read at the element index i, 1 at i / b_k (a per-row value broadcast along
@@ -191,14 +228,7 @@ std::string generate(const fopt_program& p, int n_in, const fopt_dtype* in_dt, i
     << "    unsigned x0[8], x1[8], x2[8], r[8];\n"
     << "    const bool full = base + 8 <= n;\n"
     << "    if (full) {\n";
-  for (int k = 0; k < n_in; ++k) {
-    const std::string bk = "b" + std::to_string(k), xk = "x" + std::to_string(k);
-    if (modes[k] == 1)
-      o << "      { const unsigned v = " << load_one(k, in_dt[k], "base / " + bk) << "; for (int e = 0; e < 8; ++e) " << xk
-        << "[e] = v; }\n";
-    else
-      o << "      " << load_vec(k, in_dt[k], modes[k] == 2 ? "base % " + bk : "base");
-  }
+  emit_loads(o, n_in, in_dt, modes);
   o << "    } else {\n";
   for (int k = 0; k < n_in; ++k) {
     const std::string bk = "b" + std::to_string(k);
@@ -207,24 +237,9 @@ std::string generate(const fopt_program& p, int n_in, const fopt_dtype* in_dt, i
       << " : 0u;\n";
   }
   o << "    }\n#pragma unroll\n    for (int e = 0; e < 8; ++e) {\n";
-  std::string name[16];
-  for (int v = 0; v < 16; ++v) name[v] = "0u";
-  for (int k = 0; k < n_in; ++k) name[k] = "x" + std::to_string(k) + "[e]";
-  for (int i = 0; i < p.n_insn; ++i) {
-    const fopt_insn& in = p.insn[i];
-    const char* expr = op_expr(in.op);
-    if (!expr) return "";
-    const int ar = arity_of(in.op);
-    const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
-                      C = ar > 2 ? name[in.c & 15] : "0u";
-    const std::string t = "t" + std::to_string(i);
-    o << "      unsigned " << t << "; { const unsigned a = " << A << ", b = " << B << ", c = " << C
-      << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
-      << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << " = ("
-      << expr << "); }\n";
-    name[in.dst & 15] = t;
-  }
-  o << "      r[e] = " << name[p.ret & 15] << ";\n    }\n"
+  std::string ret;
+  if (!emit_program(o, p, n_in, &ret)) return "";
+  o << "      r[e] = " << ret << ";\n    }\n"
     << "    if (full) " << store_vec(out_dt) << "    else for (int e = 0; e < 8; ++e) if (base + e < n) "
     << store_one(out_dt, "base + e", "r[e]") << "\n  }\n}\n";
   return o.str();
@@ -238,22 +253,20 @@ struct Entry {
 std::mutex g_mu;
 std::map<std::string, Entry> g_cache;
 
-CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt,
-                      const int* modes) {
+// Compiles (once per key) the source that make_src returns and fetches its kernel `entry`.
+template <typename MakeSrc>
+CUfunction compiled(const std::string& key, MakeSrc make_src, const char* entry) {
   Jit& j = jit();
   if (!j.ok) return nullptr;
-  std::string key((const char*)&p, sizeof(int32_t) * 2 + sizeof(fopt_insn) * p.n_insn);
-  key += std::to_string(ctx->device) + ":" + std::to_string(out_dt);
-  for (int k = 0; k < n_in; ++k) key += "," + std::to_string(in_dt[k]) + "/" + std::to_string(modes[k]);
   std::lock_guard<std::mutex> g(g_mu);
   auto it = g_cache.find(key);
   if (it != g_cache.end()) return it->second.failed ? nullptr : it->second.fn;
   Entry& e = g_cache[key];
   e.failed = true;
-  std::string src = generate(p, n_in, in_dt, out_dt, modes);
+  std::string src = make_src();
   if (src.empty()) return nullptr;
   nvrtcProgram prog;
-  if (j.create(&prog, src.c_str(), "fopt_ew_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return nullptr;
+  if (j.create(&prog, src.c_str(), "fopt_gen.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS) return nullptr;
   const char* opts[] = {"--gpu-architecture=sm_100a", "--std=c++17", "--fmad=false"};
   nvrtcResult rc = j.compile(prog, 3, opts);
   if (rc != NVRTC_SUCCESS) {
@@ -262,7 +275,7 @@ CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt
       j.log_size(prog, &n);
       std::string logs(n, '\0');
       j.log(prog, &logs[0]);
-      fprintf(stderr, "fopt elementwise JIT failed:\n%s\n", logs.c_str());
+      fprintf(stderr, "fopt JIT failed:\n%s\n", logs.c_str());
     }
     j.destroy(&prog);
     return nullptr;
@@ -275,10 +288,62 @@ CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt
   CUmodule mod;
   if (j.load(&mod, bin.data()) != CUDA_SUCCESS) return nullptr;
   CUfunction fn;
-  if (j.get_fn(&fn, mod, "fopt_ew_gen") != CUDA_SUCCESS) return nullptr;
+  if (j.get_fn(&fn, mod, entry) != CUDA_SUCCESS) return nullptr;
   e.fn = fn;
   e.failed = false;
   return fn;
+}
+
+std::string program_key(const fopt_program& p, int n_in, const fopt_dtype* in_dt, const int* modes) {
+  std::string key((const char*)&p, sizeof(int32_t) * 2 + sizeof(fopt_insn) * p.n_insn);
+  for (int k = 0; k < n_in; ++k) key += "," + std::to_string(in_dt[k]) + "/" + std::to_string(modes[k]);
+  return key;
+}
+
+CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt_dtype* in_dt, int out_dt,
+                      const int* modes) {
+  const std::string key = "ew|" + program_key(p, n_in, in_dt, modes) + "|" + std::to_string(ctx->device) + ":" +
+                          std::to_string(out_dt);
+  return compiled(key, [&] { return generate(p, n_in, in_dt, out_dt, modes); }, "fopt_ew_gen");
+}
+
+// A row reduction of the program's values: one warp per row of W elements (W a multiple of 8),
+// lane-strided 8-element groups folded into a per-lane accumulator, then a butterfly across the
+// warp. fold: 0 f32 add, 2 max, 3 min, 4 f32 mul (f32 values), 10 i32 wrapping add, 12 / 13 i32
+// max / min.
+std::string generate_reduce(const fopt_program& p, int n_in, const fopt_dtype* in_dt, const int* modes, int fold) {
+  std::ostringstream o;
+  const char* f = nullptr;
+  switch (fold) {
+    case 0: f = "W(__fadd_rn(F(u), F(v)))"; break;
+    case 2: f = "W(fmaxf(F(u), F(v)))"; break;
+    case 3: f = "W(fminf(F(u), F(v)))"; break;
+    case 4: f = "W(__fmul_rn(F(u), F(v)))"; break;
+    case 10: f = "(u + v)"; break;
+    case 12: f = "(unsigned)max((int)u, (int)v)"; break;
+    case 13: f = "(unsigned)min((int)u, (int)v)"; break;
+    default: return "";
+  }
+  o << kPrelude << "\nusing namespace fopt::ew;\n"
+    << "__device__ __forceinline__ unsigned fold(unsigned u, unsigned v) { return " << f << "; }\n"
+    << "extern \"C\" __global__ void __launch_bounds__(256) fopt_red_gen(const void* __restrict__ in0, "
+       "const void* __restrict__ in1, const void* __restrict__ in2, unsigned* __restrict__ out, long long rows, "
+       "long long row_len, long long b0, long long b1, long long b2, unsigned ident) {\n"
+    << "  const int lane = threadIdx.x & 31;\n"
+    << "  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;\n"
+    << "  for (long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {\n"
+    << "    unsigned acc = ident;\n"
+    << "    for (long long c = 8 * lane; c < row_len; c += 256) {\n"
+    << "      const long long base = row * row_len + c;\n"
+    << "      unsigned x0[8], x1[8], x2[8];\n";
+  emit_loads(o, n_in, in_dt, modes);
+  o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) {\n";
+  std::string ret;
+  if (!emit_program(o, p, n_in, &ret)) return "";
+  o << "        acc = fold(acc, " << ret << ");\n      }\n    }\n"
+    << "#pragma unroll\n    for (int m = 16; m; m >>= 1) acc = fold(acc, __shfl_xor_sync(0xffffffffu, acc, m));\n"
+    << "    if (lane == 0) out[row] = acc;\n  }\n}\n";
+  return o.str();
 }
 
 }  // namespace
@@ -324,7 +389,60 @@ bool launch_elementwise_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, c
   return launch_elementwise_jit_ex(ctx, prog, n_in, in, in_dt, nullptr, out, out_dt, n);
 }
 
+// Row reduction of a program's values (see generate_reduce); false when the generated kernel does
+// not apply (no NVRTC, 4-bit types, misalignment, W not a multiple of 8).
+bool launch_reduce_map_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
+                           const fopt_dtype* in_dt, const int64_t* bcast, int fold, uint32_t ident, void* out,
+                           int64_t rows, int64_t W) {
+  if (getenv("FOPT_EW_NO_JIT")) return false;
+  if (W % 8 || (uintptr_t)out % 4) return false;
+  int modes[3] = {0, 0, 0};
+  long long inner[3] = {1, 1, 1};
+  for (int k = 0; k < n_in; ++k) {
+    if (dtype_bits(in_dt[k]) < 8 || (uintptr_t)in[k] % 16) return false;
+    if (bcast && bcast[k]) {
+      const int64_t b = bcast[k] > 0 ? bcast[k] : -bcast[k];
+      if (b % 8 || (rows * W) % b) return false;
+      modes[k] = bcast[k] > 0 ? 1 : 2;
+      inner[k] = b;
+    }
+  }
+  const std::string key = "red|" + std::to_string(fold) + "|" + program_key(*prog, n_in, in_dt, modes) + "|" +
+                          std::to_string(ctx->device);
+  CUfunction fn = compiled(key, [&] { return generate_reduce(*prog, n_in, in_dt, modes, fold); }, "fopt_red_gen");
+  if (!fn) return false;
+  const void* a0 = n_in > 0 ? in[0] : out;
+  const void* a1 = n_in > 1 ? in[1] : a0;
+  const void* a2 = n_in > 2 ? in[2] : a0;
+  long long rr = rows, ww = W;
+  unsigned id = ident;
+  void* args[] = {(void*)&a0, (void*)&a1, (void*)&a2, (void*)&out, (void*)&rr, (void*)&ww,
+                  (void*)&inner[0], (void*)&inner[1], (void*)&inner[2], (void*)&id};
+  const int64_t warps = rows;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((warps * 32 + 255) / 256, 148 * 16));
+  CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, args, nullptr);
+  if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "reduce kernel launch failed"};
+  ctx->launches++;
+  g_jit_launches.fetch_add(1, std::memory_order_relaxed);
+  return true;
+}
+
 }  // namespace fopt
+
+extern "C" fopt_status fopt_reduce_map_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
+                                              int32_t fold, char* buf, size_t len, size_t* needed) {
+  if (!prog || n_in < 0 || n_in > 3) return FOPT_ERR_INVALID;
+  const int modes[3] = {0, 0, 0};
+  std::string src = fopt::generate_reduce(*prog, n_in, in_dtypes, modes, fold);
+  if (src.empty()) return FOPT_ERR_UNSUPPORTED;
+  if (needed) *needed = src.size() + 1;
+  if (buf && len) {
+    size_t n = std::min(len - 1, src.size());
+    memcpy(buf, src.data(), n);
+    buf[n] = 0;
+  }
+  return FOPT_OK;
+}
 
 extern "C" int64_t fopt_elementwise_jit_launches(void) { return fopt::g_jit_launches.load(); }
 

@@ -52,9 +52,11 @@ def init_comm(backend, rank: int, world: int) -> None:
 
 def allreduce(backend, storage) -> None:
     """Sum over the Chip axis, result on every chip (reduce over `Chip` then broadcast), in place."""
+    storage._will_write()
     check(_lib.lib().fopt_allreduce(backend.ctx, storage.ptr, storage.n, _lib.DTYPES[storage.dtype]), backend.ctx)
 
 
 def chip_shuffle(backend, dst, src, pattern) -> None:
     arr = (C.c_int32 * len(pattern))(*pattern)
+    dst._will_write()
     check(_lib.lib().fopt_chip_shuffle(backend.ctx, dst.ptr, src.ptr, src.nbytes, arr, len(pattern)), backend.ctx)

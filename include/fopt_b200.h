@@ -188,6 +188,10 @@ fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst
  * program and these dtypes (byte-multiple types). *needed = bytes including the terminator. */
 fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
                                     fopt_dtype out_dtype, char* buf, size_t len, size_t* needed);
+/* Diagnostic: the CUDA source of the fused row reduction fopt_reduce_map generates (fold: 0 f32 add,
+ * 2 / 3 f32 max / min, 4 f32 mul, 10 i32 add, 12 / 13 i32 max / min). */
+fopt_status fopt_reduce_map_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes, int32_t fold,
+                                   char* buf, size_t len, size_t* needed);
 /* Diagnostic: how many fopt_elementwise calls (process-wide) ran as a generated kernel. */
 int64_t fopt_elementwise_jit_launches(void);
 
@@ -205,6 +209,16 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
                         uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                         int allow_broadcast);
 
+/* Engine-chain fusion of a map (or zip / zip3) followed by a reduce: reduces prog(inputs) -- the values
+ * fopt_elementwise (with fopt_elementwise_bcast's broadcast codes, bcast may be NULL) would write as
+ * `dtype` -- without writing them. Covers a plain row reduction (dst cell t folds src cells
+ * t W .. t W + W - 1, W a multiple of 8) with a fold whose result does not depend on the order:
+ * i32 Add / Max / Min, f32 Max / Min, and f32 Add / Mul outside exact-fold mode (which reassociate,
+ * as fopt_reduce does there). Returns FOPT_ERR_UNSUPPORTED otherwise; the caller then writes the
+ * values with fopt_elementwise and calls fopt_reduce. */
+fopt_status fopt_reduce_map(fopt_ctx* ctx, void* out, const fopt_program* prog, int32_t n_in, const void* const* inputs,
+                            const fopt_dtype* in_dtypes, const int64_t* bcast, fopt_dtype dtype, fopt_reduce_op op,
+                            uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map);
 /* Allocation-free reduce. No counterpart in the reference: it exists for callers that cannot let the
  * library call cudaMalloc / cudaFree (a host runtime that owns the whole device-memory budget through
  * its own allocator, or a latency-critical loop that cannot absorb the device synchronisation a

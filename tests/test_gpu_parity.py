@@ -268,6 +268,57 @@ def test_lazy_broadcast_elementwise(b200, monkeypatch, path):
     assert np.array_equal(Cb.to_numpy().reshape(T, W), np.tile(c, T).reshape(T, W))
 
 
+@pytest.mark.parametrize("op,ident", [("Add", 0.0), ("Max", float("-inf")), ("Min", float("inf"))])
+def test_fused_map_reduce(b200, monkeypatch, op, ident):
+    """Engine-chain fusion: a deferred map (here |x| * s with s a lazy per-row broadcast) folded by a
+    row reduction without being written matches writing it and reducing (bit-exact for Max / Min;
+    Add reassociates, within the n-eps bound of the non-exact reduce)."""
+    T, W = 96, 4096 + 256
+    ax = dict(T=T, W=W)
+    big, rows = fb.Mapping("[T, W]", ax), fb.Mapping("[T]", ax)
+    x = rand_vals("f32", T * W)
+    r = np.abs(rand_vals("f32", T)) + 0.5
+    p = ops.Prog(2)
+    prog = p.build(p.emit("MULF", p.emit("AND", 0, p.const_i32(0x7FFFFFFF)), 1))
+    X = b200.from_vec(big, x, "f32")
+    Rb = b200.relayout(b200.from_vec(rows, r, "f32"), rows, big, allow_broadcast=True)
+    lazy = b200.zip_with(X, Rb, prog, "f32")
+    assert lazy.lazy is not None
+    before = _lib.lib().fopt_elementwise_jit_launches()
+    got = b200.reduce(lazy, op, ident, big, rows).to_numpy()
+    assert _lib.lib().fopt_elementwise_jit_launches() == before + 1  # the fused kernel, nothing else
+    assert lazy.lazy is not None  # the mapped values were never written
+    vals = np.abs(x).reshape(T, W) * r[:, None]
+    if op == "Add":
+        want = vals.astype(np.float64).sum(1)
+        assert np.all(np.abs(got - want) <= 1e-5 * np.abs(vals).sum(1) + 1e-6)
+    else:
+        want = vals.max(1) if op == "Max" else vals.min(1)
+        assert np.array_equal(got, want.astype(np.float32))
+    # and the same values through the unfused path
+    monkeypatch.setenv("FOPT_NO_FUSION", "1")
+    be2 = fb.B200(0)
+    X2 = be2.from_vec(big, x, "f32")
+    R2 = be2.relayout(be2.from_vec(rows, r, "f32"), rows, big, allow_broadcast=True)
+    plain = be2.reduce(be2.zip_with(X2, R2, prog, "f32"), op, ident, big, rows).to_numpy()
+    if op != "Add":
+        assert np.array_equal(got, plain)
+
+
+def test_deferred_values_survive_inplace_writes(b200):
+    """A deferred elementwise value reads its inputs as they were when it was made: an in-place
+    write into an input first makes the deferred value take its values."""
+    ax = dict(N=4096)
+    m = fb.Mapping("[N]", ax)
+    x = rand_vals("f32", 4096)
+    X = b200.from_vec(m, x, "f32")
+    doubled = b200.zip_with(X, X, ops.fp_binary("AddF"), "f32")
+    assert doubled.lazy is not None
+    b200.transpose(X, b200.from_vec(m, np.zeros(4096, np.float32), "f32"), m, m)  # overwrite X in place
+    assert doubled.lazy is None
+    assert np.array_equal(doubled.to_numpy(), (x + x).astype(np.float32))
+
+
 @pytest.mark.parametrize("n", [1, 7, 8, 9, 4096 * 37 + 3])
 @pytest.mark.parametrize("case", [0, 1, 3, 4])
 def test_elementwise_sizes(b200, ew_path, case, n):

@@ -143,6 +143,41 @@ def _nvrtc():
     pytest.skip("NVRTC not available")
 
 
+def _nvrtc_compile(src: bytes):
+    import ctypes as C
+    nv = _nvrtc()
+    prog_h = C.c_void_p()
+    assert nv.nvrtcCreateProgram(C.byref(prog_h), src, b"t.cu", 0, None, None) == 0
+    opts = (C.c_char_p * 3)(b"--gpu-architecture=sm_100a", b"--std=c++17", b"--fmad=false")
+    rc = nv.nvrtcCompileProgram(prog_h, 3, opts)
+    if rc != 0:
+        n = C.c_size_t()
+        nv.nvrtcGetProgramLogSize(prog_h, C.byref(n))
+        log = C.create_string_buffer(n.value)
+        nv.nvrtcGetProgramLog(prog_h, log)
+        pytest.fail(log.value.decode()[-3000:])
+    nv.nvrtcDestroyProgram(C.byref(prog_h))
+
+
+@pytest.mark.parametrize("fold", [0, 2, 3, 4, 10, 12, 13])
+def test_generated_reduce_kernels_compile(fold):
+    """The fused map + row-reduce kernels fopt_reduce_map generates compile for sm_100a."""
+    import ctypes as C
+    from furiosa_opt_b200 import ops, workloads as W
+    if fold >= 10:
+        prog, ins = ops.fxp_binary("MulInt"), ["i32", "i8"]
+    else:
+        p = ops.Prog(3)
+        prog, ins = p.build(p.emit("MULF", p.emit("MULF", 0, 1), 2)), ["bf16", "f32", "f32"]
+    lib = _lib.lib()
+    dts = (C.c_int * 3)(*[_lib.DTYPES[d] for d in ins] + [0] * (3 - len(ins)))
+    need = C.c_size_t()
+    assert lib.fopt_reduce_map_source(C.byref(prog), len(ins), dts, fold, None, 0, C.byref(need)) == 0
+    buf = C.create_string_buffer(need.value)
+    assert lib.fopt_reduce_map_source(C.byref(prog), len(ins), dts, fold, buf, need.value, None) == 0
+    _nvrtc_compile(buf.value)
+
+
 @pytest.mark.parametrize("case", ["cast_bf16_f32", "requant", "swiglu", "quant", "zip3_select", "i16_shift"])
 def test_generated_elementwise_kernels_compile(case):
     """The kernels fopt_elementwise generates compile for sm_100a (NVRTC runs without a GPU)."""
@@ -177,3 +212,40 @@ def test_generated_elementwise_kernels_compile(case):
     size = C.c_size_t()
     assert nv.nvrtcGetCUBINSize(prog_h, C.byref(size)) == 0 and size.value > 0
     nv.nvrtcDestroyProgram(C.byref(prog_h))
+
+
+def _run(prog, ins, dts, out_dt):
+    import oracle
+    insns = [(prog.insn[i].op, prog.insn[i].dst, prog.insn[i].a, prog.insn[i].b, prog.insn[i].c, prog.insn[i].imm_i)
+             for i in range(prog.n_insn)]
+    n = len(ins[0]) // 4
+    return oracle.elementwise(insns, prog.ret, ins, dts, out_dt, n)
+
+
+def test_program_composition_matches_sequential_programs():
+    """Deferred elementwise values are evaluated inside their consumer's program (ops.inline + the
+    register reassignment in Prog.build): composed results are bit-identical to running the
+    producer, writing its f32 values and running the consumer."""
+    from furiosa_opt_b200 import ops, workloads as W
+    rng = np.random.default_rng(3)
+    g, u, s = (rng.standard_normal(4096).astype(np.float32) for _ in range(3))
+    s = np.abs(s) + 0.1
+    sw, q = W._prog_swiglu(), W._prog_quant()
+    act = _run(sw, [g.tobytes(), u.tobytes()], ["f32", "f32"], "f32")
+    want = _run(q, [act, s.tobytes()], ["f32", "f32"], "i8")
+    b = ops.Prog(3)
+    p = b.build(ops.inline(b, q, [ops.inline(b, sw, [0, 1]), 2]))
+    assert _run(p, [g.tobytes(), u.tobytes(), s.tobytes()], ["f32"] * 3, "i8") == want
+    # a chain of 20 dependent steps: needs the register reassignment (more than 16 handed out)
+    step = ops.Prog(1)
+    step = step.build(step.emit("MULF", step.emit("ADDF", 0, step.const_f32(0.5)), step.const_f32(0.75)))
+    b = ops.Prog(1)
+    r = 0
+    for _ in range(6):
+        r = ops.inline(b, step, [r])
+    chain = b.build(r)
+    assert chain.n_insn <= 32
+    ref = g.tobytes()
+    for _ in range(6):
+        ref = _run(step, [ref], ["f32"], "f32")
+    assert _run(chain, [g.tobytes()], ["f32"], "f32") == ref
