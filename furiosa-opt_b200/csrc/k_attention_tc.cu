@@ -183,6 +183,30 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Blackwell's three-input max and packed f32 pair arithmetic (two independent IEEE operations).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 // Two f32 -> packed bf16x2 with one round-to-nearest-even conversion instruction.
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
@@ -610,31 +634,39 @@ __global__ void __launch_bounds__(THREADS2, 1)
         for (int c = 0; c < 128; ++c)
           if (c > r) s[c] = __float_as_uint(-INFINITY);
       }
-      // row max and sum as 8 independent chains
+      // Row max with the three-input max (two new scores per instruction, 8 independent chains);
+      // scale-and-subtract and the running sums on packed f32 pairs (two independent
+      // round-to-nearest operations each, the same results as scalar fmaf / add).
       float mx8[8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) mx8[k] = __uint_as_float(s[k]);
+      for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(__uint_as_float(s[2 * k]), __uint_as_float(s[2 * k + 1]));
 #pragma unroll
-      for (int c = 8; c < 128; c += 8)
+      for (int c = 16; c < 128; c += 16)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) mx8[k] = fmaxf(mx8[k], __uint_as_float(s[c + k]));
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
+        for (int k = 0; k < 8; ++k) mx8[k] = max3f(mx8[k], __uint_as_float(s[c + 2 * k]), __uint_as_float(s[c + 2 * k + 1]));
+      const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])) *
+                       p.scale_log2;
       // Lazy rescaling: the exponent base m moves only when the block max exceeds it by more than
       // 8 (log2 units), so probabilities stay below 2^8 and O and l share one base; the normalised
       // result is unchanged and the O rescale below becomes rare.
       const float mnew = mx > m + 8.0f ? mx : m;
       const float alpha = ex2(m - mnew);
-      float sum8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), neg2 = pack_f32x2(-mnew, -mnew);
+      uint64_t sum2[4] = {0, 0, 0, 0};
       uint32_t* pk = s;  // packed bf16 pairs overwrite the scores in place (index c / 2 <= c)
 #pragma unroll
       for (int c = 0; c < 128; c += 2) {
-        const float p0 = ex2(fmaf(__uint_as_float(s[c]), p.scale_log2, -mnew));
-        const float p1 = ex2(fmaf(__uint_as_float(s[c + 1]), p.scale_log2, -mnew));
-        sum8[(c >> 1) & 7] += p0 + p1;
+        float x0, x1;
+        unpack_f32x2(fma_f32x2(pack_f32x2(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), scale2, neg2), x0, x1);
+        const float p0 = ex2(x0), p1 = ex2(x1);
+        const uint64_t pp = pack_f32x2(p0, p1);
+        sum2[(c >> 1) & 3] = add_f32x2(sum2[(c >> 1) & 3], pp);
         pk[c / 2] = pack_bf16x2(p0, p1);
       }
-      const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      float sa[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) unpack_f32x2(sum2[k], sa[2 * k], sa[2 * k + 1]);
+      const float sum = ((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7]));
       l = l * alpha + sum;
       m = mnew;
       // S_t(j) was issued after PV_t(j - 1) completed, so the O row is stable here
