@@ -76,6 +76,14 @@ SIGNATURES = [
     ("fopt_reduce_map", _I32, [C.c_void_p, C.c_void_p, C.POINTER(Program), _I32, C.POINTER(C.c_void_p),
                                C.POINTER(C.c_int), C.POINTER(C.c_int64), C.c_int, C.c_int, C.c_uint32, C.c_void_p,
                                C.c_void_p]),
+    ("fopt_st_open", _I32, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("fopt_st_close", _I32, [C.c_void_p]),
+    ("fopt_st_count", _I32, [C.c_void_p]),
+    ("fopt_st_info", _I32, [C.c_void_p, _I32, C.POINTER(C.c_char_p), C.POINTER(C.c_char_p), C.POINTER(C.c_int32),
+                            C.POINTER(C.c_int64), _I32, C.POINTER(C.c_int64)]),
+    ("fopt_st_find", _I32, [C.c_void_p, C.c_char_p, C.POINTER(C.c_int32)]),
+    ("fopt_st_read", _I32, [C.c_void_p, C.c_void_p, _I32, C.c_void_p, _SZ]),
+    ("fopt_mapping_flat_shape", _I32, [C.c_void_p, C.POINTER(C.c_int64), _I32, C.POINTER(C.c_int32)]),
     ("fopt_broadcast_kind", _I32, [C.c_void_p, C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int64)]),
     ("fopt_reduce", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_reduce_noalloc", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),

@@ -54,6 +54,12 @@ class Mapping:
         st = _lib.lib().fopt_mapping_eval(self._h, pos, buf, n)
         return st, {k: int(buf[i]) for i, k in enumerate(self.axes)}
 
+    def flat_shape(self) -> list:
+        """The pair-split sizes (`flat_shape`, tensor/memory.rs:201-209) a loaded tensor must have."""
+        dims, n = (C.c_int64 * 32)(), C.c_int32()
+        check(_lib.lib().fopt_mapping_flat_shape(self.handle, dims, 32, C.byref(n)))
+        return [dims[k] for k in range(min(n.value, 32))]
+
     def window_base(self, offset: dict) -> int:
         out = C.c_int64()
         check(_lib.lib().fopt_window_base(self._h, ", ".join(f"{k}:{v}" for k, v in offset.items()).encode(),
@@ -73,6 +79,55 @@ class Mapping:
 
 def m(expr: str, **axes) -> Mapping:
     return Mapping(expr, axes)
+
+
+ST_DTYPES = {"BF16": "bf16", "F32": "f32", "I8": "i8", "I16": "i16", "I32": "i32", "F8_E4M3": "f8e4m3",
+             "F8_E5M2": "f8e5m2"}
+
+
+class SafeTensors:
+    """An open safetensors file (header parsed natively; tensors stream to the device on demand)."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        check(_lib.lib().fopt_st_open(os.fsencode(path), C.byref(h)))
+        self.handle = h
+        self.path = path
+
+    def __len__(self):
+        return _lib.lib().fopt_st_count(self.handle)
+
+    def info(self, index: int):
+        name, dt, nd, nb = C.c_char_p(), C.c_char_p(), C.c_int32(), C.c_int64()
+        shape = (C.c_int64 * 16)()
+        check(_lib.lib().fopt_st_info(self.handle, index, C.byref(name), C.byref(dt), C.byref(nd), shape, 16,
+                                      C.byref(nb)))
+        return name.value.decode(), dt.value.decode(), [shape[k] for k in range(nd.value)], nb.value
+
+    def names(self):
+        return [self.info(k)[0] for k in range(len(self))]
+
+    def index(self, name: str) -> int:
+        i = C.c_int32()
+        check(_lib.lib().fopt_st_find(self.handle, name.encode(), C.byref(i)))
+        return i.value
+
+    def close(self):
+        if self.handle:
+            _lib.lib().fopt_st_close(self.handle)
+            self.handle = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Storage:
@@ -208,6 +263,31 @@ class B200:
         check(_lib.lib().fopt_h2d(self.ctx, s.ptr, host, len(buf)), self.ctx)
         self.sync()
         return s
+
+    def from_safetensors(self, st, name: str, mapping: Mapping, dtype: Optional[str] = None) -> Storage:
+        """`HostTensor::from_safetensors(view).to_hbm()` (tensor/memory.rs:197-222) in one step: the
+        tensor's shape must equal the mapping's pair-split sizes and its byte length the mapping's
+        image; the bytes stream from the file into a new device storage."""
+        own = isinstance(st, (str, bytes, os.PathLike))
+        f = SafeTensors(st) if own else st
+        try:
+            i = f.index(name)
+            _, st_dt, shape, nbytes = f.info(i)
+            if st_dt not in ST_DTYPES:
+                raise ValueError(f"from_safetensors: dtype {st_dt} is not a storage type")
+            dt = ST_DTYPES[st_dt]
+            if dtype is not None and dtype != dt:
+                raise ValueError(f"from_safetensors: {name} is {dt}, not {dtype}")
+            if shape != mapping.flat_shape():
+                raise ValueError(f"from_safetensors: {name} has shape {shape}, the mapping {mapping.flat_shape()}")
+            s = Storage(self, dt, mapping.size, zero=False)
+            if nbytes != s.nbytes:
+                raise ValueError(f"from_safetensors: {name} holds {nbytes} bytes, the mapping {s.nbytes}")
+            check(_lib.lib().fopt_st_read(self.ctx, f.handle, i, s.ptr, nbytes), self.ctx)
+            return s
+        finally:
+            if own:
+                f.close()
 
     def zeroed(self, mapping: Mapping, dtype: str) -> Storage:
         return Storage(self, dtype, mapping.size)

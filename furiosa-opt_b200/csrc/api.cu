@@ -26,30 +26,9 @@ void* scratch(fopt_ctx* ctx, size_t bytes) {
 
 }  // namespace fopt
 
+thread_local std::string fopt::g_noctx_err;
+
 namespace {
-
-template <typename Fn>
-fopt_status guarded(fopt_ctx* ctx, Fn&& fn) {
-  try {
-    fn();
-    return FOPT_OK;
-  } catch (const Fail& f) {
-    if (ctx) ctx->err = f.msg;
-    return f.code;
-  } catch (const MappingError& e) {
-    if (ctx) ctx->err = e.what();
-    return FOPT_ERR_INVALID;
-  } catch (const std::exception& e) {
-    if (ctx) ctx->err = e.what();
-    return FOPT_ERR_INVALID;
-  }
-}
-
-thread_local std::string g_noctx_err;
-
-void require(bool ok, const std::string& msg) {
-  if (!ok) throw Fail{FOPT_ERR_INVALID, msg};
-}
 
 // Mappings parsed by separate fopt_mapping_parse calls carry separate axis tables; re-parse them
 // against one merged table so axis identities agree (axes match by name, as Ident does).
@@ -153,6 +132,10 @@ fopt_status fopt_destroy(fopt_ctx* ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->gemm_ws) cudaFree(ctx->gemm_ws);
   if (ctx->gemm_cnt) cudaFree(ctx->gemm_cnt);
+  for (int k = 0; k < 2; ++k) {
+    if (ctx->pinned[k]) cudaFreeHost(ctx->pinned[k]);
+    if (ctx->pinned_ev[k]) cudaEventDestroy(ctx->pinned_ev[k]);
+  }
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   extern fopt_status fopt_comm_destroy(fopt_ctx*);
   fopt_comm_destroy(ctx);

@@ -58,6 +58,8 @@ struct fopt_ctx {
   uint32_t* gemm_cnt = nullptr;  // arrival counters of the split tiles (zero between launches)
   size_t gemm_cnt_n = 0;
   bool gemm_cnt_dirty = false;
+  void* pinned[2] = {nullptr, nullptr};  // host staging for file -> device streaming
+  cudaEvent_t pinned_ev[2] = {nullptr, nullptr};
 };
 
 namespace fopt {
@@ -67,6 +69,31 @@ struct Fail {
   fopt_status code;
   std::string msg;
 };
+
+// The last error of calls made without a context (mapping parsing, file headers).
+extern thread_local std::string g_noctx_err;
+
+inline void require(bool ok, const std::string& msg) {
+  if (!ok) throw Fail{FOPT_ERR_INVALID, msg};
+}
+
+// Runs fn, turning any exception into a status (the message goes to the context's last error).
+template <typename Fn>
+fopt_status guarded(fopt_ctx* ctx, Fn&& fn) {
+  try {
+    fn();
+    return FOPT_OK;
+  } catch (const Fail& f) {
+    if (ctx) ctx->err = f.msg;
+    return f.code;
+  } catch (const MappingError& e) {
+    if (ctx) ctx->err = e.what();
+    return FOPT_ERR_INVALID;
+  } catch (const std::exception& e) {
+    if (ctx) ctx->err = e.what();
+    return FOPT_ERR_INVALID;
+  }
+}
 
 inline void cuda_check(cudaError_t e, const char* what) {
   if (e != cudaSuccess) throw Fail{FOPT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e)};

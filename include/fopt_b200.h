@@ -253,6 +253,23 @@ fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, con
                              const fopt_mapping* pre_reduce, const fopt_mapping* out_map,
                              const fopt_epilogue* epilogue);
 
+/* ---- host I/O: safetensors straight to device (HostTensor::from_safetensors + to_hbm,
+ * furiosa-opt-std/src/tensor/memory.rs:197-222) ----
+ * A safetensors file: an 8-byte little-endian header length, a JSON header of
+ * {name: {"dtype", "shape", "data_offsets": [begin, end]}}, then the data. fopt_st_read streams one
+ * tensor's bytes (its packed image for byte-multiple dtypes) through pinned staging into device
+ * memory on the context's stream. fopt_mapping_flat_shape gives the dimensions the reference
+ * checks a tensor's shape against: a mapping's pair-split sizes. */
+typedef struct fopt_safetensors fopt_safetensors;
+fopt_status fopt_st_open(const char* path, fopt_safetensors** out);
+fopt_status fopt_st_close(fopt_safetensors* st);
+int32_t fopt_st_count(const fopt_safetensors* st);
+fopt_status fopt_st_info(const fopt_safetensors* st, int32_t index, const char** name, const char** dtype,
+                         int32_t* ndim, int64_t* shape, int32_t max_dims, int64_t* bytes);
+fopt_status fopt_st_find(const fopt_safetensors* st, const char* name, int32_t* index);
+fopt_status fopt_st_read(fopt_ctx* ctx, const fopt_safetensors* st, int32_t index, void* dst, size_t bytes);
+fopt_status fopt_mapping_flat_shape(const fopt_mapping* m, int64_t* dims, int32_t max_dims, int32_t* n);
+
 /* ---- fused attention (furiosa-opt-examples/src/transformer/kernel/attention.rs:32-392) ----
  * softmax(Q K^T * scale + causal mask) V for bf16 Q [B, S, Hq, D], K/V [B, S, Hkv, D] (row-major,
  * GQA: query head h reads kv head h / (Hq/Hkv)), fp32 softmax with the reference's running max /

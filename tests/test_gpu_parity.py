@@ -691,3 +691,29 @@ def test_fp_to_fxp_edges(b200, iw):
     vals = vals.astype(np.float32)
     got, want = _ew_case(b200, ops.fp_to_fxp(iw), ["f32"], "i32", n=len(vals), values=[vals])
     assert got == want
+
+
+# ---------------------------------------------------------------------------------------------
+# host I/O
+# ---------------------------------------------------------------------------------------------
+def test_from_safetensors_streams_to_device(b200, tmp_path):
+    """HostTensor::from_safetensors + to_hbm in one step: bytes land unchanged (a 40 MiB tensor
+    crosses several pinned staging chunks), the shape is checked against the mapping's pair-split
+    sizes, and the byte count against the mapping's image."""
+    import json
+    import struct
+    rng = np.random.default_rng(9)
+    big = rng.integers(0, 2 ** 16, 20 * 1024 * 1024, dtype=np.int64).astype(np.uint16)  # bf16 bits
+    small = rng.standard_normal((24, 16)).astype(np.float32)
+    header = {"big": {"dtype": "BF16", "shape": [5120, 4096], "data_offsets": [0, big.nbytes]},
+              "small": {"dtype": "F32", "shape": [24, 16], "data_offsets": [big.nbytes, big.nbytes + small.nbytes]}}
+    text = json.dumps(header).encode()
+    p = tmp_path / "w.safetensors"
+    p.write_bytes(struct.pack("<Q", len(text)) + text + big.tobytes() + small.tobytes())
+    with fb.SafeTensors(str(p)) as st:
+        B = b200.from_safetensors(st, "big", fb.Mapping("[R, C]", dict(R=5120, C=4096)))
+        S = b200.from_safetensors(st, "small", fb.Mapping("[A, B]", dict(A=24, B=16)), dtype="f32")
+        with pytest.raises(ValueError):
+            b200.from_safetensors(st, "small", fb.Mapping("[B, A]", dict(A=24, B=16)))
+    assert B.to_bytes() == big.tobytes()
+    assert S.to_bytes() == small.tobytes()

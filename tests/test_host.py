@@ -249,3 +249,59 @@ def test_program_composition_matches_sequential_programs():
     for _ in range(6):
         ref = _run(step, [ref], ["f32"], "f32")
     assert _run(chain, [g.tobytes()], ["f32"], "f32") == ref
+
+
+def _write_safetensors(path, tensors, metadata=None):
+    """A safetensors file from {name: (dtype string, shape, raw bytes)} (the published layout)."""
+    import json
+    import struct
+    header, blobs, off = {}, [], 0
+    if metadata:
+        header["__metadata__"] = metadata
+    for name, (dt, shape, raw) in tensors.items():
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + len(raw)]}
+        blobs.append(raw)
+        off += len(raw)
+    text = json.dumps(header).encode()
+    text += b" " * ((8 - len(text) % 8) % 8)
+    with open(path, "wb") as fh:
+        fh.write(struct.pack("<Q", len(text)) + text + b"".join(blobs))
+
+
+def test_safetensors_header_and_flat_shape(tmp_path):
+    """The native safetensors reader: names, dtypes, shapes and byte counts from the header, escapes
+    and metadata skipped; and the pair-split shapes the reference checks a tensor against."""
+    rng = np.random.default_rng(0)
+    w = rng.standard_normal((8, 12)).astype(np.float32)
+    b = rng.integers(-128, 128, 40, dtype=np.int64).astype(np.int8)
+    p = tmp_path / "t.safetensors"
+    _write_safetensors(p, {'w"x': ("F32", (8, 12), w.tobytes()), "b": ("I8", (40,), b.tobytes())},
+                       metadata={"format": "pt"})
+    with fb.SafeTensors(str(p)) as st:
+        assert len(st) == 2
+        assert sorted(st.names()) == ["b", 'w"x']
+        name, dt, shape, nbytes = st.info(st.index('w"x'))
+        assert (dt, shape, nbytes) == ("F32", [8, 12], w.nbytes)
+        assert st.info(st.index("b"))[1:] == ("I8", [40], 40)
+        with pytest.raises(_lib.FoptError):
+            st.index("missing")
+    assert fb.Mapping("[H, X]", dict(H=256, X=800)).flat_shape() == [256, 800]
+    assert fb.Mapping("[[A, B], C]", dict(A=2, B=3, C=5)).flat_shape() == [2, 3, 5]
+    assert fb.Mapping("[A # 8, B]", dict(A=5, B=3)).flat_shape() == [8, 3]
+    assert fb.Mapping("[A / 4]", dict(A=16)).flat_shape() == [4]
+    bad = tmp_path / "bad.safetensors"
+    bad.write_bytes(b"\x10\x00\x00\x00\x00\x00\x00\x00{not json at all")
+    with pytest.raises(_lib.FoptError):
+        fb.SafeTensors(str(bad))
+
+
+@pytest.mark.skipif(not os.path.exists("/root/reference/furiosa-opt-examples/data/mnist/mnist.safetensors"),
+                    reason="reference tree not present")
+def test_safetensors_reads_reference_mnist_header():
+    """The reference example's own weights file parses, with the shapes its test loads them as."""
+    with fb.SafeTensors("/root/reference/furiosa-opt-examples/data/mnist/mnist.safetensors") as st:
+        info = {st.info(k)[0]: st.info(k)[1:3] for k in range(len(st))}
+    assert info["hw.fc1.weight"] == ("BF16", [256, 800])
+    assert info["hw.fc2.weight"] == ("BF16", [16, 256])
+    assert info["hw.image_0"] == ("BF16", [800])
+    assert info["label_0"] == ("I32", [1])
