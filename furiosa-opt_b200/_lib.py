@@ -92,6 +92,7 @@ SIGNATURES = [
     ("fopt_comm_unique_id", _I32, [_VP]),
     ("fopt_comm_init", _I32, [_VP, _I32, _I32, _VP]),
     ("fopt_comm_destroy", _I32, [_VP]),
+    ("fopt_allreduce_op", _I32, [_VP, _VP, _I64, C.c_int, C.c_int]),
     ("fopt_allreduce", _I32, [_VP, _VP, _I64, C.c_int]),
     ("fopt_chip_shuffle", _I32, [_VP, _VP, _VP, _SZ, C.POINTER(_I32), _I32]),
 ]

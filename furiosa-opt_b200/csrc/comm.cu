@@ -127,14 +127,26 @@ fopt_status fopt_comm_destroy(fopt_ctx* ctx) {
   });
 }
 
-fopt_status fopt_allreduce(fopt_ctx* ctx, void* buf, int64_t count, fopt_dtype dtype) {
+fopt_status fopt_allreduce_op(fopt_ctx* ctx, void* buf, int64_t count, fopt_dtype dtype, fopt_reduce_op op) {
   return guard(ctx, [&] {
     if (!ctx->nccl_comm) throw Fail{FOPT_ERR_INVALID, "fopt_allreduce: no communicator (fopt_comm_init)"};
     ncclDataType_t t;
     if (!nccl_type(dtype, &t)) throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_allreduce: dtype"};
-    nccl_check(nccl().AllReduce(buf, buf, (size_t)count, t, ncclSum, (ncclComm_t)ctx->nccl_comm, ctx->stream),
+    ncclRedOp_t r;
+    switch (op) {
+      case FOPT_RED_ADD: r = ncclSum; break;
+      case FOPT_RED_MAX: r = ncclMax; break;
+      case FOPT_RED_MIN: r = ncclMin; break;
+      case FOPT_RED_MUL: r = ncclProd; break;
+      default: throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_allreduce: saturating add has no collective"};
+    }
+    nccl_check(nccl().AllReduce(buf, buf, (size_t)count, t, r, (ncclComm_t)ctx->nccl_comm, ctx->stream),
                "ncclAllReduce");
   });
+}
+
+fopt_status fopt_allreduce(fopt_ctx* ctx, void* buf, int64_t count, fopt_dtype dtype) {
+  return fopt_allreduce_op(ctx, buf, count, dtype, FOPT_RED_ADD);
 }
 
 fopt_status fopt_chip_shuffle(fopt_ctx* ctx, void* dst, const void* src, size_t bytes, const int32_t* pattern,

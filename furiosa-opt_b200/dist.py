@@ -35,7 +35,13 @@ def exchange_unique_id(rank: int, world: int, broadcast) -> bytes:
 
 
 def init_comm(backend, rank: int, world: int) -> None:
-    """Creates the backend's NCCL communicator, rendezvousing through torch.distributed."""
+    """Creates the backend's NCCL communicator, rendezvousing through torch.distributed (a single
+    rank needs no rendezvous)."""
+    if world == 1:
+        uid = exchange_unique_id(0, 1, lambda buf: None)
+        raw = (C.c_uint8 * 128).from_buffer_copy(uid)
+        check(_lib.lib().fopt_comm_init(backend.ctx, 1, 0, raw), backend.ctx)
+        return
     import torch
     import torch.distributed as dist
 
@@ -50,10 +56,13 @@ def init_comm(backend, rank: int, world: int) -> None:
     check(_lib.lib().fopt_comm_init(backend.ctx, world, rank, raw), backend.ctx)
 
 
-def allreduce(backend, storage) -> None:
-    """Sum over the Chip axis, result on every chip (reduce over `Chip` then broadcast), in place."""
+def allreduce(backend, storage, op: str = "Add") -> None:
+    """Fold over the Chip axis, result on every chip (reduce over `Chip` then broadcast), in place.
+    op: the inter-slice reduce's Add, Max, Min or Mul."""
+    from .backend import REDUCE_OPS
     storage._will_write()
-    check(_lib.lib().fopt_allreduce(backend.ctx, storage.ptr, storage.n, _lib.DTYPES[storage.dtype]), backend.ctx)
+    check(_lib.lib().fopt_allreduce_op(backend.ctx, storage.ptr, storage.n, _lib.DTYPES[storage.dtype],
+                                       REDUCE_OPS[op]), backend.ctx)
 
 
 def chip_shuffle(backend, dst, src, pattern) -> None:

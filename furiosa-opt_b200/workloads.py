@@ -176,11 +176,14 @@ class DecoderBlockW8A8:
         rb = be.relayout(rinv, m("[T]"), m("[T, H]"), allow_broadcast=True)
         return be.zip3_with(x_f32, rb, g, _prog_scale3(), "f32")
 
-    def quantize(self, x_f32: Storage, width: str):
-        """Per-token symmetric int8: s[t] = max|x[t, :]| / 127, q = Clip(round(x / s), -127, 127)."""
+    def quantize(self, x_f32: Storage, width: str, amax_hook=None):
+        """Per-token symmetric int8: s[t] = max|x[t, :]| / 127, q = Clip(round(x / s), -127, 127).
+        amax_hook (tensor parallelism): folds the per-token maxima of this rank's columns across ranks."""
         be, m = self.be, self.m
         a = be.map(x_f32, _prog_abs(), "f32")
         amax = be.reduce(a, "Max", 0.0, m(f"[T, {width}]"), m("[T]"))
+        if amax_hook is not None:
+            amax_hook(amax)
         s = be.map(amax, _prog_token_scale(), "f32")
         sb = be.relayout(s, m("[T]"), m(f"[T, {width}]"), allow_broadcast=True)
         q = be.zip_with(x_f32, sb, _prog_quant(), "i8")
@@ -219,3 +222,73 @@ class DecoderBlockW8A8:
 
     def attention_flops(self) -> float:
         return 4.0 * self.seq * self.seq * 128 * self.Hq / 2 * self.batch
+
+
+def _prog_dequant():
+    # FxpToFp(31) -> MulF(row scale) -> MulF(column scale) -> bf16: the dequant epilogue's order
+    p = ops.Prog(3)
+    y = p.emit("FXP_TO_FP", 0, imm=31)
+    y = p.emit("MULF", p.emit("MULF", y, 1), 2)
+    return p.build(p.emit("F32_TO_BF16", y))
+
+
+class DecoderBlockW8A8TP(DecoderBlockW8A8):
+    """The config-4 block tensor-parallel over `world` GPUs (one process each, NCCL communicator
+    already initialised on `be`): query / kv heads and FFN columns split across ranks
+    (column-parallel Q, K, V, gate, up; row-parallel O and down). Weights are the single-GPU block's
+    (same seed) and each rank keeps its shard. The row-parallel projections sum their i32
+    accumulators across ranks before the dequant (exact), and the per-token quantisation scales of
+    the sharded activations take the maximum across ranks (exact), so the output is bit-identical to
+    the single-GPU block's."""
+
+    def __init__(self, be: B200, T, H, Hq, Hkv, F, batch, seq, rank: int, world: int, seed: int = 0):
+        if Hq % world or Hkv % world or F % world:
+            raise ValueError("heads and FFN width must split evenly across ranks")
+        super().__init__(be, T, H, Hq, Hkv, F, batch, seq, seed=seed)
+        from . import dist
+        self.dist, self.rank, self.world = dist, rank, world
+        self.Hq_l, self.Hkv_l, self.F_l = Hq // world, Hkv // world, F // world
+        Ql, KVl = self.Hq_l * 128, self.Hkv_l * 128
+        self.ax.update(QL=Ql, VL=KVl, FL=self.F_l)
+        h = self.host
+        rows = lambda w, n: w[rank * n:(rank + 1) * n]  # noqa: E731
+        cols = lambda w, n: np.ascontiguousarray(w[:, rank * n:(rank + 1) * n])  # noqa: E731
+        up = lambda e, a, dt: be.from_buf(self.m(e), np.ascontiguousarray(a).tobytes(), dt)  # noqa: E731
+        self.wq, self.sq = up("[QL, H]", rows(h["wq"][0], Ql), "i8"), up("[QL]", rows(h["wq"][1], Ql), "f32")
+        self.wk, self.sk = up("[VL, H]", rows(h["wk"][0], KVl), "i8"), up("[VL]", rows(h["wk"][1], KVl), "f32")
+        self.wv, self.sv = up("[VL, H]", rows(h["wv"][0], KVl), "i8"), up("[VL]", rows(h["wv"][1], KVl), "f32")
+        self.wg, self.sg = up("[FL, H]", rows(h["wg"][0], self.F_l), "i8"), up("[FL]", rows(h["wg"][1], self.F_l), "f32")
+        self.wu, self.su = up("[FL, H]", rows(h["wu"][0], self.F_l), "i8"), up("[FL]", rows(h["wu"][1], self.F_l), "f32")
+        self.wo = up("[Q, QL]", cols(h["wo"][0], Ql), "i8")
+        self.wd = up("[Q, FL]", cols(h["wd"][0], self.F_l), "i8")
+
+    def _amax_across(self, amax: Storage) -> None:
+        self.dist.allreduce(self.be, amax, "Max")
+
+    def _row_parallel(self, q: Storage, s_tok: Storage, w: Storage, s_w: Storage, k_ax: str) -> Storage:
+        be, m = self.be, self.m
+        acc = be.contraction_wide(q, w, m(f"[T, {k_ax}]"), m(f"[Q, {k_ax}]"), m(f"[T, Q, {k_ax}]"), m("[T, Q]"))
+        self.dist.allreduce(be, acc)  # i32 sums: exact
+        rs = be.relayout(s_tok, m("[T]"), m("[T, Q]"), allow_broadcast=True)
+        cs = be.relayout(s_w, m("[Q]"), m("[T, Q]"), allow_broadcast=True)
+        return be.zip3_with(acc, rs, cs, _prog_dequant(), "bf16")
+
+    def forward(self, x: Storage) -> Storage:
+        be = self.be
+        xf = be.map(x, ops.cast("bf16", "f32"), "f32")
+        q, s = self.quantize(self.rmsnorm(xf, self.g1), "H")
+        Q = self.proj(q, s, self.wq, self.sq, "H", "QL")
+        K = self.proj(q, s, self.wk, self.sk, "H", "VL")
+        V = self.proj(q, s, self.wv, self.sv, "H", "VL")
+        att = be.attention(Q, K, V, self.batch, self.seq, self.Hq_l, self.Hkv_l, 128, causal=True)
+        qa, sa = self.quantize(be.map(att, ops.cast("bf16", "f32"), "f32"), "QL", amax_hook=self._amax_across)
+        o = self._row_parallel(qa, sa, self.wo, self.so, "QL")
+        h1 = be.zip_with(x, o, _prog_residual(), "bf16")
+        h1f = be.map(h1, ops.cast("bf16", "f32"), "f32")
+        q2, s2 = self.quantize(self.rmsnorm(h1f, self.g2), "H")
+        g = self.proj(q2, s2, self.wg, self.sg, "H", "FL")
+        u = self.proj(q2, s2, self.wu, self.su, "H", "FL")
+        act = be.zip_with(g, u, _prog_swiglu(), "f32")
+        q3, s3 = self.quantize(act, "FL", amax_hook=self._amax_across)
+        d = self._row_parallel(q3, s3, self.wd, self.sd, "FL")
+        return be.zip_with(h1, d, _prog_residual(), "bf16")

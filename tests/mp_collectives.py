@@ -37,6 +37,25 @@ src = be.from_vec(m, vals[rank], "bf16")
 dst = be.zeroed(m, "bf16")
 fb.dist.chip_shuffle(be, dst, src, pattern)
 assert np.array_equal(dst.to_numpy(), vals[pattern[rank]])
+# max / min / product folds over the Chip axis (f32, exact)
+fv = [np.random.default_rng(100 + r).standard_normal(4096).astype(np.float32) for r in range(world)]
+for op, fold in (("Max", np.maximum), ("Min", np.minimum)):
+    y = be.from_vec(fb.Mapping("[E]", dict(E=4096)), fv[rank], "f32")
+    fb.dist.allreduce(be, y, op)
+    want_f = fv[0]
+    for r in range(1, world):
+        want_f = fold(want_f, fv[r])
+    assert np.array_equal(y.to_numpy(), want_f), op
+# the tensor-parallel decoder block: bit-identical to the single-GPU block (same weights)
+from furiosa_opt_b200 import workloads as W  # noqa: E402
+batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+T, H = batch * seq, Hq * 128
+tp = W.DecoderBlockW8A8TP(be, T, H, Hq, Hkv, F, batch, seq, rank, world, seed=3)
+one = W.DecoderBlockW8A8(be, T, H, Hq, Hkv, F, batch, seq, seed=3)
+xb = fb.dtypes.f32_to_bf16_bits(np.random.default_rng(5).standard_normal(T * H).astype(np.float32))
+got_tp = tp.forward(be.from_vec(tp.m("[T, H]"), xb, "bf16")).to_bytes()
+got_one = one.forward(be.from_vec(one.m("[T, H]"), xb, "bf16")).to_bytes()
+assert got_tp == got_one, "tensor-parallel block differs from the single-GPU block"
 dist.barrier()
 if rank == 0:
     print(f"collectives ok on {world} ranks")

@@ -57,3 +57,19 @@ def test_decoder_block_w8a8(b200):
     assert np.all(np.isfinite(got))
     assert err.max() <= 0.03 * scale, f"max abs err {err.max()} vs max |out| {scale}"
     assert err.mean() <= 0.003 * scale, f"mean abs err {err.mean()}"
+
+
+def test_decoder_block_tensor_parallel_one_rank_bit_exact(b200):
+    """The tensor-parallel block on one rank: its row-parallel projections take the i32 sums then
+    dequantise elementwise, and its quantisation scales pass through the (one-rank) max all-reduce;
+    the output must equal the single-GPU block's bit for bit (the 2-GPU run is in mp_collectives)."""
+    be = fb.B200(0)
+    fb.dist.init_comm(be, 0, 1)
+    batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+    T, H = batch * seq, Hq * 128
+    tp = W.DecoderBlockW8A8TP(be, T, H, Hq, Hkv, F, batch, seq, 0, 1, seed=3)
+    one = W.DecoderBlockW8A8(be, T, H, Hq, Hkv, F, batch, seq, seed=3)
+    x = fb.dtypes.f32_to_bf16_bits(np.random.default_rng(5).standard_normal(T * H).astype(np.float32))
+    a = tp.forward(be.from_vec(tp.m("[T, H]"), x, "bf16")).to_bytes()
+    b = one.forward(be.from_vec(one.m("[T, H]"), x, "bf16")).to_bytes()
+    assert a == b
