@@ -3,9 +3,10 @@
 Default (headline) workload: config 2, the standalone int8 contraction M=N=K=4096 (i32 accumulate,
 per-channel fp32 requant to i8), one step = one `contraction` call through the backend.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm_i8|gemm_bf16|attention|
-                  relayout|allreduce] [--impl ours|reference]
+                  relayout|allreduce|mnist|decoder|decoder_tp] [--impl ours|reference]
 Multi-GPU (torchrun, one rank per GPU): independent replicas of the step ("replicas only": the
-contraction does not shard), except `allreduce`, the config-5 NCCL collective.
+contraction does not shard), except `allreduce`, the config-5 NCCL collective, and `decoder_tp`,
+the config-4 block split over the GPUs (strong scaling).
 `--impl reference` times the reference algorithm's CPU restatement (the oracle port: the emulator
 itself is Rust + closed prebuilt libraries and cannot be built here) on this host's cores.
 """
@@ -292,6 +293,30 @@ def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
                         "gemm_ops": blk.gemm_ops(), "attention_flops": blk.attention_flops()})
 
 
+def wl_decoder_tp(fb, be, rank, world, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
+    """Config 4 tensor-parallel over the ranks (strong scaling: the same 8 x 512-token block, heads and
+    FFN columns split across GPUs, NCCL between the halves). Unit: tokens/s of the whole block."""
+    T, H = batch * seq, Hq * 128
+    if world > 1:
+        fb.dist.init_comm(be, rank, world)
+    else:
+        fb.dist.init_comm(be, 0, 1)
+    blk = fb.workloads.DecoderBlockW8A8TP(be, T, H, Hq, Hkv, F, batch, seq, rank, world, seed=0)
+    rng = np.random.default_rng(1)
+    X = be.from_vec(blk.m("[T, H]"), fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32)),
+                    "bf16")
+
+    def step():
+        return blk.forward(X)
+
+    return dict(step=step, units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8", aggregate=False,
+                scaling="strong", flops=blk.gemm_ops() + blk.attention_flops(),
+                metric="W8A8 decoder block tokens/s, tensor-parallel (Llama-3-8B shape, 8 x 512 tokens)",
+                workload="decoder_w8a8_tp",
+                config={"batch": batch, "seq": seq, "hidden": H, "ffn": F, "heads": Hq, "kv_heads": Hkv,
+                        "gemm_ops": blk.gemm_ops(), "attention_flops": blk.attention_flops()})
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -303,7 +328,8 @@ def run_ours(args, rank, world, local):
     wl = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
           "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
           "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
-          "decoder": lambda: wl_decoder(fb, be)}[args.workload]()
+          "decoder": lambda: wl_decoder(fb, be),
+          "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}[args.workload]()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
     clk = Clocks(local).__enter__()  # sampling runs from before warm-up to the end of the timed steps
     clk.wait_first_sample()
@@ -380,9 +406,11 @@ def run_ours(args, rank, world, local):
         roof["traffic"], roof["traffic_unit"], roof["traffic_src"] = tr[0], "bytes per launch (ncu)", tr[1]
     line = {"metric": wl["metric"], "value": round(value, 2), "unit": wl["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic (seeded)",
+            "scaling": wl.get("scaling", "weak"), "vs_baseline": None, "dtype": wl["dtype"],
+            "data": "synthetic (seeded)",
             "config": {"workload": wl["workload"], **wl["config"], "l2": "flushed (256 MiB write) between steps",
                        "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
+                                       f"tensor-parallel x{world} (NCCL)" if wl.get("scaling") == "strong" else
                                        f"replicas x{world}") if world > 1 else "1 GPU"},
             "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
             "wall_s": round(wall, 4)}
