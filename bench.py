@@ -140,17 +140,17 @@ def wl_gemm(fb, be, dtype: str, M=4096, N=4096, K=4096):
     hout = torch.empty(M * N * (1 if dtype == "i8" else 2), dtype=torch.uint8).pin_memory()
     lib = fb._lib.lib()
 
+    ep = fb.backend._ep(1, S, "N") if dtype == "i8" else None
+
     def e2e_step():
-        lib.fopt_h2d(be.ctx, A.ptr, ha.data_ptr(), ha.numel())
-        lib.fopt_h2d(be.ctx, B.ptr, hb.data_ptr(), hb.numel())
-        out = step()
-        lib.fopt_d2h(be.ctx, hout.data_ptr(), out.ptr, hout.numel())
-        return out
+        # the public host-buffer call: operands in, contraction, result out (pipelined in row chunks)
+        return be.contraction_host(ha, hb, L, R, P, O, dtype, out_dt, ep=ep, out=hout)
 
     return dict(step=step, e2e_step=e2e_step, units=ops, unit="TOPS" if dtype == "i8" else "TFLOP/s",
                 scale=1e12, metric=f"{'int8' if dtype == 'i8' else 'bf16'} GEMM "
                                    f"{'TOPS' if dtype == 'i8' else 'TFLOP/s'} (M=N=K={M})",
                 h2d=ha.numel() + hb.numel(), d2h=hout.numel(), bound="tensor",
+                e2e_api="B200.contraction_host -> fopt_contraction_host (pinned host buffers, row-chunk pipeline)",
                 algo_bytes=None, workload=f"gemm_{dtype}_{M}x{N}x{K}", dtype=dtype,
                 extra={"out_dtype": out_dt, "epilogue": "per-channel requant" if dtype == "i8" else "bf16 narrow"},
                 cpu=lambda rows: cpu_gemm(a, b, scale, dtype, M, N, K, rows),
@@ -417,7 +417,7 @@ def run_ours(args, rank, world, local):
     if e2e_ms:
         line["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
                        "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
-                       "ms_per_step": round(e2e_ms, 4)}
+                       "ms_per_step": round(e2e_ms, 4), "api": wl.get("e2e_api", "")}
     if args.workload == "allreduce" and world > 1 and args.sweep:
         line["sweep"] = sweep
     if "cpu" in wl and world == 1 and not args.no_cpu:

@@ -88,6 +88,7 @@ SIGNATURES = [
     ("fopt_reduce", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_reduce_noalloc", _I32, [_VP, _VP, _VP, C.c_int, C.c_int, C.c_uint32, _VP, _VP, C.c_int]),
     ("fopt_contraction", _I32, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP, _VP, _VP, C.POINTER(Epilogue)]),
+    ("fopt_contraction_host", _I32, [_VP, _VP, C.c_int, _VP, _VP, C.c_int, _VP, _VP, _VP, _VP, C.POINTER(Epilogue)]),
     ("fopt_attention", _I32, [_VP, _VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, C.c_float]),
     ("fopt_comm_unique_id", _I32, [_VP]),
     ("fopt_comm_init", _I32, [_VP, _I32, _I32, _VP]),

@@ -497,6 +497,23 @@ class B200:
             raise ValueError("contraction_prewidened: operands must be i32 or f32")
         return self._contract(lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, lhs.dtype)
 
+    def contraction_host(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, in_dtype: str, out_dtype: str,
+                         ep=None, out=None):
+        """The contraction on host buffers (numpy arrays, or objects with `data_ptr()` such as pinned
+        torch tensors): operands copied in, contracted and the result copied out in one pipelined
+        call (`fopt_contraction_host`). Returns the result's bytes as a numpy uint8 array (or fills
+        `out`). Asynchronous on the context's stream when `out` is given; synchronous otherwise."""
+        def addr(x):
+            return x.data_ptr() if hasattr(x, "data_ptr") else x.ctypes.data
+        res = out if out is not None else np.empty(dtypes.nbytes(out_dtype, out_map.size), np.uint8)
+        check(_lib.lib().fopt_contraction_host(self.ctx, addr(res), _lib.DTYPES[out_dtype], addr(lhs), addr(rhs),
+                                               _lib.DTYPES[in_dtype], lhs_map.handle, rhs_map.handle,
+                                               pre_reduce.handle, out_map.handle,
+                                               C.byref(ep) if ep is not None else None), self.ctx)
+        if out is None:
+            self.sync()
+        return res
+
     def contraction_wide(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map) -> Storage:
         """The engine's contract_outer widen + contract_lane fold in one op: narrow operands, wide
         (i32 / f32) output, without materialising the widened operand copies."""

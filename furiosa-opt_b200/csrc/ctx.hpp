@@ -58,6 +58,7 @@ struct fopt_ctx {
   uint32_t* gemm_cnt = nullptr;  // arrival counters of the split tiles (zero between launches)
   size_t gemm_cnt_n = 0;
   bool gemm_cnt_dirty = false;
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;  // host <-> device pipelines of the host-buffer calls
   void* pinned[2] = {nullptr, nullptr};  // host staging for file -> device streaming
   cudaEvent_t pinned_ev[2] = {nullptr, nullptr};
 };

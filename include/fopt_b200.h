@@ -270,6 +270,17 @@ fopt_status fopt_st_find(const fopt_safetensors* st, const char* name, int32_t* 
 fopt_status fopt_st_read(fopt_ctx* ctx, const fopt_safetensors* st, int32_t index, void* dst, size_t bytes);
 fopt_status fopt_mapping_flat_shape(const fopt_mapping* m, int64_t* dims, int32_t max_dims, int32_t* n);
 
+/* The same contraction on HOST buffers (the operands' and the result's packed images in host memory):
+ * one call copies in, contracts and copies out. GEMM-shaped contractions with dense rows pipeline
+ * the lhs rows, the GEMM and the result rows across two copy streams and the compute stream; use
+ * pinned host memory for the copies to overlap. Returns when the work is queued on the context's
+ * stream (fopt_sync to wait); the result equals fopt_contraction's. Scale vectors stay device
+ * pointers. */
+fopt_status fopt_contraction_host(fopt_ctx* ctx, void* host_out, fopt_dtype out_dtype, const void* host_lhs,
+                                  const void* host_rhs, fopt_dtype in_dtype, const fopt_mapping* lhs_map,
+                                  const fopt_mapping* rhs_map, const fopt_mapping* pre_reduce,
+                                  const fopt_mapping* out_map, const fopt_epilogue* epilogue);
+
 /* ---- fused attention (furiosa-opt-examples/src/transformer/kernel/attention.rs:32-392) ----
  * softmax(Q K^T * scale + causal mask) V for bf16 Q [B, S, Hq, D], K/V [B, S, Hkv, D] (row-major,
  * GQA: query head h reads kv head h / (Hq/Hkv)), fp32 softmax with the reference's running max /

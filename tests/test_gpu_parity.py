@@ -717,3 +717,23 @@ def test_from_safetensors_streams_to_device(b200, tmp_path):
             b200.from_safetensors(st, "small", fb.Mapping("[B, A]", dict(A=24, B=16)))
     assert B.to_bytes() == big.tobytes()
     assert S.to_bytes() == small.tobytes()
+
+
+@pytest.mark.parametrize("shape", [(1024, 512, 768), (96, 64, 40)])
+def test_contraction_host_buffers(b200, shape):
+    """One call from host buffers to a host result: the row-chunk pipeline (GEMM shape) and the plain
+    path (other shapes) give the device contraction's bytes, for requant and plain i32 outputs."""
+    M, K, N = shape
+    ax = dict(M=M, K=K, N=N)
+    L, R, P, O = (fb.Mapping(e, ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
+    rng = np.random.default_rng(M)
+    a = rng.integers(-128, 128, M * K).astype(np.int8)
+    b = rng.integers(-128, 128, N * K).astype(np.int8)
+    scale = rng.uniform(0.001, 0.01, N).astype(np.float32)
+    S = b200.from_vec(fb.Mapping("[N]", ax), scale, "f32")
+    A, B = b200.from_vec(L, a, "i8"), b200.from_vec(R, b, "i8")
+    want_rq = b200.contraction_requant(A, B, L, R, P, O, S, "N").to_bytes()
+    want_w = b200.contraction_wide(A, B, L, R, P, O).to_bytes()
+    ep = fb.backend._ep(1, S, "N")
+    assert b200.contraction_host(a, b, L, R, P, O, "i8", "i8", ep=ep).tobytes() == want_rq
+    assert b200.contraction_host(a, b, L, R, P, O, "i8", "i32").tobytes() == want_w
