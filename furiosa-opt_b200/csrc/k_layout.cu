@@ -7,6 +7,7 @@
 //   * tile:  the dst-innermost wheel is strided in src but another wheel is unit-stride in src ->
 //            a 32x32 shared-memory tile so both the read and the write are coalesced;
 //   * walk:  anything else, one element per thread with the odometer decomposed per position.
+#include <cstring>
 #include <algorithm>
 #include <type_traits>
 
@@ -174,43 +175,50 @@ __device__ __forceinline__ void transpose_block(const uint32_t* r, uint32_t* o) 
   }
 }
 
-template <typename T>
+// TW: tile width in words (32, or 64 for wider types); the tile is (TW E) x (TW E) elements, TW E rows
+// of TW words in shared memory. With TW = 64 a warp covers each row in two halves of 32 words, and
+// the XOR swizzle (columns 0..63) still gives every half 32 distinct banks.
+template <typename T, int TW>
 __global__ void __launch_bounds__(256) relayout_tile_w(T* __restrict__ dst, const T* __restrict__ src, KWalk others,
                                                        int64_t e0, int64_t s0, int64_t ej, int64_t wj,
                                                        int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
                                                        int64_t batches) {
-  constexpr int E = 4 / (int)sizeof(T), TT = 32 * E;
-  __shared__ uint32_t tile[TT][32];
+  constexpr int E = 4 / (int)sizeof(T), TT = TW * E;
+  __shared__ uint32_t tile[TT][TW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
     const int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
     int64_t off[2] = {0, 0};
     const bool live = walk_offsets<2>(others, b, off);
-    // rows / columns of this tile that exist (extents are multiples of E)
     const int64_t r0 = e0 - ti * TT, rj = ej - tj * TT;
     const int n0 = r0 < TT ? (int)r0 : TT, nj = rj < TT ? (int)rj : TT;
     if (live) {
       const T* sT = src + src_base + off[0] + ti * TT * s0 + tj * TT;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int a = warp + 8 * q;  // source rows E a .. E a + E - 1 of the tile
+#pragma unroll 2
+      for (int q = warp; q < TW * (TW / 32); q += 8) {
+        const int a = q % TW;                  // source rows E a .. E a + E - 1 of the tile
+        const int w = (q / TW) * 32 + lane;    // source word column
         uint32_t r[E], o[E];
 #pragma unroll
         for (int i = 0; i < E; ++i) r[i] = 0;
-        if (E * a < n0 && E * lane < nj) {
+        if (E * a < n0 && E * w < nj) {
 #pragma unroll
-          for (int i = 0; i < E; ++i) r[i] = *(const uint32_t*)(sT + (int64_t)(E * a + i) * s0 + E * lane);
+          for (int i = 0; i < E; ++i) r[i] = *(const uint32_t*)(sT + (int64_t)(E * a + i) * s0 + E * w);
         }
         transpose_block<E>(r, o);
 #pragma unroll
-        for (int k = 0; k < E; ++k) tile[E * lane + k][a ^ lane] = o[k];
+        for (int k = 0; k < E; ++k) tile[E * w + k][a ^ w] = o[k];
       }
     }
     __syncthreads();
-    if (live && E * lane < n0) {
-      T* dT = dst + dst_base + off[1] + ti * TT + tj * TT * wj + E * lane;
+    if (live) {
+      T* dT = dst + dst_base + off[1] + ti * TT + tj * TT * wj;
 #pragma unroll 4
-      for (int c = warp; c < nj; c += 8) *(uint32_t*)(dT + (int64_t)c * wj) = tile[c][lane ^ (c / E)];
+      for (int q = warp; q < nj * (TW / 32); q += 8) {
+        const int c = q / (TW / 32);              // dst row of the tile
+        const int a = (q % (TW / 32)) * 32 + lane;  // dst word
+        if (E * a < n0) *(uint32_t*)(dT + (int64_t)c * wj + E * a) = tile[c][a ^ (c / E)];
+      }
     }
     __syncthreads();
   }
@@ -449,21 +457,19 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
     int64_t nt0 = (w.extent[0] + TT - 1) / TT, ntj = (w.extent[j] + TT - 1) / TT;
     int64_t blocks = nt0 * ntj * batches;
     int grid = (int)std::min<int64_t>(blocks, (1ll << 31) - 1);  // one tile per block
-    // word tiles: element counts, strides and bases that keep every word aligned
-    // (1-byte elements only: for 2- and 4-byte elements the 64 x 64 and 32 x 32 element word tiles are
-    // too small, and the vector tile below is faster: 61 vs 84 us and 103 vs 178 us at 8192^2)
-    constexpr int EW = sizeof(T) == 1 ? 4 : 0;
-    bool words = EW > 0 && w.extent[0] % EW == 0 && w.extent[j] % EW == 0 && w.stride[0][0] % EW == 0 &&
-                 src_base % EW == 0 && dst_base % EW == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0 &&
+    // word tiles for 1-byte elements (4 x 4 byte blocks): for 2- and 4-byte elements the vector tile
+    // below is faster (its 8-byte global accesses halve the memory instructions): 61 vs 71 us (bf16)
+    // and 103 vs 146 us (f32) at 8192^2 against 64-word tiles
+    bool words = sizeof(T) == 1 && w.extent[0] % 4 == 0 && w.extent[j] % 4 == 0 && w.stride[0][0] % 4 == 0 &&
+                 src_base % 4 == 0 && dst_base % 4 == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0 &&
                  !getenv("FOPT_RELAYOUT_NO_WORDTILE");
-    for (int k = 0; words && k < others.n; ++k) words = others.stride[0][k] % EW == 0;
-    if constexpr (sizeof(T) <= 4) {
+    for (int k = 0; words && k < others.n; ++k) words = others.stride[0][k] % 4 == 0;
+    if constexpr (sizeof(T) == 1) {
       if (words) {
-        constexpr int TW = 32 * (4 / (int)sizeof(T));
-        const int64_t n0 = (w.extent[0] + TW - 1) / TW, nj = (w.extent[j] + TW - 1) / TW;
+        const int64_t n0 = (w.extent[0] + 127) / 128, nj = (w.extent[j] + 127) / 128;
         const int gw = (int)std::min<int64_t>(n0 * nj * batches, (1ll << 31) - 1);
-        relayout_tile_w<T><<<gw, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj, src_base,
-                                               dst_base, n0, nj, batches);
+        relayout_tile_w<T, 32><<<gw, 256, 0, st>>>(d, s, others, w.extent[0], w.stride[0][0], w.extent[j], wj,
+                                                   src_base, dst_base, n0, nj, batches);
         launched(ctx, "relayout_tile_w");
         return;
       }
