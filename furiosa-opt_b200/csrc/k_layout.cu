@@ -224,6 +224,105 @@ __global__ void __launch_bounds__(256) relayout_tile_w(T* __restrict__ dst, cons
   }
 }
 
+// Tile path for 2-byte elements in 8-byte units: a thread moves a 4 x 4 element block, loading four
+// 8-byte row pieces, transposing them in registers with byte permutes and storing four 8-byte
+// units into the transposed shared tile (128 rows x 32 units; unit a of tile row c sits at column
+// a ^ (c / 4), so a warp's 8-byte stores and loads take the minimum two wavefronts). Global loads and
+// stores are 8 bytes per lane, 256 contiguous bytes per warp instruction.
+__global__ void __launch_bounds__(256) relayout_tile_h(uint16_t* __restrict__ dst, const uint16_t* __restrict__ src,
+                                                       KWalk others, int64_t e0, int64_t s0, int64_t ej, int64_t wj,
+                                                       int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
+                                                       int64_t batches) {
+  __shared__ uint2 tile[128][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
+    const int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, b = blk / (nt0 * ntj);
+    int64_t off[2] = {0, 0};
+    const bool live = walk_offsets<2>(others, b, off);
+    const int64_t r0 = e0 - ti * 128, rj = ej - tj * 128;
+    const int n0 = r0 < 128 ? (int)r0 : 128, nj = rj < 128 ? (int)rj : 128;  // multiples of 4
+    if (live) {
+      const uint16_t* sT = src + src_base + off[0] + ti * 128 * s0 + tj * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int a = warp + 8 * q;  // source rows 4 a .. 4 a + 3; lane = source unit (4 columns)
+        uint2 r[4] = {make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0), make_uint2(0, 0)};
+        if (4 * a < n0 && 4 * lane < nj) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) r[i] = *(const uint2*)(sT + (int64_t)(4 * a + i) * s0 + 4 * lane);
+        }
+        // column k of the block: rows (0, 1) in .x, rows (2, 3) in .y
+        const uint2 c0 = make_uint2(__byte_perm(r[0].x, r[1].x, 0x5410), __byte_perm(r[2].x, r[3].x, 0x5410));
+        const uint2 c1 = make_uint2(__byte_perm(r[0].x, r[1].x, 0x7632), __byte_perm(r[2].x, r[3].x, 0x7632));
+        const uint2 c2 = make_uint2(__byte_perm(r[0].y, r[1].y, 0x5410), __byte_perm(r[2].y, r[3].y, 0x5410));
+        const uint2 c3 = make_uint2(__byte_perm(r[0].y, r[1].y, 0x7632), __byte_perm(r[2].y, r[3].y, 0x7632));
+        tile[4 * lane + 0][a ^ lane] = c0;
+        tile[4 * lane + 1][a ^ lane] = c1;
+        tile[4 * lane + 2][a ^ lane] = c2;
+        tile[4 * lane + 3][a ^ lane] = c3;
+      }
+    }
+    __syncthreads();
+    if (live && 4 * lane < n0) {
+      uint16_t* dT = dst + dst_base + off[1] + ti * 128 + tj * 128 * wj + 4 * lane;
+#pragma unroll 4
+      for (int c = warp; c < nj; c += 8) *(uint2*)(dT + (int64_t)c * wj) = tile[c][lane ^ (c >> 2)];
+    }
+    __syncthreads();
+  }
+}
+
+// Tile path for 1-byte elements in 8-byte units: a thread moves an 8 x 8 byte block (four 4 x 4 word
+// transposes), loading eight 8-byte row pieces and storing eight 8-byte units into the transposed
+// shared tile (128 rows x 16 units; unit a of tile row c sits at column a ^ (c / 8), so the 8-byte
+// stores and loads take the minimum two wavefronts). A warp covers two 128-byte rows per global load
+// and store.
+__global__ void __launch_bounds__(256) relayout_tile_b8(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src,
+                                                        KWalk others, int64_t e0, int64_t s0, int64_t ej, int64_t wj,
+                                                        int64_t src_base, int64_t dst_base, int64_t nt0, int64_t ntj,
+                                                        int64_t batches) {
+  __shared__ uint2 tile[128][16];
+  const int a = threadIdx.x >> 4, b = threadIdx.x & 15;  // source row block, source unit
+  for (int64_t blk = blockIdx.x; blk < nt0 * ntj * batches; blk += gridDim.x) {
+    const int64_t ti = blk % nt0, tj = (blk / nt0) % ntj, bt = blk / (nt0 * ntj);
+    int64_t off[2] = {0, 0};
+    const bool live = walk_offsets<2>(others, bt, off);
+    const int64_t r0 = e0 - ti * 128, rj = ej - tj * 128;
+    const int n0 = r0 < 128 ? (int)r0 : 128, nj = rj < 128 ? (int)rj : 128;  // multiples of 8
+    if (live) {
+      const uint8_t* sT = src + src_base + off[0] + ti * 128 * s0 + tj * 128;
+      uint32_t lo[8], hi[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) lo[i] = hi[i] = 0;
+      if (8 * a < n0 && 8 * b < nj) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint2 v = *(const uint2*)(sT + (int64_t)(8 * a + i) * s0 + 8 * b);
+          lo[i] = v.x;
+          hi[i] = v.y;
+        }
+      }
+      uint32_t tl[4], tr[4], bl[4], br[4];
+      transpose_block<4>(lo, tl);
+      transpose_block<4>(lo + 4, bl);
+      transpose_block<4>(hi, tr);
+      transpose_block<4>(hi + 4, br);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        tile[8 * b + k][a ^ b] = make_uint2(tl[k], bl[k]);
+        tile[8 * b + 4 + k][a ^ b] = make_uint2(tr[k], br[k]);
+      }
+    }
+    __syncthreads();
+    if (live && 8 * b < n0) {
+      uint8_t* dT = dst + dst_base + off[1] + ti * 128 + tj * 128 * wj + 8 * b;
+#pragma unroll 4
+      for (int c = a; c < nj; c += 16) *(uint2*)(dT + (int64_t)c * wj) = tile[c][b ^ (c >> 3)];
+    }
+    __syncthreads();
+  }
+}
+
 // ---- walk path ----
 template <typename T>
 __global__ void relayout_walk32(T* __restrict__ dst, const T* __restrict__ src, KWalk32 w, uint32_t positions,
@@ -464,7 +563,33 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
                  src_base % 4 == 0 && dst_base % 4 == 0 && (uintptr_t)src % 4 == 0 && (uintptr_t)dst % 4 == 0 &&
                  !getenv("FOPT_RELAYOUT_NO_WORDTILE");
     for (int k = 0; words && k < others.n; ++k) words = others.stride[0][k] % 4 == 0;
+    bool halves = sizeof(T) == 2 && w.extent[0] % 4 == 0 && w.extent[j] % 4 == 0 && w.stride[0][0] % 4 == 0 &&
+                  src_base % 4 == 0 && dst_base % 4 == 0 && (uintptr_t)src % 8 == 0 && (uintptr_t)dst % 8 == 0 &&
+                  !getenv("FOPT_RELAYOUT_NO_HTILE");
+    for (int k = 0; halves && k < others.n; ++k) halves = others.stride[0][k] % 4 == 0;
+    if constexpr (sizeof(T) == 2) {
+      if (halves) {
+        const int64_t n0 = (w.extent[0] + 127) / 128, nj = (w.extent[j] + 127) / 128;
+        const int gh = (int)std::min<int64_t>(n0 * nj * batches, (1ll << 31) - 1);
+        relayout_tile_h<<<gh, 256, 0, st>>>((uint16_t*)d, (const uint16_t*)s, others, w.extent[0], w.stride[0][0],
+                                            w.extent[j], wj, src_base, dst_base, n0, nj, batches);
+        launched(ctx, "relayout_tile_h");
+        return;
+      }
+    }
+    bool bytes8 = sizeof(T) == 1 && w.extent[0] % 8 == 0 && w.extent[j] % 8 == 0 && w.stride[0][0] % 8 == 0 &&
+                  src_base % 8 == 0 && dst_base % 8 == 0 && (uintptr_t)src % 8 == 0 && (uintptr_t)dst % 8 == 0 &&
+                  !getenv("FOPT_RELAYOUT_NO_B8TILE");
+    for (int k = 0; bytes8 && k < others.n; ++k) bytes8 = others.stride[0][k] % 8 == 0;
     if constexpr (sizeof(T) == 1) {
+      if (bytes8) {
+        const int64_t n0 = (w.extent[0] + 127) / 128, nj = (w.extent[j] + 127) / 128;
+        const int gb = (int)std::min<int64_t>(n0 * nj * batches, (1ll << 31) - 1);
+        relayout_tile_b8<<<gb, 256, 0, st>>>((uint8_t*)d, (const uint8_t*)s, others, w.extent[0], w.stride[0][0],
+                                             w.extent[j], wj, src_base, dst_base, n0, nj, batches);
+        launched(ctx, "relayout_tile_b8");
+        return;
+      }
       if (words) {
         const int64_t n0 = (w.extent[0] + 127) / 128, nj = (w.extent[j] + 127) / 128;
         const int gw = (int)std::min<int64_t>(n0 * nj * batches, (1ll << 31) - 1);

@@ -110,6 +110,7 @@ RELAYOUTS = [
     ("[A, B, C]", "[C, A, B]", dict(A=3, B=5, C=7), False),
     ("[A, B, C]", "[B, A, C]", dict(A=16, B=24, C=64), False),
     ("[A, B, C]", "[A, C, B]", dict(A=3, B=36, C=20), False),  # batched tiles, extents not multiples of 128
+    ("[A, B, C]", "[A, C, B]", dict(A=2, B=200, C=136), False),  # batched 8-byte-unit tiles, ragged edges
     ("[A]", "[B, A # 6]", dict(A=4, B=3), True),
     ("[C, D]", "[C, D # 64]", dict(C=13, D=61), False),
     ("[C, D # 64]", "[D, C]", dict(C=13, D=61), False),
