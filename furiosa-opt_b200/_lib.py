@@ -30,6 +30,25 @@ class Program(C.Structure):
     _fields_ = [("n_insn", C.c_int32), ("ret", C.c_int32), ("insn", Insn * 32)]
 
 
+class RowSlot(C.Structure):
+    """`fopt_row_slot`: one per-row scalar of a row program."""
+    _fields_ = [("kind", C.c_int32), ("op", C.c_int32), ("identity_bits", C.c_uint32), ("dtype", C.c_int32),
+                ("prog", C.POINTER(Program)), ("src", C.c_void_p), ("out", C.c_void_p)]
+
+
+ROW_FOLD, ROW_SCALAR, ROW_LOAD = 0, 1, 2
+REDUCE_OPS = {"Add": 0, "AddSat": 1, "Max": 2, "Min": 3, "Mul": 4}  # fopt_reduce_op
+ROW_MAX_LEAVES = ROW_MAX_HELD = ROW_MAX_SLOTS = 8
+
+
+class RowPlan(C.Structure):
+    """`fopt_row_plan`: a row program (leaves, held values, per-row slots, final program)."""
+    _fields_ = [("n_leaves", C.c_int32), ("n_held", C.c_int32), ("n_slots", C.c_int32),
+                ("leaf", C.c_void_p * 8), ("leaf_dtype", C.c_int32 * 8), ("leaf_bcast", C.c_int64 * 8),
+                ("held", C.POINTER(Program) * 8), ("slot", RowSlot * 8), ("final_prog", C.POINTER(Program)),
+                ("out", C.c_void_p), ("out_dtype", C.c_int32), ("rows", C.c_int64), ("row_len", C.c_int64)]
+
+
 class Epilogue(C.Structure):
     _fields_ = [("kind", C.c_int32), ("scale", C.c_void_p), ("scale_axis", C.c_char_p), ("int_width", C.c_int32),
                 ("clip_lo", C.c_int32), ("clip_hi", C.c_int32), ("row_scale", C.c_void_p)]
@@ -76,6 +95,13 @@ SIGNATURES = [
     ("fopt_reduce_map", _I32, [C.c_void_p, C.c_void_p, C.POINTER(Program), _I32, C.POINTER(C.c_void_p),
                                C.POINTER(C.c_int), C.POINTER(C.c_int64), C.c_int, C.c_int, C.c_uint32, C.c_void_p,
                                C.c_void_p]),
+    ("fopt_capture_begin", _I32, [C.c_void_p]),
+    ("fopt_capture_end", _I32, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("fopt_graph_launch", _I32, [C.c_void_p, C.c_void_p]),
+    ("fopt_graph_destroy", _I32, [C.c_void_p, C.c_void_p]),
+    ("fopt_row_reduce_shape", _I32, [C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    ("fopt_row_program", _I32, [C.c_void_p, C.POINTER(RowPlan)]),
+    ("fopt_row_program_source", _I32, [C.POINTER(RowPlan), C.c_char_p, _SZ, C.POINTER(_SZ)]),
     ("fopt_st_open", _I32, [C.c_char_p, C.POINTER(C.c_void_p)]),
     ("fopt_st_close", _I32, [C.c_void_p]),
     ("fopt_st_count", _I32, [C.c_void_p]),

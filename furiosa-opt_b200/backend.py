@@ -19,10 +19,10 @@ from typing import Optional, Sequence
 
 import numpy as np
 
-from . import _lib, dtypes, ops
+from . import _lib, dtypes, ops, rowfuse
 from ._lib import check
 
-REDUCE_OPS = {"Add": 0, "AddSat": 1, "Max": 2, "Min": 3, "Mul": 4}
+REDUCE_OPS = _lib.REDUCE_OPS
 
 
 class Mapping:
@@ -145,7 +145,10 @@ class Storage:
         self.nbytes = dtypes.nbytes(dtype, n)
         self._ptr = C.c_void_p()
         # lazy: ("bcast", src Storage, Src Mapping, Dst Mapping, bcast code of fopt_elementwise_bcast)
-        #    or ("ew", program, leaf inputs): values not yet written (leaves may be lazy broadcasts)
+        #    or ("ew", program, leaf inputs, origin): values not yet written (leaves may be lazy
+        #       broadcasts; origin = (program, inputs) of the op that made it, before composition)
+        #    or ("red", src Storage, op, identity bits, Src, Dst, rows, row length): a plain row
+        #       reduction of a deferred elementwise value, not yet run
         self.lazy = lazy
         self._dependents = weakref.WeakSet()  # lazy storages that read this one
         if lazy is None:
@@ -157,7 +160,7 @@ class Storage:
     def _lazy_sources(self):
         if self.lazy is None:
             return []
-        return [self.lazy[1]] if self.lazy[0] == "bcast" else list(self.lazy[2])
+        return list(self.lazy[2]) if self.lazy[0] == "ew" else [self.lazy[1]]
 
     def _will_write(self) -> None:
         """Called before anything writes into this storage in place: lazy storages that read it
@@ -171,6 +174,8 @@ class Storage:
         alloc = _lib.lib().fopt_alloc if zero else _lib.lib().fopt_alloc_uninit
         check(alloc(self.backend.ctx, self.nbytes, C.byref(p)), self.backend.ctx)
         self._ptr = p
+        # allocated while a step is being captured: the graph owns the memory once the capture ends
+        self._capture = getattr(self.backend, "_capturing", None)
 
     @property
     def ptr(self) -> C.c_void_p:
@@ -181,10 +186,14 @@ class Storage:
                 self._alloc(True)
                 check(_lib.lib().fopt_transpose(self.backend.ctx, self._ptr, src.ptr, _lib.DTYPES[src.dtype],
                                                 Src.handle, Dst.handle, 0, 0, 1), self.backend.ctx)
-            else:
-                _, prog, leaves = lazy
+            elif lazy[0] == "ew":
+                _, prog, leaves, origin = lazy
                 self._alloc(dtypes.BITS[self.dtype] == 4)
-                self.backend._run_ew(prog, leaves, self)
+                self.backend._run_ew(prog, leaves, self, origin)
+            else:
+                _, src, op, bits, Src, Dst, _, _ = lazy
+                self._alloc(False)
+                self.backend._run_reduce(self, src, op, bits, Src, Dst)
         return self._ptr
 
     @property
@@ -218,9 +227,36 @@ class Storage:
 
     def __del__(self):
         try:
+            cap = getattr(self, "_capture", None)
+            if cap is not None and getattr(self.backend, "_capturing", None) is not cap:
+                return  # a graph's allocation (released by the graph)
             if self._ptr:
                 _lib.lib().fopt_free(self.backend.ctx, self._ptr)
                 self._ptr = C.c_void_p()
+        except Exception:
+            pass
+
+
+class Graph:
+    """A captured step (see `B200.capture`)."""
+
+    def __init__(self, be: "B200", handle, outputs, token):
+        self.be, self._h, self.outputs, self._token = be, handle, outputs, token
+
+    def launch(self):
+        check(_lib.lib().fopt_graph_launch(self.be.ctx, self._h), self.be.ctx)
+        return self.outputs
+
+    def close(self):
+        if self._h:
+            check(_lib.lib().fopt_graph_destroy(self.be.ctx, self._h), self.be.ctx)
+            self._h = C.c_void_p()
+            for o in (self.outputs if isinstance(self.outputs, tuple) else (self.outputs,)):
+                o._ptr = C.c_void_p()  # released with the graph
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass
 
@@ -247,6 +283,34 @@ class B200:
         self.eager_broadcast = bool(os.environ.get("FOPT_EAGER_BROADCAST"))
         # engine-chain fusion of elementwise results (off: every op writes its result)
         self.fuse = not os.environ.get("FOPT_NO_FUSION")
+        # row programs: a row reduction and the elementwise ops that read its broadcast result run as
+        # one kernel per row (off: the reduction runs as its own kernel first)
+        self.row_fusion = not os.environ.get("FOPT_NO_ROW_FUSION")
+        self._capturing = None  # the open capture's token (see `capture`)
+
+    # ---- CUDA graphs of whole steps ----
+    def capture(self, fn) -> "Graph":
+        """Records the device work of `fn()` (a step: a decoder block's forward, an MLP pass) into a
+        CUDA graph instead of running it; `Graph.launch` replays it without the host work. `fn`
+        returns a storage or a tuple of them: they are written inside the capture and hold each
+        launch's results (same addresses every launch). Inputs are storages allocated before the
+        capture: write new values into them between launches. Run `fn` once before capturing so
+        its kernels are compiled and its workspaces sized."""
+        if self._capturing is not None:
+            raise RuntimeError("capture: a capture is already open")
+        check(_lib.lib().fopt_capture_begin(self.ctx), self.ctx)
+        token = object()
+        self._capturing = token
+        handle = C.c_void_p()
+        try:
+            outs = fn()
+            for o in (outs if isinstance(outs, tuple) else (outs,)):
+                o.ptr  # noqa: B018 (written inside the capture)
+        finally:
+            st = _lib.lib().fopt_capture_end(self.ctx, C.byref(handle))
+            self._capturing = None
+        check(st, self.ctx)
+        return Graph(self, handle, outs, token)
 
     # ---- lifecycle (backend/mod.rs:45-90) ----
     def from_vec(self, mapping: Mapping, data, dtype: str) -> Storage:
@@ -314,6 +378,7 @@ class B200:
     # a fused row reduction (`reduce`) folds the values without writing them, and any other use
     # writes them out first. Leaf inputs are ordinary storages or lazy broadcasts.
     DEFER = ("f32", "i32")
+    MAX_LEAVES = 8
 
     @staticmethod
     def _leaf_args(leaves):
@@ -333,7 +398,8 @@ class B200:
 
     def _compose(self, prog, inputs: Sequence[Storage]):
         """Returns (program, leaves) with deferred elementwise inputs folded in, or None when the
-        result would need more than 3 leaves, 32 instructions or 16 registers."""
+        result would need more than 8 leaves, 32 instructions or 16 registers. More than 3 leaves
+        run as a row program or through the origin (see `_run_ew`)."""
         leaves, keymap = [], {}
 
         def leaf_reg(st):
@@ -345,11 +411,11 @@ class B200:
         parts = []  # per consumer input: ("leaf", reg) or ("prog", program, [leaf regs])
         for s in inputs:
             if s.lazy is not None and s.lazy[0] == "ew":
-                _, q, qleaves = s.lazy
+                _, q, qleaves, _ = s.lazy
                 parts.append(("prog", q, [leaf_reg(l) for l in qleaves]))
             else:
                 parts.append(("leaf", leaf_reg(s)))
-        if len(leaves) > 3:
+        if len(leaves) > self.MAX_LEAVES:
             return None
         out = ops.Prog(len(leaves))
         regs = []
@@ -360,7 +426,15 @@ class B200:
         except ValueError:
             return None
 
-    def _run_ew(self, prog, leaves, out: Storage) -> None:
+    def _run_ew(self, prog, leaves, out: Storage, origin=None) -> None:
+        if self.fuse and self.row_fusion and rowfuse.try_row_program(self, prog, leaves, out, origin):
+            return
+        if len(leaves) > 3:  # the generated kernels take 3 inputs: evaluate the deferred inputs first
+            oprog, inputs = origin
+            cprog, cleaves = self._compose(oprog, [self._force(s) if s.lazy is not None and s.lazy[0] == "ew" else s
+                                                   for s in inputs])
+            self._run_ew(cprog, cleaves, out)
+            return
         ptrs, dts, codes, any_bcast = self._leaf_args(leaves)
         if any_bcast:
             st = _lib.lib().fopt_elementwise_bcast(self.ctx, C.byref(prog), len(leaves), ptrs, dts, codes, out._ptr,
@@ -383,10 +457,11 @@ class B200:
             composed = self._compose(prog, [self._force(s) if s.lazy is not None and s.lazy[0] == "ew" else s
                                             for s in inputs])
         cprog, leaves = composed
+        origin = (prog, list(inputs))
         if self.fuse and out_dtype in self.DEFER:
-            return Storage(self, out_dtype, n, lazy=("ew", cprog, leaves))
+            return Storage(self, out_dtype, n, lazy=("ew", cprog, leaves, origin))
         out = Storage(self, out_dtype, n, zero=dtypes.BITS[out_dtype] == 4)
-        self._run_ew(cprog, leaves, out)
+        self._run_ew(cprog, leaves, out, origin)
         return out
 
     @staticmethod
@@ -449,25 +524,40 @@ class B200:
     # ---- reduce (backend/mod.rs:128-133) ----
     def reduce(self, src: Storage, op: str, identity, Src: Mapping, Dst: Mapping,
                allow_broadcast: bool = False) -> Storage:
-        out = Storage(self, src.dtype, Dst.size, zero=False)
+        """A row reduction of a deferred elementwise value comes back lazy when row programs are on:
+        it runs when its value is needed, or inside the row program of a consumer of its broadcast."""
         if src.dtype == "i32":
             bits = int(np.int32(identity).view(np.uint32))
         elif src.dtype == "bf16":
             bits = int(np.uint32(dtypes.f32_to_bf16_bits(np.float32(identity))) << 16)
         else:
             bits = int(np.float32(identity).view(np.uint32))
-        if src.lazy is not None and src.lazy[0] == "ew" and not allow_broadcast:
-            _, prog, leaves = src.lazy
+        if (self.fuse and self.row_fusion and src.lazy is not None and src.lazy[0] == "ew" and not allow_broadcast
+                and src.dtype in self.DEFER):
+            rows, W = C.c_int64(), C.c_int64()
+            st = _lib.lib().fopt_row_reduce_shape(self.ctx, Src.handle, Dst.handle, C.byref(rows), C.byref(W))
+            if st == 0 and rows.value == Dst.size:
+                return Storage(self, src.dtype, Dst.size,
+                               lazy=("red", src, op, bits, Src, Dst, rows.value, W.value))
+            if st not in (0, _lib.FOPT_ERR_UNSUPPORTED):
+                check(st, self.ctx)
+        out = Storage(self, src.dtype, Dst.size, zero=False)
+        self._run_reduce(out, src, op, bits, Src, Dst, allow_broadcast)
+        return out
+
+    def _run_reduce(self, out: Storage, src: Storage, op: str, bits: int, Src: Mapping, Dst: Mapping,
+                    allow_broadcast: bool = False) -> None:
+        if src.lazy is not None and src.lazy[0] == "ew" and not allow_broadcast and len(src.lazy[2]) <= 3:
+            _, prog, leaves, _ = src.lazy
             ptrs, dts, codes, _ = self._leaf_args(leaves)
-            st = _lib.lib().fopt_reduce_map(self.ctx, out.ptr, C.byref(prog), len(leaves), ptrs, dts, codes,
+            st = _lib.lib().fopt_reduce_map(self.ctx, out._ptr, C.byref(prog), len(leaves), ptrs, dts, codes,
                                             _lib.DTYPES[src.dtype], REDUCE_OPS[op], bits, Src.handle, Dst.handle)
             if st == 0:
-                return out
+                return
             if st != _lib.FOPT_ERR_UNSUPPORTED:
                 check(st, self.ctx)
-        check(_lib.lib().fopt_reduce(self.ctx, out.ptr, src.ptr, _lib.DTYPES[src.dtype], REDUCE_OPS[op], bits,
+        check(_lib.lib().fopt_reduce(self.ctx, out._ptr, src.ptr, _lib.DTYPES[src.dtype], REDUCE_OPS[op], bits,
                                      Src.handle, Dst.handle, int(allow_broadcast)), self.ctx)
-        return out
 
     # ---- contraction (backend/mod.rs:135-157) ----
     ACC = {"i8": "i32", "i4": "i32", "i5": "i32", "i9": "i32", "bf16": "f32", "f8e4m3": "f32", "f8e5m2": "f32"}

@@ -8,6 +8,8 @@
 #include <cstring>
 #include <sstream>
 
+#include <unordered_set>
+
 #include "ctx.hpp"
 
 using namespace fopt;
@@ -95,6 +97,15 @@ std::vector<std::pair<std::string, int64_t>> parse_offset(const std::string& s) 
 }
 
 }  // namespace
+
+struct fopt_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::unordered_set<void*> owned;  // allocations of the capture that it did not free
+  bool launched = false;
+  int64_t kernels = 0;              // kernels the captured step launches (counted per replay)
+  int64_t launches_before = 0;
+};
 
 extern "C" {
 
@@ -189,6 +200,7 @@ fopt_status fopt_alloc(fopt_ctx* ctx, size_t bytes, void** dptr) {
   return guarded(ctx, [&] {
     require(dptr != nullptr, "fopt_alloc: null out pointer");
     cuda_check(cudaMallocAsync(dptr, std::max<size_t>(bytes, 1), ctx->stream), "cudaMallocAsync");
+    if (ctx->capture) ctx->capture->owned.insert(*dptr);
     cuda_check(cudaMemsetAsync(*dptr, 0, std::max<size_t>(bytes, 1), ctx->stream), "zero fill");
   });
 }
@@ -197,12 +209,101 @@ fopt_status fopt_alloc_uninit(fopt_ctx* ctx, size_t bytes, void** dptr) {
   return guarded(ctx, [&] {
     require(dptr != nullptr, "fopt_alloc_uninit: null out pointer");
     cuda_check(cudaMallocAsync(dptr, std::max<size_t>(bytes, 1), ctx->stream), "cudaMallocAsync");
+    if (ctx->capture) ctx->capture->owned.insert(*dptr);
   });
 }
 
 fopt_status fopt_free(fopt_ctx* ctx, void* dptr) {
+  if (!ctx) return FOPT_ERR_INVALID;
   return guarded(ctx, [&] {
-    if (dptr) cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");
+    if (!dptr) return;
+    if (ctx->capture) {
+      if (ctx->capture->owned.erase(dptr))
+        cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");  // a free node of the graph
+      else
+        ctx->deferred_free.push_back(dptr);  // memory from before the capture: released after it
+      return;
+    }
+    auto it = ctx->graph_mem.find(dptr);
+    if (it != ctx->graph_mem.end()) {  // a graph's allocation: it is no longer the graph's to release
+      fopt_graph* g = it->second;
+      ctx->graph_mem.erase(it);
+      g->owned.erase(dptr);
+      if (!g->launched) return;  // never mapped
+    }
+    cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");
+  });
+}
+
+// ---- CUDA graphs of whole steps ----
+// A step (for example a decoder block's forward) issued between fopt_capture_begin and
+// fopt_capture_end is recorded from the context's stream into a CUDA graph instead of run; each
+// fopt_graph_launch then replays every kernel, copy and stream-ordered allocation of the step in
+// one call, without the host work that issued them. Allocations made during the capture become the
+// graph's own: those freed during it are released inside the graph, the others (the step's
+// outputs) keep their addresses across launches and are released when the graph is launched again
+// or destroyed.
+fopt_status fopt_capture_begin(fopt_ctx* ctx) {
+  return guarded(ctx, [&] {
+    require(!ctx->capture, "fopt_capture_begin: a capture is already open");
+    require(ctx->stream != nullptr, "fopt_capture_begin: the legacy default stream cannot be captured");
+    auto* g = new fopt_graph;
+    cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeRelaxed);
+    if (e != cudaSuccess) {
+      delete g;
+      cuda_check(e, "cudaStreamBeginCapture");
+    }
+    g->launches_before = ctx->launches;
+    ctx->capture = g;
+  });
+}
+
+fopt_status fopt_capture_end(fopt_ctx* ctx, fopt_graph** out) {
+  return guarded(ctx, [&] {
+    require(ctx->capture && out, "fopt_capture_end: no capture is open");
+    fopt_graph* g = ctx->capture;
+    ctx->capture = nullptr;
+    *out = nullptr;
+    g->kernels = ctx->launches - g->launches_before;  // recorded, not run
+    ctx->launches = g->launches_before;
+    cudaError_t e = cudaStreamEndCapture(ctx->stream, &g->graph);
+    if (e == cudaSuccess)
+      e = cudaGraphInstantiateWithFlags(&g->exec, g->graph, cudaGraphInstantiateFlagAutoFreeOnLaunch);
+    for (void* p : ctx->deferred_free) cudaFreeAsync(p, ctx->stream);
+    ctx->deferred_free.clear();
+    if (e != cudaSuccess) {
+      if (g->graph) cudaGraphDestroy(g->graph);
+      delete g;
+      cuda_check(e, "graph capture");
+    }
+    for (void* p : g->owned) ctx->graph_mem[p] = g;
+    *out = g;
+  });
+}
+
+fopt_status fopt_graph_launch(fopt_ctx* ctx, fopt_graph* g) {
+  return guarded(ctx, [&] {
+    require(g && g->exec, "fopt_graph_launch: no graph");
+    require(!ctx->capture, "fopt_graph_launch: a capture is open");
+    cuda_check(cudaGraphLaunch(g->exec, ctx->stream), "cudaGraphLaunch");
+    g->launched = true;
+    ctx->launches += g->kernels;
+  });
+}
+
+fopt_status fopt_graph_destroy(fopt_ctx* ctx, fopt_graph* g) {
+  if (!g) return FOPT_OK;
+  return guarded(ctx, [&] {
+    cuda_check(cudaStreamSynchronize(ctx->stream), "sync");
+    for (void* p : g->owned) {
+      ctx->graph_mem.erase(p);
+      if (g->launched) cudaFreeAsync(p, ctx->stream);  // the last launch's allocations still live
+    }
+    cudaGetLastError();  // a release the runtime had already done reports here, not at the next launch
+    cuda_check(cudaStreamSynchronize(ctx->stream), "sync");
+    if (g->exec) cudaGraphExecDestroy(g->exec);
+    if (g->graph) cudaGraphDestroy(g->graph);
+    delete g;
   });
 }
 
@@ -408,7 +509,7 @@ fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst
 static std::shared_ptr<FoldKPlan> reduce_plan(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                                               int allow_broadcast) {
   std::string key = "r|" + src_map->key + "|" + dst_map->key + "|" + std::to_string(allow_broadcast);
-  {
+  if (ctx) {
     std::lock_guard<std::mutex> g(ctx->mu);
     auto it = ctx->folds.find(key);
     if (it != ctx->folds.end()) return it->second;
@@ -418,6 +519,7 @@ static std::shared_ptr<FoldKPlan> reduce_plan(fopt_ctx* ctx, const fopt_mapping*
   if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
     throw Fail{FOPT_ERR_UNSUPPORTED, "reduce: mappings are not affine-factorisable"};
   auto kp = std::make_shared<FoldKPlan>(to_kfold(fp));
+  if (!ctx) return kp;  // host-only query (fopt_row_reduce_shape without a context)
   std::lock_guard<std::mutex> g(ctx->mu);
   ctx->folds[key] = kp;
   return kp;
@@ -432,6 +534,47 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
     auto kp = reduce_plan(ctx, src_map, dst_map, allow_broadcast);
     launch_reduce(ctx, *kp, out, src, dtype, op, identity_bits, src_map->m.size());
   });
+}
+
+// A plain row reduction: dst cell t folds src cells t * W .. t * W + W - 1.
+static bool plain_row_reduce(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map, int64_t* rows,
+                             int64_t* W) {
+  auto kp = reduce_plan(ctx, src_map, dst_map, 0);
+  const KWalk &o = kp->out, &r = kp->residue;
+  if (o.n != 1 || r.n != 1 || o.live[0] != o.extent[0] || r.live[0] != r.extent[0] || r.stride[0][0] != 1 ||
+      o.stride[0][0] != r.extent[0] || kp->out_positions != o.extent[0] ||
+      src_map->m.size() != o.extent[0] * r.extent[0])
+    return false;
+  *rows = o.extent[0];
+  *W = r.extent[0];
+  return true;
+}
+
+fopt_status fopt_row_reduce_shape(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                  int64_t* rows, int64_t* row_len) {
+  bool ok = false;
+  fopt_status st = guarded(ctx, [&] {
+    require(src_map && dst_map && rows && row_len, "fopt_row_reduce_shape: bad arguments");
+    ok = plain_row_reduce(ctx, src_map, dst_map, rows, row_len);
+  });
+  if (st == FOPT_OK && !ok) {
+    if (ctx) ctx->err = "fopt_row_reduce_shape: not a plain row reduction";
+    return FOPT_ERR_UNSUPPORTED;
+  }
+  return st;
+}
+
+fopt_status fopt_row_program(fopt_ctx* ctx, const fopt_row_plan* plan) {
+  bool ran = false;
+  fopt_status st = guarded(ctx, [&] {
+    require(plan && plan->out, "fopt_row_program: bad arguments");
+    ran = launch_row_jit(ctx, *plan);
+  });
+  if (st == FOPT_OK && !ran) {
+    ctx->err = "fopt_row_program: no generated kernel for this plan";
+    return FOPT_ERR_UNSUPPORTED;
+  }
+  return st;
 }
 
 fopt_status fopt_reduce_map(fopt_ctx* ctx, void* out, const fopt_program* prog, int32_t n_in, const void* const* inputs,
@@ -455,15 +598,9 @@ fopt_status fopt_reduce_map(fopt_ctx* ctx, void* out, const fopt_program* prog, 
       else if (op == FOPT_RED_MIN) fold = 13;
     }
     if (fold < 0) return;
-    // a plain row reduction: dst cell t folds src cells t * W .. t * W + W - 1
-    auto kp = reduce_plan(ctx, src_map, dst_map, 0);
-    const KWalk &o = kp->out, &r = kp->residue;
-    if (o.n != 1 || r.n != 1 || o.live[0] != o.extent[0] || r.live[0] != r.extent[0] || r.stride[0][0] != 1 ||
-        o.stride[0][0] != r.extent[0] || kp->out_positions != o.extent[0] ||
-        src_map->m.size() != o.extent[0] * r.extent[0])
-      return;
-    ran = launch_reduce_map_jit(ctx, prog, n_in, inputs, in_dtypes, bcast, fold, identity_bits, out, o.extent[0],
-                                r.extent[0]);
+    int64_t rows = 0, W = 0;
+    if (!plain_row_reduce(ctx, src_map, dst_map, &rows, &W)) return;
+    ran = launch_reduce_map_jit(ctx, prog, n_in, inputs, in_dtypes, bcast, fold, identity_bits, out, rows, W);
   });
   if (st == FOPT_OK && !ran) {
     ctx->err = "fopt_reduce_map: no fused kernel for this reduction";

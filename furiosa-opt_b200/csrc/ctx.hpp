@@ -38,8 +38,13 @@ struct FoldKPlan {
 
 }  // namespace fopt
 
+struct fopt_graph;
+
 struct fopt_ctx {
   int device = 0;
+  fopt_graph* capture = nullptr;        // the step being captured into a CUDA graph, if any
+  std::vector<void*> deferred_free;     // frees of pre-capture memory requested during a capture
+  std::map<void*, fopt_graph*> graph_mem;  // allocations that belong to a captured graph
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   int exact_fold = 0;
@@ -117,6 +122,7 @@ void launch_relayout(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void
 void launch_transmute(fopt_ctx* ctx, const RankWalk& src, const RankWalk& dst, void* out, const void* in, int dtype);
 bool launch_elementwise_jit_ex(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                                const fopt_dtype* in_dt, const int64_t* bcast, void* out, fopt_dtype out_dt, int64_t n);
+bool launch_row_jit(fopt_ctx* ctx, const fopt_row_plan& plan);
 bool launch_reduce_map_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                            const fopt_dtype* in_dt, const int64_t* bcast, int fold, uint32_t ident, void* out,
                            int64_t rows, int64_t W);

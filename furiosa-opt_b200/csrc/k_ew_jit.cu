@@ -17,6 +17,7 @@
 #include <sstream>
 #include <cstring>
 #include <string>
+#include <vector>
 
 #include "ctx.hpp"
 #include "ew_ops.cuh"
@@ -178,10 +179,11 @@ int arity_of(int op) {
 // Emits the program's instructions for element e of inputs x0..x2 (one scoped block per
 // instruction, every value in a named register); *ret names the result. False for an opcode the
 // table lacks.
-bool emit_program(std::ostringstream& o, const fopt_program& p, int n_in, std::string* ret) {
+bool emit_program_named(std::ostringstream& o, const fopt_program& p, const std::string* inputs, int n_in,
+                        std::string* ret, const std::string& tag = "t") {
   std::string name[16];
   for (int v = 0; v < 16; ++v) name[v] = "0u";
-  for (int k = 0; k < n_in; ++k) name[k] = "x" + std::to_string(k) + "[e]";
+  for (int k = 0; k < n_in && k < 16; ++k) name[k] = inputs[k];
   for (int i = 0; i < p.n_insn; ++i) {
     const fopt_insn& in = p.insn[i];
     const char* expr = op_expr(in.op);
@@ -189,7 +191,7 @@ bool emit_program(std::ostringstream& o, const fopt_program& p, int n_in, std::s
     const int ar = arity_of(in.op);
     const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
                       C = ar > 2 ? name[in.c & 15] : "0u";
-    const std::string t = "t" + std::to_string(i);
+    const std::string t = tag + std::to_string(i);
     o << "      unsigned " << t << "; { const unsigned a = " << A << ", b = " << B << ", c = " << C
       << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
       << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << " = ("
@@ -198,6 +200,12 @@ bool emit_program(std::ostringstream& o, const fopt_program& p, int n_in, std::s
   }
   *ret = name[p.ret & 15];
   return true;
+}
+
+bool emit_program(std::ostringstream& o, const fopt_program& p, int n_in, std::string* ret) {
+  std::string names[16];
+  for (int k = 0; k < n_in && k < 16; ++k) names[k] = "x" + std::to_string(k) + "[e]";
+  return emit_program_named(o, p, names, n_in, ret);
 }
 
 // Loads the 8 elements at `base` of every input into x0..x2 (modes as for generate below).
@@ -307,9 +315,11 @@ CUfunction kernel_for(fopt_ctx* ctx, const fopt_program& p, int n_in, const fopt
   return compiled(key, [&] { return generate(p, n_in, in_dt, out_dt, modes); }, "fopt_ew_gen");
 }
 
-// A row reduction of the program's values: one warp per row of W elements (W a multiple of 8),
-// lane-strided 8-element groups folded into a per-lane accumulator, then a butterfly across the
-// warp. fold: 0 f32 add, 2 max, 3 min, 4 f32 mul (f32 values), 10 i32 wrapping add, 12 / 13 i32
+// A row reduction of the program's values: one warp per row of W elements (W a multiple of 8), in
+// a fixed order that does not depend on the launch: 8-element group g of the row goes to slot
+// g % 256 and each slot folds its groups in order (lane L keeps slots L + 32 j, j < 8, in acc[j]);
+// a butterfly folds each set of 32 slots, then the 8 results fold in order j = 0 .. 7. The row
+// programs (generate_row) fold in the same order with one thread per slot. fold: 0 f32 add, 2 max, 3 min, 4 f32 mul (f32 values), 10 i32 wrapping add, 12 / 13 i32
 // max / min.
 std::string generate_reduce(const fopt_program& p, int n_in, const fopt_dtype* in_dt, const int* modes, int fold) {
   std::ostringstream o;
@@ -332,20 +342,257 @@ std::string generate_reduce(const fopt_program& p, int n_in, const fopt_dtype* i
     << "  const int lane = threadIdx.x & 31;\n"
     << "  const long long nw = ((long long)gridDim.x * blockDim.x) >> 5;\n"
     << "  for (long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {\n"
-    << "    unsigned acc = ident;\n"
-    << "    for (long long c = 8 * lane; c < row_len; c += 256) {\n"
+    << "    unsigned acc[8];\n"
+    << "#pragma unroll\n    for (int j = 0; j < 8; ++j) acc[j] = ident;\n"
+    << "    for (long long c0 = 8 * lane; c0 < row_len; c0 += 2048) {\n"
+    << "#pragma unroll\n    for (int j = 0; j < 8; ++j) {\n"
+    << "      const long long c = c0 + 256 * j;\n"
+    << "      if (c >= row_len) break;\n"
     << "      const long long base = row * row_len + c;\n"
     << "      unsigned x0[8], x1[8], x2[8];\n";
   emit_loads(o, n_in, in_dt, modes);
   o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) {\n";
   std::string ret;
   if (!emit_program(o, p, n_in, &ret)) return "";
-  o << "        acc = fold(acc, " << ret << ");\n      }\n    }\n"
-    << "#pragma unroll\n    for (int m = 16; m; m >>= 1) acc = fold(acc, __shfl_xor_sync(0xffffffffu, acc, m));\n"
-    << "    if (lane == 0) out[row] = acc;\n  }\n}\n";
+  o << "        acc[j] = fold(acc[j], " << ret << ");\n      }\n    }\n    }\n"
+    << "#pragma unroll\n    for (int j = 0; j < 8; ++j)\n"
+    << "#pragma unroll\n      for (int m = 16; m; m >>= 1) acc[j] = fold(acc[j], __shfl_xor_sync(0xffffffffu, acc[j], m));\n"
+    << "    unsigned r = acc[0];\n"
+    << "#pragma unroll\n    for (int j = 1; j < 8; ++j) r = fold(r, acc[j]);\n"
+    << "    if (lane == 0) out[row] = r;\n  }\n}\n";
   return o.str();
 }
 
+
+// ---- row programs ----
+const char* fold_expr(int fold) {
+  switch (fold) {
+    case 0: return "W(__fadd_rn(F(u), F(v)))";
+    case 2: return "W(fmaxf(F(u), F(v)))";
+    case 3: return "W(fminf(F(u), F(v)))";
+    case 4: return "W(__fmul_rn(F(u), F(v)))";
+    case 10: return "(u + v)";
+    case 12: return "(unsigned)max((int)u, (int)v)";
+    case 13: return "(unsigned)min((int)u, (int)v)";
+    default: return nullptr;
+  }
+}
+
+// Which of the first n registers the program reads before writing them (its inputs in use).
+unsigned inputs_read(const fopt_program& p, int n) {
+  unsigned used = 0, written = 0;
+  for (int i = 0; i < p.n_insn; ++i) {
+    const fopt_insn& in = p.insn[i];
+    const int ar = arity_of(in.op), rs[3] = {in.a & 15, in.b & 15, in.c & 15};
+    for (int q = 0; q < ar; ++q)
+      if (rs[q] < n && !(written >> rs[q] & 1)) used |= 1u << rs[q];
+    written |= 1u << (in.dst & 15);
+  }
+  if ((p.ret & 15) < n && !(written >> (p.ret & 15) & 1)) used |= 1u << (p.ret & 15);
+  return used;
+}
+
+// words (32-bit) of one 8-element group of a leaf held raw
+int raw_words(int dt) { return dtype_bits(dt) / 4; }
+
+std::string raw_load(int k, int dt, const std::string& dst) {
+  const std::string in = "in" + std::to_string(k);
+  std::ostringstream o;
+  switch (dtype_bits(dt)) {
+    case 32:
+      o << "{ const uint4* q = (const uint4*)" << in << " + (base >> 2); const uint4 u0 = q[0], u1 = q[1]; " << dst
+        << "[0]=u0.x; " << dst << "[1]=u0.y; " << dst << "[2]=u0.z; " << dst << "[3]=u0.w; " << dst << "[4]=u1.x; "
+        << dst << "[5]=u1.y; " << dst << "[6]=u1.z; " << dst << "[7]=u1.w; }\n";
+      break;
+    case 16:
+      o << "{ const uint4 u = *((const uint4*)" << in << " + (base >> 3)); " << dst << "[0]=u.x; " << dst << "[1]=u.y; "
+        << dst << "[2]=u.z; " << dst << "[3]=u.w; }\n";
+      break;
+    default:
+      o << "{ const uint2 u = *((const uint2*)" << in << " + (base >> 3)); " << dst << "[0]=u.x; " << dst
+        << "[1]=u.y; }\n";
+  }
+  return o.str();
+}
+
+// x[0..7] from the raw words of one group (the element forms load_vec gives)
+std::string raw_unpack(int dt, const std::string& raw, const std::string& x) {
+  std::ostringstream o;
+  switch (dtype_bits(dt)) {
+    case 32: o << "for (int j = 0; j < 8; ++j) " << x << "[j] = " << raw << "[j];\n"; break;
+    case 16:
+      if (dt == FOPT_BF16)
+        o << "for (int j = 0; j < 4; ++j) { " << x << "[2*j] = " << raw << "[j] << 16; " << x << "[2*j+1] = " << raw
+          << "[j] & 0xffff0000u; }\n";
+      else
+        o << "for (int j = 0; j < 4; ++j) { " << x << "[2*j] = (unsigned)(int)(short)(" << raw << "[j] & 0xffffu); "
+          << x << "[2*j+1] = (unsigned)((int)" << raw << "[j] >> 16); }\n";
+      break;
+    default: {
+      const bool sgn = dt == FOPT_I8 || dt == FOPT_I5;
+      o << "for (int j = 0; j < 8; ++j) { const unsigned b = (" << raw << "[j >> 2] >> (8 * (j & 3))) & 0xffu; " << x
+        << "[j] = " << (sgn ? "(unsigned)(int)(signed char)b" : "b") << "; }\n";
+    }
+  }
+  return o.str();
+}
+
+std::string load_at(int dt, const std::string& ptr, const std::string& i) {
+  switch (dt) {
+    case FOPT_I32: case FOPT_F32: return "((const unsigned*)" + ptr + ")[" + i + "]";
+    case FOPT_BF16: return "(((unsigned)((const unsigned short*)" + ptr + ")[" + i + "]) << 16)";
+    case FOPT_I16: case FOPT_I9: return "((unsigned)(int)((const short*)" + ptr + ")[" + i + "])";
+    case FOPT_I8: case FOPT_I5: return "((unsigned)(int)((const signed char*)" + ptr + ")[" + i + "])";
+    default: return "((unsigned)((const unsigned char*)" + ptr + ")[" + i + "])";
+  }
+}
+
+// One CTA of 256 threads per row; thread t owns the 8-element groups t + 256 kc (kc < KC), which is
+// slot t of the fold order generate_reduce documents. Passes: one per FOLD slot, then the final
+// program. Leaves read in a later pass are kept raw in registers when they fit, else read again
+// (from cache); held values are computed in the first pass and kept.
+std::string generate_row(const fopt_row_plan& P, const int* folds) {
+  const int nL = P.n_leaves, nH = P.n_held, nS = P.n_slots;
+  const int64_t W = P.row_len;
+  const int KC = (int)((W + 2047) / 2048);
+  std::ostringstream o;
+  int modes[FOPT_ROW_MAX_LEAVES];
+  for (int k = 0; k < nL; ++k) modes[k] = P.leaf_bcast[k] == 0 ? 0 : P.leaf_bcast[k] > 0 ? 1 : 2;
+  // passes and the leaves each reads
+  std::vector<int> pass_slot;  // FOLD slot index per pass, -1 for the final
+  for (int j = 0; j < nS; ++j)
+    if (P.slot[j].kind == FOPT_ROW_FOLD) pass_slot.push_back(j);
+  pass_slot.push_back(-1);
+  const int nE = nL + nH + nS;
+  auto pass_prog = [&](int j) -> const fopt_program& { return j < 0 ? *P.final_prog : *P.slot[j].prog; };
+  unsigned later_leaves = 0, held_leaves = 0;
+  for (size_t q = 1; q < pass_slot.size(); ++q) later_leaves |= inputs_read(pass_prog(pass_slot[q]), nE) & ((1u << nL) - 1);
+  for (int h = 0; h < nH; ++h) held_leaves |= inputs_read(*P.held[h], nL);
+  int keep_words = nH * 8;
+  unsigned keep_raw = 0;  // mode-0 leaves read again later, kept raw when the registers allow
+  for (int k = 0; k < nL; ++k)
+    if ((later_leaves >> k & 1) && modes[k] == 0 && (keep_words + raw_words(P.leaf_dtype[k])) * KC <= 64) {
+      keep_raw |= 1u << k;
+      keep_words += raw_words(P.leaf_dtype[k]);
+    }
+  if (nH * 8 * KC > 64) return "";  // held values must fit in registers
+  o << kPrelude << "\nusing namespace fopt::ew;\n";
+  for (int j = 0; j < nS; ++j)
+    if (P.slot[j].kind == FOPT_ROW_FOLD)
+      o << "__device__ __forceinline__ unsigned fold" << j << "(unsigned u, unsigned v) { return " << fold_expr(folds[j])
+        << "; }\n";
+  o << "struct RowArgs { const void* in[8]; long long b[8]; const void* ld[8]; void* so[8]; void* out; long long rows; };\n"
+    << "extern \"C\" __global__ void __launch_bounds__(256) fopt_row_gen(const RowArgs a) {\n"
+    << "  constexpr long long RL = " << W << "LL;\n  constexpr int KC = " << KC << ";\n"
+    << "  __shared__ unsigned part[" << std::max<size_t>(1, pass_slot.size() - 1) << "][8];\n"
+    << "  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;\n  (void)lane; (void)warp;\n"
+    << "  void* const out = a.out;\n  (void)out;\n";
+  for (int k = 0; k < nL; ++k)
+    o << "  const void* const in" << k << " = a.in[" << k << "]; const long long b" << k << " = a.b[" << k
+      << "]; (void)b" << k << ";\n";
+  o << "  for (long long row = blockIdx.x; row < a.rows; row += gridDim.x) {\n";
+  for (int k = 0; k < nL; ++k)
+    if (keep_raw >> k & 1) o << "    unsigned raw" << k << "[KC][" << raw_words(P.leaf_dtype[k]) << "];\n";
+  for (int h = 0; h < nH; ++h) o << "    unsigned hv" << h << "[KC][8];\n";
+  for (int j = 0; j < nS; ++j) o << "    unsigned s" << j << " = 0u;\n";
+  std::string names[16];
+  for (int k = 0; k < nL; ++k) names[k] = "x" + std::to_string(k) + "[e]";
+  for (int h = 0; h < nH; ++h) names[nL + h] = "hv" + std::to_string(h) + "[kc][e]";
+  for (int j = 0; j < nS; ++j) names[nL + nH + j] = "s" + std::to_string(j);
+  std::string snames[16];
+  for (int j = 0; j < nS; ++j) snames[j] = "s" + std::to_string(j);
+  size_t pass = 0;
+  int nfold = 0;
+  auto emit_pass = [&](int j) -> bool {
+    const bool first = pass == 0;
+    const fopt_program& prog = pass_prog(j);
+    unsigned need = inputs_read(prog, nE) & ((1u << nL) - 1);
+    if (first) need |= held_leaves;
+    o << "    {\n";
+    if (j >= 0) o << "    unsigned acc = " << P.slot[j].identity_bits << "u;\n";
+    o << "#pragma unroll\n    for (int kc = 0; kc < KC; ++kc) {\n"
+      << "      const long long c = 8 * t + 2048 * kc;\n      if (c < RL) {\n"
+      << "      const long long base = row * RL + c;\n";
+    for (int k = 0; k < nL; ++k) {
+      if (!(need >> k & 1) && !(first && (keep_raw >> k & 1))) continue;
+      const std::string xk = "x" + std::to_string(k), bk = "b" + std::to_string(k);
+      o << "      unsigned " << xk << "[8];\n";
+      if (keep_raw >> k & 1) {
+        const std::string raw = "raw" + std::to_string(k) + "[kc]";
+        if (first) o << "      " << raw_load(k, P.leaf_dtype[k], raw);
+        o << "#pragma unroll\n      " << raw_unpack(P.leaf_dtype[k], raw, xk);
+      } else if (modes[k] == 1) {
+        o << "      { const unsigned v = " << load_one(k, P.leaf_dtype[k], "base / " + bk) << "; for (int e = 0; e < 8; ++e) "
+          << xk << "[e] = v; }\n";
+      } else {
+        o << "      " << load_vec(k, P.leaf_dtype[k], modes[k] == 2 ? "base % " + bk : "base");
+      }
+    }
+    if (j < 0) o << "      unsigned r[8];\n";
+    o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) {\n";
+    if (first) {
+      for (int h = 0; h < nH; ++h) {
+        std::string ret;
+        if (!emit_program_named(o, *P.held[h], names, nL, &ret, "h" + std::to_string(h) + "_")) return false;
+        o << "        hv" << h << "[kc][e] = " << ret << ";\n";
+      }
+    }
+    std::string ret;
+    if (!emit_program_named(o, prog, names, nE, &ret)) return false;
+    if (j >= 0)
+      o << "        acc = fold" << j << "(acc, " << ret << ");\n      }\n";
+    else
+      o << "        r[e] = " << ret << ";\n      }\n      " << store_vec(P.out_dtype);
+    o << "      }\n    }\n";
+    if (j >= 0) {
+      o << "#pragma unroll\n    for (int m = 16; m; m >>= 1) acc = fold" << j << "(acc, __shfl_xor_sync(0xffffffffu, acc, m));\n"
+        << "    if (lane == 0) part[" << nfold << "][warp] = acc;\n    __syncthreads();\n"
+        << "    s" << j << " = part[" << nfold << "][0];\n"
+        << "#pragma unroll\n    for (int w = 1; w < 8; ++w) s" << j << " = fold" << j << "(s" << j << ", part[" << nfold
+        << "][w]);\n";
+      ++nfold;
+    }
+    o << "    }\n";
+    ++pass;
+    return true;
+  };
+  for (int j = 0; j < nS; ++j) {
+    const fopt_row_slot& sl = P.slot[j];
+    if (sl.kind == FOPT_ROW_FOLD) {
+      if (!emit_pass(j)) return "";
+    } else if (sl.kind == FOPT_ROW_SCALAR) {
+      o << "    {\n";
+      std::string ret;
+      if (!emit_program_named(o, *sl.prog, snames, j, &ret, "q" + std::to_string(j) + "_")) return "";
+      o << "    s" << j << " = " << ret << ";\n    }\n";
+    } else {
+      o << "    s" << j << " = " << load_at(sl.dtype, "a.ld[" + std::to_string(j) + "]", "row") << ";\n";
+    }
+    if (sl.kind != FOPT_ROW_LOAD)
+      o << "    if (t == 0 && a.so[" << j << "]) ((unsigned*)a.so[" << j << "])[row] = s" << j << ";\n";
+  }
+  if (!emit_pass(-1)) return "";
+  o << "    __syncthreads();\n  }\n}\n";
+  return o.str();
+}
+
+std::string row_key(const fopt_row_plan& P, const int* folds) {
+  auto prog_bytes = [](const fopt_program* p) {
+    return p ? std::string((const char*)p, sizeof(int32_t) * 2 + sizeof(fopt_insn) * p->n_insn) : std::string("-");
+  };
+  std::string key = "row|" + std::to_string(P.row_len) + "|" + std::to_string(P.out_dtype) + "|";
+  for (int k = 0; k < P.n_leaves; ++k)
+    key += std::to_string(P.leaf_dtype[k]) + "/" + std::to_string(P.leaf_bcast[k] == 0 ? 0 : P.leaf_bcast[k] > 0 ? 1 : 2) + ",";
+  key += "|";
+  for (int h = 0; h < P.n_held; ++h) key += prog_bytes(P.held[h]) + "#";
+  key += "|";
+  for (int j = 0; j < P.n_slots; ++j) {
+    const fopt_row_slot& sl = P.slot[j];
+    key += std::to_string(sl.kind) + ":" + std::to_string(folds[j]) + ":" + std::to_string(sl.identity_bits) + ":" +
+           std::to_string(sl.dtype) + ":" + (sl.kind == FOPT_ROW_LOAD ? std::string("-") : prog_bytes(sl.prog)) + "#";
+  }
+  return key + "|" + prog_bytes(P.final_prog);
+}
 }  // namespace
 
 std::atomic<int64_t> g_jit_launches{0};
@@ -427,6 +674,93 @@ bool launch_reduce_map_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, co
   return true;
 }
 
+
+// The fold code (generate_reduce's numbering) of a reduce op on a 32-bit value type, -1 if none.
+int row_fold_code(int dtype, int op, bool exact) {
+  if (dtype == FOPT_F32) {
+    if (op == FOPT_RED_MAX) return 2;
+    if (op == FOPT_RED_MIN) return 3;
+    if (!exact && op == FOPT_RED_ADD) return 0;
+    if (!exact && op == FOPT_RED_MUL) return 4;
+  } else if (dtype == FOPT_I32) {
+    if (op == FOPT_RED_ADD) return 10;
+    if (op == FOPT_RED_MAX) return 12;
+    if (op == FOPT_RED_MIN) return 13;
+  }
+  return -1;
+}
+
+// Validates a row plan's shape and fills the fold codes; false when the generated kernel does not
+// apply to it (pointers are not looked at).
+bool row_plan_supported(const fopt_row_plan& P, bool exact, int* folds) {
+  if (P.n_leaves < 0 || P.n_leaves > FOPT_ROW_MAX_LEAVES || P.n_held < 0 || P.n_held > FOPT_ROW_MAX_HELD ||
+      P.n_slots < 0 || P.n_slots > FOPT_ROW_MAX_SLOTS || P.n_leaves + P.n_held + P.n_slots > 16)
+    return false;
+  if (P.row_len <= 0 || P.row_len % 8 || P.row_len > 32768 || P.rows <= 0 || !P.final_prog) return false;
+  if (dtype_bits(P.out_dtype) < 8) return false;
+  for (int k = 0; k < P.n_leaves; ++k) {
+    if (dtype_bits(P.leaf_dtype[k]) < 8) return false;
+    const int64_t b = P.leaf_bcast[k] < 0 ? -P.leaf_bcast[k] : P.leaf_bcast[k];
+    if (b && b % 8) return false;
+  }
+  for (int h = 0; h < P.n_held; ++h)
+    if (!P.held[h] || P.held[h]->n_insn > 32) return false;
+  for (int j = 0; j < P.n_slots; ++j) {
+    const fopt_row_slot& sl = P.slot[j];
+    folds[j] = -1;
+    if (sl.kind == FOPT_ROW_FOLD) {
+      if (!sl.prog || sl.prog->n_insn > 32 || (folds[j] = row_fold_code(sl.dtype, sl.op, exact)) < 0) return false;
+    } else if (sl.kind == FOPT_ROW_SCALAR) {
+      if (!sl.prog || sl.prog->n_insn > 32 || (sl.dtype != FOPT_F32 && sl.dtype != FOPT_I32)) return false;
+    } else if (sl.kind == FOPT_ROW_LOAD) {
+      if (dtype_bits(sl.dtype) < 8) return false;
+    } else {
+      return false;
+    }
+  }
+  return P.final_prog->n_insn <= 32;
+}
+
+bool launch_row_jit(fopt_ctx* ctx, const fopt_row_plan& P) {
+  if (getenv("FOPT_EW_NO_JIT")) return false;
+  int folds[FOPT_ROW_MAX_SLOTS];
+  if (!row_plan_supported(P, ctx->exact_fold, folds)) return false;
+  if ((uintptr_t)P.out % 16) return false;
+  for (int k = 0; k < P.n_leaves; ++k)
+    if (!P.leaf[k] || (uintptr_t)P.leaf[k] % 16) return false;
+  for (int j = 0; j < P.n_slots; ++j) {
+    if (P.slot[j].kind == FOPT_ROW_LOAD && !P.slot[j].src) return false;
+    if (P.slot[j].out && (uintptr_t)P.slot[j].out % 4) return false;
+  }
+  const std::string key = row_key(P, folds) + "|" + std::to_string(ctx->device);
+  CUfunction fn = compiled(key, [&] { return generate_row(P, folds); }, "fopt_row_gen");
+  if (!fn) return false;
+  struct RowArgs {
+    const void* in[8];
+    long long b[8];
+    const void* ld[8];
+    void* so[8];
+    void* out;
+    long long rows;
+  } args{};
+  for (int k = 0; k < P.n_leaves; ++k) {
+    args.in[k] = P.leaf[k];
+    args.b[k] = P.leaf_bcast[k] < 0 ? -P.leaf_bcast[k] : P.leaf_bcast[k];
+  }
+  for (int j = 0; j < P.n_slots; ++j) {
+    args.ld[j] = P.slot[j].kind == FOPT_ROW_LOAD ? P.slot[j].src : nullptr;
+    args.so[j] = P.slot[j].kind == FOPT_ROW_LOAD ? nullptr : P.slot[j].out;
+  }
+  args.out = P.out;
+  args.rows = P.rows;
+  void* params[] = {(void*)&args};
+  const unsigned grid = (unsigned)std::min<int64_t>(P.rows, 1 << 30);
+  CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, params, nullptr);
+  if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "row program launch failed"};
+  ctx->launches++;
+  g_jit_launches.fetch_add(1, std::memory_order_relaxed);
+  return true;
+}
 }  // namespace fopt
 
 extern "C" fopt_status fopt_reduce_map_source(const fopt_program* prog, int32_t n_in, const fopt_dtype* in_dtypes,
@@ -451,6 +785,21 @@ extern "C" fopt_status fopt_elementwise_source(const fopt_program* prog, int32_t
   if (!prog || n_in < 0 || n_in > 3) return FOPT_ERR_INVALID;
   const int modes[3] = {0, 0, 0};
   std::string src = fopt::generate(*prog, n_in, in_dtypes, out_dtype, modes);
+  if (src.empty()) return FOPT_ERR_UNSUPPORTED;
+  if (needed) *needed = src.size() + 1;
+  if (buf && len) {
+    size_t n = std::min(len - 1, src.size());
+    memcpy(buf, src.data(), n);
+    buf[n] = 0;
+  }
+  return FOPT_OK;
+}
+
+extern "C" fopt_status fopt_row_program_source(const fopt_row_plan* plan, char* buf, size_t len, size_t* needed) {
+  int folds[FOPT_ROW_MAX_SLOTS];
+  if (!plan) return FOPT_ERR_INVALID;
+  if (!fopt::row_plan_supported(*plan, false, folds)) return FOPT_ERR_UNSUPPORTED;
+  std::string src = fopt::generate_row(*plan, folds);
   if (src.empty()) return FOPT_ERR_UNSUPPORTED;
   if (needed) *needed = src.size() + 1;
   if (buf && len) {

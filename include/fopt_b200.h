@@ -219,6 +219,65 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
 fopt_status fopt_reduce_map(fopt_ctx* ctx, void* out, const fopt_program* prog, int32_t n_in, const void* const* inputs,
                             const fopt_dtype* in_dtypes, const int64_t* bcast, fopt_dtype dtype, fopt_reduce_op op,
                             uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map);
+/* CUDA graphs of whole steps (no counterpart in the reference, whose host drives every op). Work
+ * issued on ctx between fopt_capture_begin and fopt_capture_end is recorded into a graph, not run
+ * (no call in between may synchronise: fopt_sync, fopt_d2h, fopt_equal); fopt_graph_launch
+ * replays it on ctx's stream. Storages allocated during the capture and not freed in it keep their
+ * addresses across launches (the step's outputs) and must not be freed by the caller; they are
+ * released when the graph is launched again or destroyed. Frees of older memory requested during
+ * the capture happen when it ends. */
+typedef struct fopt_graph fopt_graph;
+fopt_status fopt_capture_begin(fopt_ctx* ctx);
+fopt_status fopt_capture_end(fopt_ctx* ctx, fopt_graph** out);
+fopt_status fopt_graph_launch(fopt_ctx* ctx, fopt_graph* graph);
+fopt_status fopt_graph_destroy(fopt_ctx* ctx, fopt_graph* graph);
+
+/* Whether reducing src_map into dst_map is a plain row reduction (dst cell t folds src cells
+ * t W .. t W + W - 1): FOPT_OK with *rows and *row_len filled, FOPT_ERR_UNSUPPORTED otherwise.
+ * Host-only: ctx may be NULL. */
+fopt_status fopt_row_reduce_shape(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                  int64_t* rows, int64_t* row_len);
+
+/* Engine-chain fusion across a row reduction (no single counterpart in the reference: it runs, in one
+ * pass per row, what the reference does as a chain of BufStorage::reduce, broadcast transpose and
+ * map / zip / zip3 calls, buf.rs:203-250, 257-313, 331-376). Each row of row_len elements is read
+ * once; per-row scalars (a fold of an element program over the row, a program over earlier scalars,
+ * or a load of a per-row value) are computed in order, and the final element program writes the
+ * row. Element programs read registers: leaves 0 .. n_leaves-1, then held values, then slots.
+ * Held values are programs over the leaves, evaluated in the first pass and kept in registers for
+ * the later passes. The f32 folds use the fixed order of fopt_reduce_map (256 slots of 8-element
+ * groups, each folded in order, a butterfly within each 32 slots, then the 8 partial results in
+ * order), so a fused row computes the bits of the unfused chain. FOPT_ERR_UNSUPPORTED when the
+ * generated kernel does not apply (no NVRTC, sub-byte types, misalignment, row_len not a multiple of
+ * 8 or above 32768, exact-fold mode with an f32 Add / Mul fold); nothing is written then. */
+typedef enum { FOPT_ROW_FOLD = 0, FOPT_ROW_SCALAR = 1, FOPT_ROW_LOAD = 2 } fopt_row_slot_kind;
+typedef struct fopt_row_slot {
+  int32_t kind;                /* fopt_row_slot_kind */
+  int32_t op;                  /* FOLD: fopt_reduce_op */
+  uint32_t identity_bits;      /* FOLD: the fold's start value */
+  int32_t dtype;               /* FOLD / SCALAR: f32 or i32 (the value's type); LOAD: the stored type */
+  const fopt_program* prog;    /* FOLD: element program; SCALAR: program over slots 0 .. this - 1 */
+  const void* src;             /* LOAD: [rows] values */
+  void* out;                   /* optional: [rows] 32-bit values of this slot written out */
+} fopt_row_slot;
+#define FOPT_ROW_MAX_LEAVES 8
+#define FOPT_ROW_MAX_HELD 8
+#define FOPT_ROW_MAX_SLOTS 8
+typedef struct fopt_row_plan {
+  int32_t n_leaves, n_held, n_slots;
+  const void* leaf[FOPT_ROW_MAX_LEAVES];
+  int32_t leaf_dtype[FOPT_ROW_MAX_LEAVES];
+  int64_t leaf_bcast[FOPT_ROW_MAX_LEAVES]; /* 0: element i; > 0: i / b; < 0: i % -b (fopt_elementwise_bcast) */
+  const fopt_program* held[FOPT_ROW_MAX_HELD];
+  fopt_row_slot slot[FOPT_ROW_MAX_SLOTS];
+  const fopt_program* final_prog;
+  void* out;
+  int32_t out_dtype;
+  int64_t rows, row_len;
+} fopt_row_plan;
+fopt_status fopt_row_program(fopt_ctx* ctx, const fopt_row_plan* plan);
+/* Diagnostic: the CUDA source fopt_row_program generates for the plan (pointers may be NULL). */
+fopt_status fopt_row_program_source(const fopt_row_plan* plan, char* buf, size_t len, size_t* needed);
 /* Allocation-free reduce. No counterpart in the reference: it exists for callers that cannot let the
  * library call cudaMalloc / cudaFree (a host runtime that owns the whole device-memory budget through
  * its own allocator, or a latency-critical loop that cannot absorb the device synchronisation a

@@ -738,3 +738,134 @@ def test_contraction_host_buffers(b200, shape):
     ep = fb.backend._ep(1, S, "N")
     assert b200.contraction_host(a, b, L, R, P, O, "i8", "i8", ep=ep).tobytes() == want_rq
     assert b200.contraction_host(a, b, L, R, P, O, "i8", "i32").tobytes() == want_w
+
+
+# ---------------------------------------------------------------------------------------------
+# row programs (engine-chain fusion across a row reduction)
+# ---------------------------------------------------------------------------------------------
+def _rms_quant_chain(be, x_bf16, g_f32, T, Wd):
+    """RMSNorm then per-token int8 quantisation, as the decoder block writes it."""
+    from furiosa_opt_b200 import workloads as Wl
+    ax = dict(T=T, H=Wd)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+    x = be.from_vec(m("[T, H]"), x_bf16, "bf16")
+    g = be.relayout(be.from_vec(m("[H]"), g_f32, "f32"), m("[H]"), m("[T, H]"), True)
+    xf = be.map(x, ops.cast("bf16", "f32"), "f32")
+    sq = be.zip_with(xf, xf, ops.fp_binary("MulF"), "f32")
+    ss = be.reduce(sq, "Add", 0.0, m("[T, H]"), m("[T]"))
+    rinv = be.map(ss, Wl._prog_rinv(Wd), "f32")
+    xn = be.zip3_with(xf, be.relayout(rinv, m("[T]"), m("[T, H]"), True), g, Wl._prog_scale3(), "f32")
+    amax = be.reduce(be.map(xn, Wl._prog_abs(), "f32"), "Max", 0.0, m("[T, H]"), m("[T]"))
+    s = be.map(amax, Wl._prog_token_scale(), "f32")
+    q = be.zip_with(xn, be.relayout(s, m("[T]"), m("[T, H]"), True), Wl._prog_quant(), "i8")
+    return q, s, ss, rinv
+
+
+@pytest.fixture
+def row_toggle(b200):
+    saved = b200.row_fusion
+    yield b200
+    b200.row_fusion = saved
+
+
+@pytest.mark.parametrize("T,Wd", [(96, 4096), (7, 4360), (33, 2048 * 16), (5, 8)])
+def test_row_program_rmsnorm_quant_matches_unfused(row_toggle, T, Wd):
+    """One row program (one launch) computes the bits of the unfused chain: the quantised values,
+    the token scales and the intermediate per-row sums and reciprocals it writes out. Widths cover
+    a partial last group of 2048, a width whose held value exceeds the register budget (read again
+    from cache instead) and a single 8-element group."""
+    be = row_toggle
+    rng = np.random.default_rng(T + Wd)
+    x = dtypes.f32_to_bf16_bits((rng.standard_normal(T * Wd) * rng.uniform(0.1, 4, T).repeat(Wd)).astype(np.float32))
+    x[:Wd] = dtypes.f32_to_bf16_bits(np.zeros(Wd, np.float32))  # an all-zero row: the scale clamps
+    g = (1.0 + 0.1 * rng.standard_normal(Wd)).astype(np.float32)
+    be.row_fusion = True
+    before = _lib.lib().fopt_elementwise_jit_launches()
+    q, s, ss, rinv = _rms_quant_chain(be, x, g, T, Wd)
+    fused = [q.to_bytes(), s.to_bytes(), ss.to_bytes(), rinv.to_bytes()]
+    assert _lib.lib().fopt_elementwise_jit_launches() == before + 1
+    be.row_fusion = False
+    q2, s2, ss2, rinv2 = _rms_quant_chain(be, x, g, T, Wd)
+    assert fused == [q2.to_bytes(), s2.to_bytes(), ss2.to_bytes(), rinv2.to_bytes()]
+    # and against the arithmetic in numpy (f32 sums reassociate: scale within 1e-5 relative)
+    xf = dtypes.bf16_bits_to_f32(x).reshape(T, Wd).astype(np.float64)
+    want_ss = (xf * xf).sum(1)
+    assert np.allclose(np.frombuffer(fused[2], np.float32), want_ss, rtol=1e-4, atol=1e-30)
+
+
+def test_row_program_i32_folds_and_loads(row_toggle):
+    """i32 folds (wrapping Add, Min), a per-row value already written out (a LOAD slot) and a
+    repeated-row leaf, at a width that is not a multiple of 2048."""
+    be = row_toggle
+    T, Wd = 40, 3000
+    ax = dict(T=T, H=Wd)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+    rng = np.random.default_rng(11)
+    a = rng.integers(-2**31, 2**31, T * Wd, dtype=np.int64).astype(np.int32)
+    c = rng.integers(-1000, 1000, Wd).astype(np.int32)
+    off = rng.integers(-50, 50, T).astype(np.int32)
+
+    def chain():
+        A = be.from_vec(m("[T, H]"), a, "i32")
+        Cb = be.relayout(be.from_vec(m("[H]"), c, "i32"), m("[H]"), m("[T, H]"), True)
+        Ob = be.relayout(be.from_vec(m("[T]"), off, "i32"), m("[T]"), m("[T, H]"), True)
+        v = be.zip3_with(A, Cb, Ob, _add3(), "i32")
+        tot = be.reduce(v, "Add", 0, m("[T, H]"), m("[T]"))
+        lo = be.reduce(v, "Min", 2**31 - 1, m("[T, H]"), m("[T]"))
+        p = ops.Prog(2)
+        d = be.zip_with(tot, lo, p.build(p.emit("SUB_FXP", 0, 1)), "i32")
+        p = ops.Prog(2)
+        out = be.zip_with(v, be.relayout(d, m("[T]"), m("[T, H]"), True), p.build(p.emit("XOR", 0, 1)), "i16")
+        return out.to_bytes(), tot.to_bytes(), lo.to_bytes()
+
+    be.row_fusion = True
+    fused = chain()
+    be.row_fusion = False
+    assert fused == chain()
+    v = (a.reshape(T, Wd).astype(np.int64) + c[None, :] + off[:, None]).astype(np.int32)
+    assert np.array_equal(np.frombuffer(fused[1], np.int32), v.astype(np.int64).sum(1).astype(np.int32))
+    assert np.array_equal(np.frombuffer(fused[2], np.int32), v.min(1))
+
+
+def _add3():
+    p = ops.Prog(3)
+    return p.build(p.emit("ADD_FXP", p.emit("ADD_FXP", 0, 1), 2))
+
+
+def test_row_program_falls_back_through_origin(row_toggle, monkeypatch):
+    """With row programs off, a value composed from more than 3 leaves runs through its origin
+    (its deferred inputs written first) and matches the chain run op by op."""
+    be = row_toggle
+    T, Wd = 16, 256
+    rng = np.random.default_rng(2)
+    x = dtypes.f32_to_bf16_bits(rng.standard_normal(T * Wd).astype(np.float32))
+    g = rng.uniform(0.5, 1.5, Wd).astype(np.float32)
+    be.row_fusion = False
+    q, s, _, _ = _rms_quant_chain(be, x, g, T, Wd)
+    monkeypatch.setenv("FOPT_NO_FUSION", "1")
+    eager = fb.B200(0)
+    q2, s2, _, _ = _rms_quant_chain(eager, x, g, T, Wd)
+    # the eager chain sums its squares with the general reduce (another f32 order): scales agree
+    # to rounding, quantised values within one step
+    assert np.allclose(s.to_numpy(), s2.to_numpy(), rtol=1e-5)
+    d = np.abs(q.to_numpy().astype(np.int32) - q2.to_numpy().astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() < 1e-3
+
+
+def test_decoder_block_row_programs_bit_exact(row_toggle):
+    """The decoder block with row programs equals the block without them bit for bit, in fewer
+    launches."""
+    from furiosa_opt_b200 import workloads as Wl
+    be = row_toggle
+    batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+    T, H = batch * seq, Hq * 128
+    blk = Wl.DecoderBlockW8A8(be, T, H, Hq, Hkv, F, batch, seq, seed=3)
+    x = dtypes.f32_to_bf16_bits(np.random.default_rng(5).standard_normal(T * H).astype(np.float32))
+    outs, launches = [], []
+    for on in (True, False):
+        be.row_fusion = on
+        n0 = be.launches
+        outs.append(blk.forward(be.from_vec(blk.m("[T, H]"), x, "bf16")).to_bytes())
+        launches.append(be.launches - n0)
+    assert outs[0] == outs[1]
+    assert launches[0] < launches[1], launches

@@ -305,3 +305,86 @@ def test_safetensors_reads_reference_mnist_header():
     assert info["hw.fc2.weight"] == ("BF16", [16, 256])
     assert info["hw.image_0"] == ("BF16", [800])
     assert info["label_0"] == ("I32", [1])
+
+
+def _fake_backend(monkeypatch):
+    """A B200 without a device: storages get fake addresses and every elementwise materialisation
+    is lowered to a row program (or None) and recorded instead of run."""
+    import ctypes as C
+    import itertools
+    from furiosa_opt_b200 import backend as B, rowfuse
+    addrs = itertools.count(1)
+
+    def fake_alloc(self, zero):
+        self._ptr = C.c_void_p(next(addrs) << 16)
+
+    monkeypatch.setattr(B.Storage, "_alloc", fake_alloc)
+    monkeypatch.setattr(B.Storage, "__del__", lambda self: None)
+    built = []
+    monkeypatch.setattr(B.B200, "_run_ew", lambda self, prog, leaves, out, origin=None: built.append(
+        rowfuse.build_row_program(self, prog, leaves, out, origin)))
+    be = B.B200.__new__(B.B200)
+    be.ctx, be.device, be.eager_broadcast, be.fuse, be.row_fusion = None, 0, False, True, True
+    return B, be, built
+
+
+def _row_source(plan) -> bytes:
+    import ctypes as C
+    lib = _lib.lib()
+    need = C.c_size_t()
+    assert lib.fopt_row_program_source(C.byref(plan), None, 0, C.byref(need)) == 0
+    buf = C.create_string_buffer(need.value)
+    assert lib.fopt_row_program_source(C.byref(plan), buf, need.value, None) == 0
+    return buf.value
+
+
+def test_row_programs_lower_the_decoder_chains(monkeypatch):
+    """RMSNorm -> per-token quantisation, the attention output's quantisation and SwiGLU ->
+    quantisation each lower to one row program (leaves, held values, per-row slots) whose generated
+    kernel compiles for sm_100a."""
+    from furiosa_opt_b200 import ops, workloads as Wl
+    B, be, built = _fake_backend(monkeypatch)
+    T, H, F = 64, 4096, 14336
+    blk = Wl.DecoderBlockW8A8.__new__(Wl.DecoderBlockW8A8)
+    blk.be, blk.T, blk.H, blk.F = be, T, H, F
+    blk.ax = dict(T=T, H=H, Q=H, V=1024, F=F)
+    blk.p_rinv_h = Wl._prog_rinv(H)
+    FOLD, SCALAR = _lib.ROW_FOLD, _lib.ROW_SCALAR
+
+    # RMSNorm then quantisation: x (bf16) and the gain (a repeated row) are the leaves; the f32
+    # cast of x is held; slots: sum of squares, 1 / rms, max |x_n|, token scale
+    x = B.Storage(be, "bf16", T * H)
+    g = be.relayout(B.Storage(be, "f32", H), blk.m("[H]"), blk.m("[T, H]"), True)
+    q, s = blk.quantize(blk.rmsnorm(be.map(x, ops.cast("bf16", "f32"), "f32"), g), "H")
+    plan = built[-1].plan
+    assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.rows, plan.row_len) == (2, 1, 4, T, H)
+    assert [plan.slot[j].kind for j in range(4)] == [FOLD, SCALAR, FOLD, SCALAR]
+    assert plan.leaf_bcast[1] == -H and built[-1].slot_nodes[3] is s
+    _nvrtc_compile(_row_source(plan))
+
+    # the attention output: one fold (max |x|), then the scale
+    att = B.Storage(be, "bf16", T * H)
+    qa, sa = blk.quantize(be.map(att, ops.cast("bf16", "f32"), "f32"), "H")
+    plan = built[-1].plan
+    assert (plan.n_leaves, plan.n_held, plan.n_slots) == (1, 1, 2)
+    assert [plan.slot[j].kind for j in range(2)] == [FOLD, SCALAR]
+    _nvrtc_compile(_row_source(plan))
+
+    # SwiGLU then quantisation over F: the activation is computed once and held between the passes
+    gate, up = B.Storage(be, "bf16", T * F), B.Storage(be, "bf16", T * F)
+    q3, s3 = blk.quantize(be.zip_with(gate, up, Wl._prog_swiglu(), "f32"), "F")
+    plan = built[-1].plan
+    assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.row_len) == (2, 1, 2, F)
+    _nvrtc_compile(_row_source(plan))
+
+
+def test_row_programs_decline_without_a_reduction(monkeypatch):
+    """A zip with a broadcast of a value written out is no row program."""
+    from furiosa_opt_b200 import ops, workloads as Wl
+    B, be, built = _fake_backend(monkeypatch)
+    T, H = 8, 64
+    ax = dict(T=T, H=H)
+    x = B.Storage(be, "f32", T * H)
+    sb = be.relayout(B.Storage(be, "f32", T), fb.Mapping("[T]", ax), fb.Mapping("[T, H]", ax), True)
+    be.zip_with(x, sb, Wl._prog_quant(), "i8")
+    assert built == [None]
