@@ -268,12 +268,46 @@ def wl_mnist(fb, be, B=64, I=784, H=128, O=10):
     X, W1, W2, S1 = (be.from_vec(m("[B, I]"), x, "i8"), be.from_vec(m("[H, I]"), w1, "i8"),
                      be.from_vec(m("[O, H]"), w2, "i8"), be.from_vec(m("[H]"), s1, "f32"))
 
-    def step():
-        return fb.workloads.mnist_int8_forward(be, X, W1, W2, S1, B, I, H, O)
-
-    return dict(step=step, units=B, unit="images/s", scale=1.0, bound="latency", flops=2.0 * B * (I * H + H * O),
+    fwd = lambda: fb.workloads.mnist_int8_forward(be, X, W1, W2, S1, B, I, H, O)  # noqa: E731
+    out_bytes = fwd().nbytes
+    step, e2e_step, hx, hout = graphed_step(fb, be, fwd, X, out_bytes)
+    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(),
+                e2e_api="fopt_h2d -> captured forward (fopt_graph_launch) -> fopt_d2h (pinned host buffers)",
+                units=B, unit="images/s", scale=1.0, bound="latency", flops=2.0 * B * (I * H + H * O),
                 metric="MNIST-shaped int8 MLP forward, images/s (64x784 -> 128 -> 10)", workload="mnist_int8_mlp",
-                dtype="i8", config={"B": B, "I": I, "H": H, "O": O})
+                dtype="i8", config={"B": B, "I": I, "H": H, "O": O, "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
+
+
+def graphed_step(fb, be, forward, X, out_bytes):
+    """A step that runs `forward` once eagerly (kernels compiled, workspaces sized), then captures
+    it into a CUDA graph and replays the graph every later step: the same kernels without the host
+    work of issuing them (FOPT_NO_GRAPH=1 issues every step from the host). The end-to-end step
+    copies the input X in from pinned host memory and the result out."""
+    import torch
+
+    use_graph = not os.environ.get("FOPT_NO_GRAPH")
+    state = {}
+
+    def step():
+        if not use_graph:
+            return forward()
+        if "graph" not in state:
+            if not state.get("eager"):
+                state["eager"] = True
+                return forward()
+            state["graph"] = be.capture(forward)
+        return state["graph"].launch()
+
+    hx = torch.from_numpy(X.to_numpy().view(np.uint8).copy()).pin_memory()
+    hout = torch.empty(out_bytes, dtype=torch.uint8).pin_memory()
+    lib = fb._lib.lib()
+
+    def e2e_step():
+        fb._lib.check(lib.fopt_h2d(be.ctx, X.ptr, C.c_void_p(hx.data_ptr()), hx.numel()), be.ctx)
+        out = step()
+        fb._lib.check(lib.fopt_d2h(be.ctx, C.c_void_p(hout.data_ptr()), out.ptr, hout.numel()), be.ctx)
+
+    return step, e2e_step, hx, hout
 
 
 def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
@@ -284,34 +318,7 @@ def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
     X = be.from_vec(blk.m("[T, H]"), fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32)),
                     "bf16")
 
-    # the block's forward runs once eagerly (kernels compiled, workspaces sized), is then captured
-    # into a CUDA graph, and every later step replays the graph: the same kernels, without the
-    # host work of issuing them (FOPT_NO_GRAPH=1 issues every step from the host instead)
-    use_graph = not os.environ.get("FOPT_NO_GRAPH")
-    state = {}
-
-    def step():
-        if not use_graph:
-            return blk.forward(X)
-        if "graph" not in state:
-            if not state.get("eager"):
-                state["eager"] = True
-                return blk.forward(X)
-            state["graph"] = be.capture(lambda: blk.forward(X))
-        return state["graph"].launch()
-
-    import torch
-
-    hx = torch.from_numpy(X.to_numpy().view(np.uint8).copy()).pin_memory()
-    hout = torch.empty(T * H * 2, dtype=torch.uint8).pin_memory()
-    lib = fb._lib.lib()
-
-    def e2e_step():
-        # host bf16 activations in, the block, host bf16 activations out
-        fb._lib.check(lib.fopt_h2d(be.ctx, X.ptr, C.c_void_p(hx.data_ptr()), hx.numel()), be.ctx)
-        out = step()
-        fb._lib.check(lib.fopt_d2h(be.ctx, C.c_void_p(hout.data_ptr()), out.ptr, hout.numel()), be.ctx)
-
+    step, e2e_step, hx, hout = graphed_step(fb, be, lambda: blk.forward(X), X, T * H * 2)
     return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(),
                 e2e_api="fopt_h2d -> captured block (fopt_graph_launch) -> fopt_d2h (pinned host buffers)",
                 units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8",
@@ -319,7 +326,7 @@ def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
                 metric="W8A8 decoder block tokens/s (Llama-3-8B shape, 8 x 512 tokens)", workload="decoder_w8a8",
                 config={"batch": batch, "seq": seq, "hidden": H, "ffn": F, "heads": Hq, "kv_heads": Hkv,
                         "gemm_ops": blk.gemm_ops(), "attention_flops": blk.attention_flops(),
-                        "cuda_graph": use_graph})
+                        "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
 def wl_decoder_tp(fb, be, rank, world, batch=8, seq=512, Hq=32, Hkv=8, F=14336):

@@ -16,9 +16,19 @@ using namespace fopt;
 
 namespace fopt {
 
+// Frees an outgrown context buffer, or keeps it until the context goes away while a captured graph
+// (which may have recorded its address) exists.
+void release_ctx_buffer(fopt_ctx* ctx, void* p) {
+  if (!p) return;
+  if (ctx->graphs_alive > 0 || ctx->capture)
+    ctx->retired.push_back(p);
+  else
+    cuda_check(cudaFree(p), "buffer free");
+}
+
 void* scratch(fopt_ctx* ctx, size_t bytes) {
   if (bytes > ctx->scratch_bytes) {
-    if (ctx->scratch) cuda_check(cudaFree(ctx->scratch), "scratch free");
+    release_ctx_buffer(ctx, ctx->scratch);
     size_t want = std::max(bytes, ctx->scratch_bytes * 2);
     cuda_check(cudaMalloc(&ctx->scratch, want), "scratch alloc");
     ctx->scratch_bytes = want;
@@ -143,6 +153,7 @@ fopt_status fopt_destroy(fopt_ctx* ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->gemm_ws) cudaFree(ctx->gemm_ws);
   if (ctx->gemm_cnt) cudaFree(ctx->gemm_cnt);
+  for (void* p : ctx->retired) cudaFree(p);
   if (ctx->copy_in) cudaStreamDestroy(ctx->copy_in);
   if (ctx->copy_out) cudaStreamDestroy(ctx->copy_out);
   for (int k = 0; k < 2; ++k) {
@@ -277,6 +288,7 @@ fopt_status fopt_capture_end(fopt_ctx* ctx, fopt_graph** out) {
       cuda_check(e, "graph capture");
     }
     for (void* p : g->owned) ctx->graph_mem[p] = g;
+    ctx->graphs_alive++;
     *out = g;
   });
 }
@@ -304,6 +316,10 @@ fopt_status fopt_graph_destroy(fopt_ctx* ctx, fopt_graph* g) {
     if (g->exec) cudaGraphExecDestroy(g->exec);
     if (g->graph) cudaGraphDestroy(g->graph);
     delete g;
+    if (--ctx->graphs_alive == 0) {
+      for (void* p : ctx->retired) cudaFree(p);
+      ctx->retired.clear();
+    }
   });
 }
 
@@ -439,6 +455,7 @@ fopt_status fopt_transmute(fopt_ctx* ctx, void* dst, const void* src, fopt_dtype
         require(k < live_src.size(), "transmute: dst_map has more live elements than src_map");
         t[q] = live_src[k++];
       }
+    require(!ctx->capture, "transmute: a non-affine transmute uploads a table per call and cannot be captured");
     int64_t* dt = (int64_t*)scratch(ctx, sizeof(int64_t) * std::max<size_t>(t.size(), 1));
     cuda_check(cudaMemcpyAsync(dt, t.data(), sizeof(int64_t) * t.size(), cudaMemcpyHostToDevice, ctx->stream),
                "transmute table");

@@ -34,6 +34,18 @@ struct RelayoutPlan {
 struct FoldKPlan {
   KWalk out{}, residue{};
   int64_t out_positions = 0, residue_positions = 0, residue_live = 0;
+  // the live residue deltas of 1 or 2 memories, uploaded once (freed with the context)
+  mutable int64_t* dev_deltas[2] = {nullptr, nullptr};
+  mutable int64_t dev_count[2] = {0, 0};
+  mutable std::mutex dev_mu;
+  FoldKPlan() = default;
+  FoldKPlan(const FoldKPlan& o)
+      : out(o.out), residue(o.residue), out_positions(o.out_positions), residue_positions(o.residue_positions),
+        residue_live(o.residue_live) {}
+  ~FoldKPlan() {
+    for (auto* d : dev_deltas)
+      if (d) cudaFree(d);
+  }
 };
 
 }  // namespace fopt
@@ -45,6 +57,8 @@ struct fopt_ctx {
   fopt_graph* capture = nullptr;        // the step being captured into a CUDA graph, if any
   std::vector<void*> deferred_free;     // frees of pre-capture memory requested during a capture
   std::map<void*, fopt_graph*> graph_mem;  // allocations that belong to a captured graph
+  int graphs_alive = 0;                 // captured graphs not yet destroyed
+  std::vector<void*> retired;           // outgrown context buffers a live graph may still use
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   int exact_fold = 0;
@@ -122,6 +136,7 @@ void launch_relayout(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, const void
 void launch_transmute(fopt_ctx* ctx, const RankWalk& src, const RankWalk& dst, void* out, const void* in, int dtype);
 bool launch_elementwise_jit_ex(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                                const fopt_dtype* in_dt, const int64_t* bcast, void* out, fopt_dtype out_dt, int64_t n);
+void release_ctx_buffer(fopt_ctx* ctx, void* p);
 bool launch_row_jit(fopt_ctx* ctx, const fopt_row_plan& plan);
 bool launch_reduce_map_jit(fopt_ctx* ctx, const fopt_program* prog, int n_in, const void* const* in,
                            const fopt_dtype* in_dt, const int64_t* bcast, int fold, uint32_t ident, void* out,

@@ -447,35 +447,64 @@ std::string load_at(int dt, const std::string& ptr, const std::string& i) {
   }
 }
 
-// One CTA of 256 threads per row; thread t owns the 8-element groups t + 256 kc (kc < KC), which is
-// slot t of the fold order generate_reduce documents. Passes: one per FOLD slot, then the final
-// program. Leaves read in a later pass are kept raw in registers when they fit, else read again
-// (from cache); held values are computed in the first pass and kept.
+// How a row program is laid out on threads: tpr threads per row (32, 64, 128 or 256; 256 / tpr rows
+// per CTA of 256), each keeping spt = 256 / tpr fold slots; the row's data a later pass needs stays in
+// registers (held values, and mode-0 leaves kept raw) within about 64 registers a thread.
+struct RowLayout {
+  int KC = 1, tpr = 256, spt = 1;
+  unsigned keep_raw = 0, later_leaves = 0, held_leaves = 0;
+  std::vector<int> pass_slot;  // FOLD slot index per pass, -1 for the final program
+  bool unrolled = false;       // slots and groups unrolled (held values in registers)
+  bool ok = false;
+};
+
+RowLayout row_layout(const fopt_row_plan& P) {
+  RowLayout L;
+  const int nL = P.n_leaves, nH = P.n_held, nS = P.n_slots, nE = nL + nH + nS;
+  L.KC = (int)((P.row_len + 2047) / 2048);
+  for (int j = 0; j < nS; ++j)
+    if (P.slot[j].kind == FOPT_ROW_FOLD) L.pass_slot.push_back(j);
+  L.pass_slot.push_back(-1);
+  auto pass_prog = [&](int j) -> const fopt_program& { return j < 0 ? *P.final_prog : *P.slot[j].prog; };
+  for (size_t q = 1; q < L.pass_slot.size(); ++q)
+    L.later_leaves |= inputs_read(pass_prog(L.pass_slot[q]), nE) & ((1u << nL) - 1);
+  for (int h = 0; h < nH; ++h) L.held_leaves |= inputs_read(*P.held[h], nL);
+  if (nH * 8 * L.KC > 64) return L;  // held values must fit in registers
+  int words = nH * 8;                // registers per slot and group of 8 elements
+  // Without held values the passes loop over the row (small code, few registers, many rows per
+  // SM) and read their leaves again from cache. With held values every slot and group is unrolled
+  // to keep them in registers; leaves a later pass reads are then kept raw when they fit too.
+  L.unrolled = nH > 0;
+  for (int k = 0; L.unrolled && k < nL; ++k)
+    if ((L.later_leaves >> k & 1) && P.leaf_bcast[k] == 0 && (words + raw_words(P.leaf_dtype[k])) * L.KC <= 64) {
+      L.keep_raw |= 1u << k;
+      words += raw_words(P.leaf_dtype[k]);
+    }
+  L.tpr = 256;
+  for (int tpr = 32; tpr <= 256; tpr *= 2)
+    if ((256 / tpr) * L.KC * words <= 64) {
+      L.tpr = tpr;
+      break;
+    }
+  L.spt = 256 / L.tpr;
+  L.ok = true;
+  return L;
+}
+
+// Thread t of a row (lane = t % 32, warp w = t / 32 of nw = tpr / 32) keeps slots 32 j + lane for
+// j = w + nw i (i < spt): the 8-element groups g = 32 j + lane + 256 kc of the row, folded in kc
+// order, which is the order generate_reduce documents. Passes: one per FOLD slot, then the final
+// program.
 std::string generate_row(const fopt_row_plan& P, const int* folds) {
-  const int nL = P.n_leaves, nH = P.n_held, nS = P.n_slots;
+  const int nL = P.n_leaves, nH = P.n_held, nS = P.n_slots, nE = nL + nH + nS;
   const int64_t W = P.row_len;
-  const int KC = (int)((W + 2047) / 2048);
+  const RowLayout L = row_layout(P);
+  if (!L.ok) return "";
+  const int KC = L.KC, TPR = L.tpr, SPT = L.spt, NW = TPR / 32, RPC = 256 / TPR;
   std::ostringstream o;
   int modes[FOPT_ROW_MAX_LEAVES];
   for (int k = 0; k < nL; ++k) modes[k] = P.leaf_bcast[k] == 0 ? 0 : P.leaf_bcast[k] > 0 ? 1 : 2;
-  // passes and the leaves each reads
-  std::vector<int> pass_slot;  // FOLD slot index per pass, -1 for the final
-  for (int j = 0; j < nS; ++j)
-    if (P.slot[j].kind == FOPT_ROW_FOLD) pass_slot.push_back(j);
-  pass_slot.push_back(-1);
-  const int nE = nL + nH + nS;
   auto pass_prog = [&](int j) -> const fopt_program& { return j < 0 ? *P.final_prog : *P.slot[j].prog; };
-  unsigned later_leaves = 0, held_leaves = 0;
-  for (size_t q = 1; q < pass_slot.size(); ++q) later_leaves |= inputs_read(pass_prog(pass_slot[q]), nE) & ((1u << nL) - 1);
-  for (int h = 0; h < nH; ++h) held_leaves |= inputs_read(*P.held[h], nL);
-  int keep_words = nH * 8;
-  unsigned keep_raw = 0;  // mode-0 leaves read again later, kept raw when the registers allow
-  for (int k = 0; k < nL; ++k)
-    if ((later_leaves >> k & 1) && modes[k] == 0 && (keep_words + raw_words(P.leaf_dtype[k])) * KC <= 64) {
-      keep_raw |= 1u << k;
-      keep_words += raw_words(P.leaf_dtype[k]);
-    }
-  if (nH * 8 * KC > 64) return "";  // held values must fit in registers
   o << kPrelude << "\nusing namespace fopt::ew;\n";
   for (int j = 0; j < nS; ++j)
     if (P.slot[j].kind == FOPT_ROW_FOLD)
@@ -483,21 +512,24 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
         << "; }\n";
   o << "struct RowArgs { const void* in[8]; long long b[8]; const void* ld[8]; void* so[8]; void* out; long long rows; };\n"
     << "extern \"C\" __global__ void __launch_bounds__(256) fopt_row_gen(const RowArgs a) {\n"
-    << "  constexpr long long RL = " << W << "LL;\n  constexpr int KC = " << KC << ";\n"
-    << "  __shared__ unsigned part[" << std::max<size_t>(1, pass_slot.size() - 1) << "][8];\n"
-    << "  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;\n  (void)lane; (void)warp;\n"
+    << "  constexpr long long RL = " << W << "LL;\n  constexpr int KC = " << KC << ", SPT = " << SPT
+    << ", NW = " << NW << ", RPC = " << RPC << ";\n"
+    << "  __shared__ unsigned part[" << std::max<size_t>(1, L.pass_slot.size() - 1) << "][RPC][8];\n"
+    << "  const int t = threadIdx.x % " << TPR << ", rr = threadIdx.x / " << TPR
+    << ", lane = t & 31, w = t >> 5;\n  (void)lane; (void)w; (void)rr;\n"
     << "  void* const out = a.out;\n  (void)out;\n";
   for (int k = 0; k < nL; ++k)
     o << "  const void* const in" << k << " = a.in[" << k << "]; const long long b" << k << " = a.b[" << k
       << "]; (void)b" << k << ";\n";
-  o << "  for (long long row = blockIdx.x; row < a.rows; row += gridDim.x) {\n";
+  o << "  for (long long row0 = (long long)blockIdx.x * RPC; row0 < a.rows; row0 += (long long)gridDim.x * RPC) {\n"
+    << "    const long long row = row0 + rr;\n    const bool live = row < a.rows;\n";
   for (int k = 0; k < nL; ++k)
-    if (keep_raw >> k & 1) o << "    unsigned raw" << k << "[KC][" << raw_words(P.leaf_dtype[k]) << "];\n";
-  for (int h = 0; h < nH; ++h) o << "    unsigned hv" << h << "[KC][8];\n";
+    if (L.keep_raw >> k & 1) o << "    unsigned raw" << k << "[SPT][KC][" << raw_words(P.leaf_dtype[k]) << "];\n";
+  for (int h = 0; h < nH; ++h) o << "    unsigned hv" << h << "[SPT][KC][8];\n";
   for (int j = 0; j < nS; ++j) o << "    unsigned s" << j << " = 0u;\n";
   std::string names[16];
   for (int k = 0; k < nL; ++k) names[k] = "x" + std::to_string(k) + "[e]";
-  for (int h = 0; h < nH; ++h) names[nL + h] = "hv" + std::to_string(h) + "[kc][e]";
+  for (int h = 0; h < nH; ++h) names[nL + h] = "hv" + std::to_string(h) + "[i][kc][e]";
   for (int j = 0; j < nS; ++j) names[nL + nH + j] = "s" + std::to_string(j);
   std::string snames[16];
   for (int j = 0; j < nS; ++j) snames[j] = "s" + std::to_string(j);
@@ -507,18 +539,26 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
     const bool first = pass == 0;
     const fopt_program& prog = pass_prog(j);
     unsigned need = inputs_read(prog, nE) & ((1u << nL) - 1);
-    if (first) need |= held_leaves;
+    if (first) need |= L.held_leaves;
     o << "    {\n";
-    if (j >= 0) o << "    unsigned acc = " << P.slot[j].identity_bits << "u;\n";
-    o << "#pragma unroll\n    for (int kc = 0; kc < KC; ++kc) {\n"
-      << "      const long long c = 8 * t + 2048 * kc;\n      if (c < RL) {\n"
+    if (L.unrolled) {
+      if (j >= 0)
+        o << "    unsigned acc[SPT];\n#pragma unroll\n    for (int i = 0; i < SPT; ++i) acc[i] = "
+          << P.slot[j].identity_bits << "u;\n";
+      o << "#pragma unroll\n    for (int i = 0; i < SPT; ++i)\n#pragma unroll\n    for (int kc = 0; kc < KC; ++kc) {\n";
+    } else {
+      o << "#pragma unroll 1\n    for (int i = 0; i < SPT; ++i) {\n";
+      if (j >= 0) o << "    unsigned acc = " << P.slot[j].identity_bits << "u;\n";
+      o << "#pragma unroll " << (KC <= 4 ? KC : 2) << "\n    for (int kc = 0; kc < KC; ++kc) {\n";
+    }
+    o << "      const long long c = 256 * (w + NW * i) + 8 * lane + 2048 * kc;\n      if (live && c < RL) {\n"
       << "      const long long base = row * RL + c;\n";
     for (int k = 0; k < nL; ++k) {
-      if (!(need >> k & 1) && !(first && (keep_raw >> k & 1))) continue;
+      if (!(need >> k & 1) && !(first && (L.keep_raw >> k & 1))) continue;
       const std::string xk = "x" + std::to_string(k), bk = "b" + std::to_string(k);
       o << "      unsigned " << xk << "[8];\n";
-      if (keep_raw >> k & 1) {
-        const std::string raw = "raw" + std::to_string(k) + "[kc]";
+      if (L.keep_raw >> k & 1) {
+        const std::string raw = "raw" + std::to_string(k) + "[i][kc]";
         if (first) o << "      " << raw_load(k, P.leaf_dtype[k], raw);
         o << "#pragma unroll\n      " << raw_unpack(P.leaf_dtype[k], raw, xk);
       } else if (modes[k] == 1) {
@@ -534,22 +574,50 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
       for (int h = 0; h < nH; ++h) {
         std::string ret;
         if (!emit_program_named(o, *P.held[h], names, nL, &ret, "h" + std::to_string(h) + "_")) return false;
-        o << "        hv" << h << "[kc][e] = " << ret << ";\n";
+        o << "        hv" << h << "[i][kc][e] = " << ret << ";\n";
       }
     }
     std::string ret;
     if (!emit_program_named(o, prog, names, nE, &ret)) return false;
+    const std::string acc = L.unrolled ? "acc[i]" : "acc";
     if (j >= 0)
-      o << "        acc = fold" << j << "(acc, " << ret << ");\n      }\n";
+      o << "        " << acc << " = fold" << j << "(" << acc << ", " << ret << ");\n      }\n";
     else
       o << "        r[e] = " << ret << ";\n      }\n      " << store_vec(P.out_dtype);
     o << "      }\n    }\n";
+    if (!L.unrolled) {
+      // slot set w + NW i is complete: butterfly it and fold it in (NW = 1: sets come in order
+      // j = i), or park it for the in-order fold across the row's warps
+      if (j >= 0) {
+        o << "#pragma unroll\n    for (int m = 16; m; m >>= 1) acc = fold" << j
+          << "(acc, __shfl_xor_sync(0xffffffffu, acc, m));\n";
+        if (NW == 1)
+          o << "    s" << j << " = i == 0 ? acc : fold" << j << "(s" << j << ", acc);\n";
+        else
+          o << "    if (lane == 0) part[" << nfold << "][rr][w + NW * i] = acc;\n";
+      }
+      o << "    }\n";
+      if (j >= 0 && NW > 1)
+        o << "    __syncthreads();\n    s" << j << " = part[" << nfold << "][rr][0];\n#pragma unroll\n"
+          << "    for (int q = 1; q < 8; ++q) s" << j << " = fold" << j << "(s" << j << ", part[" << nfold << "][rr][q]);\n";
+      if (j >= 0) ++nfold;
+      o << "    }\n";
+      ++pass;
+      return true;
+    }
     if (j >= 0) {
-      o << "#pragma unroll\n    for (int m = 16; m; m >>= 1) acc = fold" << j << "(acc, __shfl_xor_sync(0xffffffffu, acc, m));\n"
-        << "    if (lane == 0) part[" << nfold << "][warp] = acc;\n    __syncthreads();\n"
-        << "    s" << j << " = part[" << nfold << "][0];\n"
-        << "#pragma unroll\n    for (int w = 1; w < 8; ++w) s" << j << " = fold" << j << "(s" << j << ", part[" << nfold
-        << "][w]);\n";
+      // butterfly per slot set, then the 8 sets in order j = 0 .. 7 (set w + NW i of this thread)
+      o << "#pragma unroll\n    for (int i = 0; i < SPT; ++i)\n#pragma unroll\n"
+        << "      for (int m = 16; m; m >>= 1) acc[i] = fold" << j << "(acc[i], __shfl_xor_sync(0xffffffffu, acc[i], m));\n";
+      if (NW == 1) {
+        o << "    s" << j << " = acc[0];\n#pragma unroll\n    for (int i = 1; i < 8; ++i) s" << j << " = fold" << j
+          << "(s" << j << ", acc[i]);\n";
+      } else {
+        o << "    if (lane == 0)\n#pragma unroll\n      for (int i = 0; i < SPT; ++i) part[" << nfold
+          << "][rr][w + NW * i] = acc[i];\n    __syncthreads();\n"
+          << "    s" << j << " = part[" << nfold << "][rr][0];\n#pragma unroll\n    for (int q = 1; q < 8; ++q) s" << j
+          << " = fold" << j << "(s" << j << ", part[" << nfold << "][rr][q]);\n";
+      }
       ++nfold;
     }
     o << "    }\n";
@@ -566,13 +634,14 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
       if (!emit_program_named(o, *sl.prog, snames, j, &ret, "q" + std::to_string(j) + "_")) return "";
       o << "    s" << j << " = " << ret << ";\n    }\n";
     } else {
-      o << "    s" << j << " = " << load_at(sl.dtype, "a.ld[" + std::to_string(j) + "]", "row") << ";\n";
+      o << "    if (live) s" << j << " = " << load_at(sl.dtype, "a.ld[" + std::to_string(j) + "]", "row") << ";\n";
     }
     if (sl.kind != FOPT_ROW_LOAD)
-      o << "    if (t == 0 && a.so[" << j << "]) ((unsigned*)a.so[" << j << "])[row] = s" << j << ";\n";
+      o << "    if (t == 0 && live && a.so[" << j << "]) ((unsigned*)a.so[" << j << "])[row] = s" << j << ";\n";
   }
   if (!emit_pass(-1)) return "";
-  o << "    __syncthreads();\n  }\n}\n";
+  if (NW > 1) o << "    __syncthreads();\n";
+  o << "  }\n}\n";
   return o.str();
 }
 
@@ -754,7 +823,8 @@ bool launch_row_jit(fopt_ctx* ctx, const fopt_row_plan& P) {
   args.out = P.out;
   args.rows = P.rows;
   void* params[] = {(void*)&args};
-  const unsigned grid = (unsigned)std::min<int64_t>(P.rows, 1 << 30);
+  const int rpc = 256 / row_layout(P).tpr;
+  const unsigned grid = (unsigned)std::min<int64_t>((P.rows + rpc - 1) / rpc, 1 << 30);
   CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, params, nullptr);
   if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "row program launch failed"};
   ctx->launches++;

@@ -142,28 +142,18 @@ struct CArgs {
   const float* scale;
 };
 
+__device__ __forceinline__ uint32_t int_finish(const CArgs& a, int32_t acc, int64_t sidx);
+
 __device__ __forceinline__ uint32_t contract_cell(const CArgs& a, int64_t bl, int64_t br, int64_t sidx) {
   uint32_t res;
   if (is_int_in(a.in_dt)) {
-    int32_t acc = 0;
+    uint32_t acc = 0;  // wrapping i32 sum
     for (int64_t r = 0; r < a.nd; ++r) {
       int64_t pl = bl + a.dl[r], pr = br + a.dr[r];
       if (pl < a.lhs_elems && pr < a.rhs_elems)
-        acc += (int32_t)load_word(a.lhs, a.in_dt, pl) * (int32_t)load_word(a.rhs, a.in_dt, pr);
+        acc += (uint32_t)((int32_t)load_word(a.lhs, a.in_dt, pl) * (int32_t)load_word(a.rhs, a.in_dt, pr));
     }
-    if (a.ep_kind == 1) {
-      float y = F(fxp_to_fp_bits(acc, (uint32_t)a.int_width));
-      const float sv = a.scale[sidx];
-      // x86 products (the reference's host) return a NaN operand unchanged and make 0 * inf the
-      // negative default NaN; the GPU would return a positive canonical NaN for both
-      y = __fmul_rn(y, sv);
-      if (y != y) y = sv != sv ? sv : __uint_as_float(0xffc00000u);
-      int32_t q = fp_to_fxp(y, (uint32_t)a.int_width);
-      q = max(a.clip_lo, min(a.clip_hi, q));
-      return (uint32_t)q;
-    }
-    if (a.ep_kind == 2) acc = max(acc, 0);
-    res = (uint32_t)acc;
+    return int_finish(a, (int32_t)acc, sidx);
   } else {
     float acc = 0.0f;
     for (int64_t r = 0; r < a.nd; ++r) {
@@ -186,6 +176,27 @@ __device__ __forceinline__ uint32_t contract_cell(const CArgs& a, int64_t bl, in
   return res;
 }
 
+// The epilogue of an integer cell: requant (1), ReLU (2) or the raw i32 sum.
+__device__ __forceinline__ uint32_t int_finish(const CArgs& a, int32_t acc, int64_t sidx) {
+  uint32_t res;
+  {
+    if (a.ep_kind == 1) {
+      float y = F(fxp_to_fp_bits(acc, (uint32_t)a.int_width));
+      const float sv = a.scale[sidx];
+      // x86 products (the reference's host) return a NaN operand unchanged and make 0 * inf the
+      // negative default NaN; the GPU would return a positive canonical NaN for both
+      y = __fmul_rn(y, sv);
+      if (y != y) y = sv != sv ? sv : __uint_as_float(0xffc00000u);
+      int32_t q = fp_to_fxp(y, (uint32_t)a.int_width);
+      q = max(a.clip_lo, min(a.clip_hi, q));
+      return (uint32_t)q;
+    }
+    if (a.ep_kind == 2) acc = max(acc, 0);
+    res = (uint32_t)acc;
+  }
+  return res;
+}
+
 __global__ void contract_cell_kernel(CArgs a, KWalk ow, int64_t out_positions) {
   for (int64_t o = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; o < out_positions;
        o += (int64_t)gridDim.x * blockDim.x) {
@@ -193,6 +204,27 @@ __global__ void contract_cell_kernel(CArgs a, KWalk ow, int64_t out_positions) {
     uint32_t v = 0;
     if (walk_offsets<3>(ow, o, off)) v = contract_cell(a, off[0], off[1], off[2]);
     store_word(a.out, a.out_dt, o, v);
+  }
+}
+
+// Integer contractions with long residue lists: a warp per output cell, its lanes taking every
+// 32nd residue; the wrapping i32 sum does not depend on the order, so the cell is the same.
+__global__ void contract_cell_warp_kernel(CArgs a, KWalk ow, int64_t out_positions) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t o = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_positions; o += nw) {
+    int64_t off[3] = {0, 0, 0};
+    const bool live = walk_offsets<3>(ow, o, off);
+    uint32_t acc = 0;
+    if (live)
+      for (int64_t r = lane; r < a.nd; r += 32) {
+        const int64_t pl = off[0] + a.dl[r], pr = off[1] + a.dr[r];
+        if (pl < a.lhs_elems && pr < a.rhs_elems)
+          acc += (uint32_t)((int32_t)load_word(a.lhs, a.in_dt, pl) * (int32_t)load_word(a.rhs, a.in_dt, pr));
+      }
+#pragma unroll
+    for (int m = 16; m; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) store_word(a.out, a.out_dt, o, live ? int_finish(a, (int32_t)acc, off[2]) : 0u);
   }
 }
 
@@ -212,14 +244,26 @@ __global__ void contract_cell_nibble_kernel(CArgs a, KWalk ow, int64_t out_posit
   }
 }
 
+bool int_in_host(int dt) {
+  return dt == FOPT_I8 || dt == FOPT_I4 || dt == FOPT_I5 || dt == FOPT_I9 || dt == FOPT_I16 || dt == FOPT_I32;
+}
+
 int grid_for(int64_t work) {
   return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 148 * 32));
 }
 
 }  // namespace
 
-// Live residue deltas in walk order, for `m` memories, into device scratch.
-static const int64_t* upload_deltas(fopt_ctx* ctx, const KWalk& rw, int nmem, int64_t* count) {
+// Live residue deltas in walk order, for `m` memories, in device memory owned by the plan: uploaded
+// on first use and kept, so a launch captured into a CUDA graph reads a table that outlives it.
+static const int64_t* upload_deltas(fopt_ctx* ctx, const FoldKPlan& p, int nmem, int64_t* count) {
+  std::lock_guard<std::mutex> g(p.dev_mu);
+  if (p.dev_deltas[nmem - 1]) {
+    *count = p.dev_count[nmem - 1];
+    return p.dev_deltas[nmem - 1];
+  }
+  if (ctx->capture) throw Fail{FOPT_ERR_INVALID, "a reduce / contraction plan first used inside a capture: run the step once before capturing"};
+  const KWalk& rw = p.residue;
   std::vector<int64_t> d[3];
   int64_t n = 1;
   for (int i = 0; i < rw.n; ++i) n *= rw.extent[i];
@@ -239,11 +283,13 @@ static const int64_t* upload_deltas(fopt_ctx* ctx, const KWalk& rw, int nmem, in
   }
   *count = (int64_t)d[0].size();
   size_t bytes = sizeof(int64_t) * d[0].size() * nmem;
-  int64_t* dev = (int64_t*)scratch(ctx, std::max<size_t>(bytes, 16));
+  int64_t* dev = nullptr;
+  cuda_check(cudaMalloc(&dev, std::max<size_t>(bytes, 16)), "delta table alloc");
   for (int m = 0; m < nmem; ++m)
-    cuda_check(cudaMemcpyAsync(dev + m * d[0].size(), d[m].data(), sizeof(int64_t) * d[m].size(),
-                               cudaMemcpyHostToDevice, ctx->stream),
+    cuda_check(cudaMemcpy(dev + m * d[0].size(), d[m].data(), sizeof(int64_t) * d[m].size(), cudaMemcpyHostToDevice),
                "upload deltas");
+  p.dev_deltas[nmem - 1] = dev;
+  p.dev_count[nmem - 1] = *count;
   return dev;
 }
 
@@ -262,7 +308,7 @@ void launch_reduce(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src
     return;
   }
   int64_t nd;
-  const int64_t* delta = upload_deltas(ctx, p.residue, 1, &nd);
+  const int64_t* delta = upload_deltas(ctx, p, 1, &nd);
   reduce_cell_kernel<<<grid_for(p.out_positions), 256, 0, ctx->stream>>>(out, src, dtype, op, ident, p.out,
                                                                           p.out_positions, delta, nd, src_elems);
   launched(ctx, "reduce_cell");
@@ -272,7 +318,7 @@ void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, in
                                 const void* rhs, int in_dt, int64_t lhs_elems, int64_t rhs_elems,
                                 const fopt_epilogue* ep, const int64_t*, const float* scale) {
   int64_t nd;
-  const int64_t* d = upload_deltas(ctx, p.residue, 2, &nd);
+  const int64_t* d = upload_deltas(ctx, p, 2, &nd);
   CArgs a{};
   a.out = out;
   a.out_dt = out_dt;
@@ -292,6 +338,8 @@ void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, in
   if (dtype_bits(out_dt) == 4) {
     contract_cell_nibble_kernel<<<grid_for((p.out_positions + 1) / 2), 256, 0, ctx->stream>>>(a, p.out,
                                                                                                p.out_positions);
+  } else if (int_in_host(in_dt) && nd >= 32) {
+    contract_cell_warp_kernel<<<grid_for(p.out_positions * 32), 256, 0, ctx->stream>>>(a, p.out, p.out_positions);
   } else {
     contract_cell_kernel<<<grid_for(p.out_positions), 256, 0, ctx->stream>>>(a, p.out, p.out_positions);
   }

@@ -917,12 +917,12 @@ int plan_split(fopt_ctx* ctx, Params& p, int ntiles, int pairs, int kblocks, int
   const size_t ws_bytes = (size_t)rem * split * 256 * bn * 4;
   const size_t n_cnt = (size_t)rem * 2 * EPI_WARPS;
   if (ws_bytes > ctx->gemm_ws_bytes) {
-    if (ctx->gemm_ws) cuda_check(cudaFree(ctx->gemm_ws), "gemm workspace free");
+    release_ctx_buffer(ctx, ctx->gemm_ws);
     cuda_check(cudaMalloc(&ctx->gemm_ws, ws_bytes), "gemm workspace alloc");
     ctx->gemm_ws_bytes = ws_bytes;
   }
   if (n_cnt > ctx->gemm_cnt_n) {
-    if (ctx->gemm_cnt) cuda_check(cudaFree(ctx->gemm_cnt), "gemm counters free");
+    release_ctx_buffer(ctx, ctx->gemm_cnt);
     cuda_check(cudaMalloc(&ctx->gemm_cnt, n_cnt * 4), "gemm counters alloc");
     ctx->gemm_cnt_n = n_cnt;
     ctx->gemm_cnt_dirty = true;

@@ -155,6 +155,20 @@ class _Planner:
         return b.build(ops.inline(b, root_prog, [reg(c) for c in root_inputs]))
 
 
+def _cheap(pl, x) -> bool:
+    leaves = set()
+
+    def walk(n, depth):
+        if id(n) in pl.leaf_of:
+            leaves.add(id(n))
+            return 0
+        prog, inputs = _children(n)
+        return prog.n_insn + sum(walk(c, depth + 1) for c in inputs)
+
+    insns = walk(x, 0)
+    return insns <= 2 and len(leaves) == 1
+
+
 class RowBuild:
     """A lowered row program: the ctypes plan (slot outputs not yet set), the scalar storages its
     FOLD / SCALAR slots compute (in slot order, None for LOAD slots) and what keeps it alive."""
@@ -187,6 +201,9 @@ def build_row_program(be, prog, leaves, out, origin):
         held, seen = [], set()
         for inputs in passes[1:]:
             pl.frontier(inputs, held, seen)
+        # a value a couple of instructions from one leaf (a cast) is cheaper to recompute from the
+        # leaf kept raw, which takes fewer registers than the 32-bit value
+        held = [x for x in held if not _cheap(pl, x)]
         KC = (W + 2047) // 2048
         if len(held) > _lib.ROW_MAX_HELD or len(held) * 8 * KC > 64:
             held = []

@@ -101,3 +101,26 @@ def test_decoder_block_graph_replay_bit_exact(b200):
     g.close()
     # the backend keeps working after the graph is gone
     assert blk.forward(b200.from_vec(blk.m("[T, H]"), xs[1], "bf16")).to_bytes() == want[1]
+
+
+def test_mnist_int8_graph_replay_bit_exact(b200):
+    """The int8 MLP (generic contraction kernels over cached residue tables) captured once and
+    replayed on new inputs gives the eager forward's logits."""
+    B, I, H, O = 64, 784, 128, 10
+    _, w1, w2, s1 = W.mnist_inputs(0, B, I, H, O)
+    ax = dict(B=B, I=I, H=H, O=O)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+    W1, W2, S1 = b200.from_vec(m("[H, I]"), w1, "i8"), b200.from_vec(m("[O, H]"), w2, "i8"), \
+        b200.from_vec(m("[H]"), s1, "f32")
+    rng = np.random.default_rng(4)
+    xs = [rng.integers(-128, 128, B * I).astype(np.int8) for _ in range(3)]
+    fwd = lambda X: W.mnist_int8_forward(b200, X, W1, W2, S1, B, I, H, O)  # noqa: E731
+    want = [fwd(b200.from_vec(m("[B, I]"), x, "i8")).to_bytes() for x in xs]
+    X = b200.from_vec(m("[B, I]"), xs[0], "i8")
+    fwd(X)
+    g = b200.capture(lambda: fwd(X))
+    lib = fb._lib.lib()
+    for x, w in zip(xs, want):
+        fb._lib.check(lib.fopt_h2d(b200.ctx, X.ptr, x.ctypes.data, x.nbytes), b200.ctx)
+        assert g.launch().to_bytes() == w
+    g.close()

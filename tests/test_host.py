@@ -351,22 +351,25 @@ def test_row_programs_lower_the_decoder_chains(monkeypatch):
     blk.p_rinv_h = Wl._prog_rinv(H)
     FOLD, SCALAR = _lib.ROW_FOLD, _lib.ROW_SCALAR
 
-    # RMSNorm then quantisation: x (bf16) and the gain (a repeated row) are the leaves; the f32
-    # cast of x is held; slots: sum of squares, 1 / rms, max |x_n|, token scale
+    # RMSNorm then quantisation: x (bf16) and the gain (a repeated row) are the leaves; x stays in
+    # registers raw (its f32 cast is recomputed, not held); slots: sum of squares, 1 / rms,
+    # max |x_n|, token scale; one warp per row
     x = B.Storage(be, "bf16", T * H)
     g = be.relayout(B.Storage(be, "f32", H), blk.m("[H]"), blk.m("[T, H]"), True)
     q, s = blk.quantize(blk.rmsnorm(be.map(x, ops.cast("bf16", "f32"), "f32"), g), "H")
     plan = built[-1].plan
-    assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.rows, plan.row_len) == (2, 1, 4, T, H)
+    assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.rows, plan.row_len) == (2, 0, 4, T, H)
     assert [plan.slot[j].kind for j in range(4)] == [FOLD, SCALAR, FOLD, SCALAR]
     assert plan.leaf_bcast[1] == -H and built[-1].slot_nodes[3] is s
-    _nvrtc_compile(_row_source(plan))
+    src = _row_source(plan)
+    assert b"NW = 1, RPC = 8" in src
+    _nvrtc_compile(src)
 
     # the attention output: one fold (max |x|), then the scale
     att = B.Storage(be, "bf16", T * H)
     qa, sa = blk.quantize(be.map(att, ops.cast("bf16", "f32"), "f32"), "H")
     plan = built[-1].plan
-    assert (plan.n_leaves, plan.n_held, plan.n_slots) == (1, 1, 2)
+    assert (plan.n_leaves, plan.n_held, plan.n_slots) == (1, 0, 2)
     assert [plan.slot[j].kind for j in range(2)] == [FOLD, SCALAR]
     _nvrtc_compile(_row_source(plan))
 
@@ -375,7 +378,9 @@ def test_row_programs_lower_the_decoder_chains(monkeypatch):
     q3, s3 = blk.quantize(be.zip_with(gate, up, Wl._prog_swiglu(), "f32"), "F")
     plan = built[-1].plan
     assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.row_len) == (2, 1, 2, F)
-    _nvrtc_compile(_row_source(plan))
+    src = _row_source(plan)
+    assert b"NW = 8, RPC = 1" in src
+    _nvrtc_compile(src)
 
 
 def test_row_programs_decline_without_a_reduction(monkeypatch):
