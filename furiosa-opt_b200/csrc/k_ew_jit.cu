@@ -179,24 +179,128 @@ int arity_of(int op) {
 // Emits the program's instructions for element e of inputs x0..x2 (one scoped block per
 // instruction, every value in a named register); *ret names the result. False for an opcode the
 // table lacks.
+// A DivF by a row-uniform input whose quotient only feeds one FpToFxp: run as qdiv_fxp.
+struct QuantFuse {
+  int div_i = -1, fxp_i = -1, slot_reg = -1;
+  unsigned iw = 31;
+};
+
+std::vector<QuantFuse> find_quant_fuses(const fopt_program& p, int uniform_lo, int uniform_hi) {
+  std::vector<QuantFuse> out;
+  unsigned written = 0;
+  for (int i = 0; i < p.n_insn; ++i) {
+    const fopt_insn& in = p.insn[i];
+    if (in.op == FOPT_OP_DIVF) {
+      const int b = in.b & 15, d = in.dst & 15;
+      if (b >= uniform_lo && b < uniform_hi && !(written >> b & 1)) {
+        int uses = 0, fxp = -1;
+        bool overwritten = false;
+        for (int j = i + 1; j < p.n_insn && !overwritten; ++j) {
+          const fopt_insn& q = p.insn[j];
+          const int ar = arity_of(q.op), rs[3] = {q.a & 15, q.b & 15, q.c & 15};
+          for (int k = 0; k < ar; ++k)
+            if (rs[k] == d) {
+              ++uses;
+              if (q.op == FOPT_OP_FP_TO_FXP && k == 0) fxp = j;
+            }
+          if ((q.dst & 15) == d) overwritten = true;
+        }
+        if (uses == 1 && fxp >= 0 && (overwritten || (p.ret & 15) != d) && p.insn[fxp].imm_i >= 0 &&
+            p.insn[fxp].imm_i <= 31)
+          out.push_back(QuantFuse{i, fxp, b, (unsigned)p.insn[fxp].imm_i});
+      }
+    }
+    written |= 1u << (in.dst & 15);
+  }
+  return out;
+}
+
 bool emit_program_named(std::ostringstream& o, const fopt_program& p, const std::string* inputs, int n_in,
-                        std::string* ret, const std::string& tag = "t") {
+                        std::string* ret, const std::string& tag = "t",
+                        const std::vector<QuantFuse>* fuses = nullptr) {
   std::string name[16];
   for (int v = 0; v < 16; ++v) name[v] = "0u";
   for (int k = 0; k < n_in && k < 16; ++k) name[k] = inputs[k];
+  std::map<int, std::string> fused_dividend;  // fxp instruction -> dividend name
   for (int i = 0; i < p.n_insn; ++i) {
     const fopt_insn& in = p.insn[i];
+    const QuantFuse* qf = nullptr;
+    if (fuses)
+      for (const auto& f : *fuses)
+        if (f.div_i == i || f.fxp_i == i) qf = &f;
+    if (qf && qf->div_i == i) {  // the quotient is formed inside the FpToFxp below
+      fused_dividend[qf->fxp_i] = name[in.a & 15];
+      name[in.dst & 15] = "0u";
+      continue;
+    }
+    const std::string t = tag + std::to_string(i);
+    if (qf && qf->fxp_i == i) {
+      o << "      const unsigned " << t << " = qdiv_fxp(" << fused_dividend[i] << ", " << inputs[qf->slot_reg] << ", rq"
+        << qf->slot_reg << "_" << qf->iw << ", " << qf->iw << "u);\n";
+      name[in.dst & 15] = t;
+      continue;
+    }
     const char* expr = op_expr(in.op);
     if (!expr) return false;
     const int ar = arity_of(in.op);
     const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
                       C = ar > 2 ? name[in.c & 15] : "0u";
-    const std::string t = tag + std::to_string(i);
     o << "      unsigned " << t << "; { const unsigned a = " << A << ", b = " << B << ", c = " << C
       << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
       << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << " = ("
       << expr << "); }\n";
     name[in.dst & 15] = t;
+  }
+  *ret = name[p.ret & 15];
+  return true;
+}
+
+// The same program emitted instruction by instruction over a group of 8 elements: each instruction
+// is an unrolled loop over e writing an 8-entry array, so the 8 independent chains interleave.
+// Inputs are expressions in e ("x0[e]") or uniform names. A fused quantising division computes
+// every element's fast result and a flag without branching, then one rarely taken loop redoes the
+// flagged elements exactly. *ret names the result as an expression in e.
+bool emit_program_vec(std::ostringstream& o, const fopt_program& p, const std::string* inputs, int n_in,
+                      std::string* ret, const std::string& tag, const std::vector<QuantFuse>* fuses = nullptr) {
+  std::string name[16];
+  for (int v = 0; v < 16; ++v) name[v] = "0u";
+  for (int k = 0; k < n_in && k < 16; ++k) name[k] = inputs[k];
+  std::map<int, std::string> fused_dividend;
+  for (int i = 0; i < p.n_insn; ++i) {
+    const fopt_insn& in = p.insn[i];
+    const QuantFuse* qf = nullptr;
+    if (fuses)
+      for (const auto& f : *fuses)
+        if (f.div_i == i || f.fxp_i == i) qf = &f;
+    if (qf && qf->div_i == i) {
+      fused_dividend[qf->fxp_i] = name[in.a & 15];
+      name[in.dst & 15] = "0u";
+      continue;
+    }
+    const std::string t = tag + std::to_string(i);
+    if (qf && qf->fxp_i == i) {
+      const std::string a = fused_dividend[i], sv = inputs[qf->slot_reg],
+                        rq = "rq" + std::to_string(qf->slot_reg) + "_" + std::to_string(qf->iw);
+      o << "      unsigned " << t << "[8]; bool " << t << "_slow = false;\n#pragma unroll\n"
+        << "      for (int e = 0; e < 8; ++e) { bool ok; " << t << "[e] = qdiv_fxp_fast(" << a << ", " << rq
+        << ", &ok); " << t << "_slow |= !ok; }\n"
+        << "      if (" << t << "_slow) {\n#pragma unroll\n      for (int e = 0; e < 8; ++e) { bool ok; "
+        << "(void)qdiv_fxp_fast(" << a << ", " << rq << ", &ok); if (!ok) " << t << "[e] = qdiv_fxp(" << a << ", "
+        << sv << ", " << rq << ", " << qf->iw << "u); }\n      }\n";
+      name[in.dst & 15] = t + "[e]";
+      continue;
+    }
+    const char* expr = op_expr(in.op);
+    if (!expr) return false;
+    const int ar = arity_of(in.op);
+    const std::string A = ar > 0 ? name[in.a & 15] : "0u", B = ar > 1 ? name[in.b & 15] : "0u",
+                      C = ar > 2 ? name[in.c & 15] : "0u";
+    o << "      unsigned " << t << "[8];\n#pragma unroll\n      for (int e = 0; e < 8; ++e) { const unsigned a = " << A
+      << ", b = " << B << ", c = " << C
+      << "; const int ia = (int)a, ib = (int)b; const float fa = F(a), fb = F(b), fc = F(c); const int imm = "
+      << in.imm_i << "; (void)ia; (void)ib; (void)fa; (void)fb; (void)fc; (void)c; (void)imm; " << t << "[e] = ("
+      << expr << "); }\n";
+    name[in.dst & 15] = t + "[e]";
   }
   *ret = name[p.ret & 15];
   return true;
@@ -486,6 +590,8 @@ RowLayout row_layout(const fopt_row_plan& P) {
       L.tpr = tpr;
       break;
     }
+  // enough warps to hide latency: about 48 a SM over the 148 SMs
+  while (L.tpr < 256 && P.rows * (L.tpr / 32) < 148 * 48) L.tpr *= 2;
   L.spt = 256 / L.tpr;
   L.ok = true;
   return L;
@@ -540,7 +646,12 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
     const fopt_program& prog = pass_prog(j);
     unsigned need = inputs_read(prog, nE) & ((1u << nL) - 1);
     if (first) need |= L.held_leaves;
+    const std::vector<QuantFuse> fuses =
+        getenv("FOPT_ROW_NO_QDIV") ? std::vector<QuantFuse>{} : find_quant_fuses(prog, nL + nH, nE);
     o << "    {\n";
+    for (const auto& f : fuses)
+      o << "    const float rq" << f.slot_reg << "_" << f.iw << " = qdiv_factor(" << names[f.slot_reg] << ", " << f.iw
+        << "u);\n";
     if (L.unrolled) {
       if (j >= 0)
         o << "    unsigned acc[SPT];\n#pragma unroll\n    for (int i = 0; i < SPT; ++i) acc[i] = "
@@ -569,17 +680,17 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
       }
     }
     if (j < 0) o << "      unsigned r[8];\n";
-    o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) {\n";
     if (first) {
       for (int h = 0; h < nH; ++h) {
         std::string ret;
-        if (!emit_program_named(o, *P.held[h], names, nL, &ret, "h" + std::to_string(h) + "_")) return false;
-        o << "        hv" << h << "[i][kc][e] = " << ret << ";\n";
+        if (!emit_program_vec(o, *P.held[h], names, nL, &ret, "h" + std::to_string(h) + "_")) return false;
+        o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) hv" << h << "[i][kc][e] = " << ret << ";\n";
       }
     }
     std::string ret;
-    if (!emit_program_named(o, prog, names, nE, &ret)) return false;
+    if (!emit_program_vec(o, prog, names, nE, &ret, "t", &fuses)) return false;
     const std::string acc = L.unrolled ? "acc[i]" : "acc";
+    o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) {\n";
     if (j >= 0)
       o << "        " << acc << " = fold" << j << "(" << acc << ", " << ret << ");\n      }\n";
     else

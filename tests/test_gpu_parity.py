@@ -869,3 +869,45 @@ def test_decoder_block_row_programs_bit_exact(row_toggle):
         launches.append(be.launches - n0)
     assert outs[0] == outs[1]
     assert launches[0] < launches[1], launches
+
+
+def test_row_program_quantise_near_ties(row_toggle):
+    """Per-token quantisation through a row program (its division by the per-row scale runs as a
+    reciprocal product with an exact fallback near rounding ties) equals the unfused chain's exact
+    division bit for bit, on values placed within a few ulps of half-integer quotients, exact
+    ties, zeros, huge values and rows whose scale is 0 or NaN."""
+    from furiosa_opt_b200 import workloads as Wl
+    be = row_toggle
+    T, Wd = 64, 1024
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((T, Wd)) * rng.uniform(0.01, 100, (T, 1))).astype(np.float32)
+    amax = np.abs(x).max(1)
+    s = np.maximum(amax, np.float32(1e-12)) / np.float32(127)
+    k = rng.integers(-127, 127, (T, Wd)).astype(np.float32) + np.float32(0.5)
+    near = (k * s[:, None]).astype(np.float32)
+    ulps = rng.integers(-3, 4, (T, Wd)).astype(np.int32)
+    near = (near.view(np.int32) + ulps).view(np.float32)
+    pick = rng.random((T, Wd)) < 0.5
+    x = np.where(pick, near, x).astype(np.float32)
+    x[:, 0] = amax  # keep each row's max where it was, so the scale stays s
+    x[1, :] = 0.0
+    x[2, 5] = np.float32(3e38)
+    x[3, :] = np.nan
+    ax = dict(T=T, H=Wd)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+
+    def chain():
+        X = be.from_vec(m("[T, H]"), x.reshape(-1), "f32")
+        a = be.map(be.map(X, Wl._prog_abs(), "f32"), ops.Prog(1).build(0), "f32")
+        mx = be.reduce(a, "Max", 0.0, m("[T, H]"), m("[T]"))
+        sc = be.map(mx, Wl._prog_token_scale(), "f32")
+        xd = be.map(X, ops.Prog(1).build(0), "f32")  # a deferred value, so the chain stays lazy
+        q = be.zip_with(xd, be.relayout(sc, m("[T]"), m("[T, H]"), True), Wl._prog_quant(), "i8")
+        return q.to_bytes(), sc.to_bytes()
+
+    be.row_fusion = True
+    before = _lib.lib().fopt_elementwise_jit_launches()
+    fused = chain()
+    assert _lib.lib().fopt_elementwise_jit_launches() == before + 1
+    be.row_fusion = False
+    assert fused == chain()

@@ -362,7 +362,7 @@ def test_row_programs_lower_the_decoder_chains(monkeypatch):
     assert [plan.slot[j].kind for j in range(4)] == [FOLD, SCALAR, FOLD, SCALAR]
     assert plan.leaf_bcast[1] == -H and built[-1].slot_nodes[3] is s
     src = _row_source(plan)
-    assert b"NW = 1, RPC = 8" in src
+    assert b"NW = 8, RPC = 1" in src  # 64 rows: the whole CTA on a row
     _nvrtc_compile(src)
 
     # the attention output: one fold (max |x|), then the scale
