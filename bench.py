@@ -342,10 +342,10 @@ def wl_decoder_tp(fb, be, rank, world, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
     X = be.from_vec(blk.m("[T, H]"), fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32)),
                     "bf16")
 
-    def step():
-        return blk.forward(X)
-
-    return dict(step=step, units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8", aggregate=False,
+    step, e2e_step, hx, hout = graphed_step(fb, be, lambda: blk.forward(X), X, T * H * 2)
+    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(),
+                e2e_api="fopt_h2d -> captured block with its NCCL all-reduces (fopt_graph_launch) -> fopt_d2h",
+                units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8", aggregate=False,
                 scaling="strong", flops=blk.gemm_ops() + blk.attention_flops(),
                 metric="W8A8 decoder block tokens/s, tensor-parallel (Llama-3-8B shape, 8 x 512 tokens)",
                 workload="decoder_w8a8_tp",
