@@ -172,6 +172,9 @@ struct Params {
   // every range leaves its partial accumulator in ws, and the last range to finish adds them up
   // and runs the epilogue (cnt: one arrival counter per split tile, CTA and epilogue warp)
   int n_whole, split;
+  // or (halves = 1) the last wave's tiles [n_whole, ntiles) each run as two half-width tiles (BN / 2
+  // columns), which fill up to twice as many pairs in half the time; no partials are involved
+  int halves;
   uint32_t* ws;
   uint32_t* cnt;
   int trace_units;
@@ -182,11 +185,16 @@ struct Params {
 // One unit of the paired kernel's persistent loop: a whole tile, or one K-range of a split tile.
 struct Unit {
   int tile, kb0, kb1, part, sp;  // sp: index among the split tiles (-1 for a whole tile)
+  int nh;                        // half-width unit: which half of the tile's columns (-1: all of them)
 };
 __device__ __forceinline__ Unit unit_of(const Params& p, int u, int kblocks) {
   Unit w;
+  w.nh = -1;
   if (u < p.n_whole) {
     w.tile = u; w.kb0 = 0; w.kb1 = kblocks; w.part = 0; w.sp = -1;
+  } else if (p.halves) {
+    const int v = u - p.n_whole;
+    w.tile = p.n_whole + (v >> 1); w.nh = v & 1; w.kb0 = 0; w.kb1 = kblocks; w.part = 0; w.sp = -1;
   } else {
     const int v = u - p.n_whole;
     w.sp = v / p.split;
@@ -498,10 +506,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 //   acc_full[a]  (each CTA): MMA commit after the tile's last k-block, delivered to both
 //   acc_empty[a] (even CTA): one arrival per epilogue warp of both CTAs (16)
 // ---------------------------------------------------------------------------------------------
-constexpr int RING2_BYTES = 192 * 1024;
+// The operand ring: the mainloop is bound by the bytes in flight from L2 (a half-width tile's
+// k-blocks take as long as a whole one's), so the ring takes all the shared memory it can: 7 stages
+// at BN = 256 (the column scales are then read from L1 instead of staged), 9 at BN = 128.
+constexpr int RING2_BYTES = 224 * 1024;
+constexpr int SMEM_LIMIT = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
 template <int BN>
 constexpr int stages2() {
   return RING2_BYTES / (128 * BKB + (BN / 2) * BKB);
+}
+template <int BN>
+constexpr int scale_stage_bytes2() {  // the epilogue's staged column scales, when they still fit
+  return stages2<BN>() * (128 * BKB + (BN / 2) * BKB) + 1024 + 256 + 2 * EPI_WARPS * (BN / 2) * 4 <= SMEM_LIMIT
+             ? 2 * EPI_WARPS * (BN / 2) * 4
+             : 0;
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -576,7 +594,8 @@ __device__ __forceinline__ void add_staged(uint32_t* r, const uint32_t* stage, i
 
 template <bool IS_F16, int BN, int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmBh, Params p) {
   constexpr int STAGES2 = stages2<BN>();
   constexpr int A_BYTES = 128 * BKB;
   constexpr int B_BYTES = (BN / 2) * BKB;
@@ -602,7 +621,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int tiles_m = p.M / 256, tiles_n = p.N / BN;
   const int ntiles = tiles_m * tiles_n;
   const int kblocks = p.K * (IS_F16 ? 2 : 1) / BKB;
-  const int nunits = p.n_whole + (ntiles - p.n_whole) * p.split;
+  const int nunits = p.n_whole + (ntiles - p.n_whole) * (p.halves ? 2 : p.split);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES2; ++s) {
@@ -634,16 +653,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = pair; u < nunits; u += npairs) {
         const Unit w = unit_of(p, u, kblocks);
         const int m0 = (w.tile % tiles_m) * 256 + (int)rank * 128;
-        const int n0 = (w.tile / tiles_m) * BN + (int)rank * (BN / 2);
+        // each CTA holds half the unit's columns of B: BN / 2 of a whole tile, BN / 4 of a half
+        // (through the narrower box of tmBh)
+        const int n0 = (w.tile / tiles_m) * BN + (w.nh < 0 ? (int)rank * (BN / 2) : w.nh * (BN / 2) + (int)rank * (BN / 4));
+        const CUtensorMap* mB = w.nh < 0 ? &tmB : &tmBh;
+        const uint32_t tx = w.nh < 0 ? 2 * STAGE_BYTES : 2 * (A_BYTES + B_BYTES / 2);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(smem_u32(&empty[stage]), phase ^ 1, abort_flag, p.err, 201)) goto done_producer2;
           const uint32_t fb_local = smem_u32(&full[stage]);
           const uint32_t fb_pair = map_to_rank(fb_local, 0);
-          if (rank == 0) mbar_expect_tx(fb_local, 2 * STAGE_BYTES);
+          if (rank == 0) mbar_expect_tx(fb_local, tx);
           const int kx = kb * (IS_F16 ? BKB / 2 : BKB);
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           tma_load_2d_pair(sa, &tmA, fb_pair, kx, m0);
-          tma_load_2d_pair(sa + A_BYTES, &tmB, fb_pair, kx, n0);
+          tma_load_2d_pair(sa + A_BYTES, mB, fb_pair, kx, n0);
           if (++stage == STAGES2) {
             stage = 0;
             phase ^= 1;
@@ -666,12 +689,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
       else
         idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+      const uint32_t idesc_half = (idesc & ~(0x3fu << 17)) | ((uint32_t)(BN >> 4) << 17);  // N = BN / 2
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int u = pair; u < nunits; u += npairs) {
         const Unit w = unit_of(p, u, kblocks);
+        const uint32_t id = w.nh < 0 ? idesc : idesc_half;
         if (!mbar_wait(smem_u32(&acc_empty[acc]), acc_phase ^ 1, abort_flag, p.err, 203)) break;
         fence_after();
         if (p.trace) p.trace[u * 5] = globaltimer();
@@ -689,9 +714,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < BKB / KSTEP_BYTES; ++k) {
             const uint64_t adv = (uint64_t)((k * KSTEP_BYTES) >> 4);
             if (IS_F16)
-              mma2_f16(dcol, da + adv, db + adv, idesc, (kb != w.kb0) | (k != 0));
+              mma2_f16(dcol, da + adv, db + adv, id, (kb != w.kb0) | (k != 0));
             else
-              mma2_i8(dcol, da + adv, db + adv, idesc, (kb != w.kb0) | (k != 0));
+              mma2_i8(dcol, da + adv, db + adv, id, (kb != w.kb0) | (k != 0));
           }
           mma2_commit_both(smem_u32(&empty[stage]));
           if (++stage == STAGES2) {
@@ -718,18 +743,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t acc_phase = 0;
     for (int u = pair; u < nunits; u += npairs) {
       const Unit w = unit_of(p, u, kblocks);
-      const int m0 = (w.tile % tiles_m) * 256, n0 = (w.tile / tiles_m) * BN;
+      const int m0 = (w.tile % tiles_m) * 256, n0 = (w.tile / tiles_m) * BN + (w.nh < 0 ? 0 : w.nh * (BN / 2));
+      const int ncols = w.nh < 0 ? BN : BN / 2;
       // Stage this warp's column scales in shared memory while the MMAs run: its own copy, so
       // only the warp synchronises (double-buffered by accumulator). Chunk c = half + 2 i has its
       // 32 scales at wsc + 32 i.
       float* wsc = sscale + (acc * EPI_WARPS + (warp - 2)) * (BN / 2);
       float rs = 0.0f;
-      if constexpr (kColScale) {
+      constexpr bool kStaged = scale_stage_bytes2<BN>() > 0;
+      if constexpr (kColScale && kStaged) {
 #pragma unroll
-        for (int i = 0; i < BN / 64; ++i) wsc[i * 32 + lane] = __ldg(p.scale + n0 + (half + 2 * i) * 32 + lane);
-        if constexpr (MODE == EP_DQ) rs = __ldg(p.row_scale + m0 + row_in_tile);
+        for (int i = 0; i < BN / 64; ++i)
+          if (i < ncols / 64) wsc[i * 32 + lane] = __ldg(p.scale + n0 + (half + 2 * i) * 32 + lane);
         __syncwarp();
       }
+      if constexpr (MODE == EP_DQ) rs = __ldg(p.row_scale + m0 + row_in_tile);
       bool ok = mbar_wait(smem_u32(&acc_full[acc]), acc_phase, abort_flag, p.err, 205);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
@@ -811,12 +839,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (w.sp >= 0 && good) good = fetch(q_last);
         if (good) {
 #pragma unroll 1
-          for (int c = half; c < BN / 32; c += EPI_WARPS / 4) {
+          for (int c = half; c < ncols / 32; c += EPI_WARPS / 4) {
             uint32_t r[32];
             tmem_ld32(tbase + (uint32_t)(c * 32), r);
             if (tracer && w.sp < 0 && c == half) p.trace[u * 5 + 4] = globaltimer();
             if (w.sp >= 0) add_staged<IS_F16>(r, stage, (c - half) >> 1, lane);
-            const float* csc = wsc + (c - half) * 16;
+            const float* csc = kStaged ? wsc + (c - half) * 16 : p.scale + n0 + c * 32;
             const uint32_t nanmask = MODE == EP_RQ31 ? __ballot_sync(0xffffffffu, csc[lane] != csc[lane]) : 0u;
             epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r, csc, rs, nanmask);
           }
@@ -903,17 +931,27 @@ void launch(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const Par
 int plan_split(fopt_ctx* ctx, Params& p, int ntiles, int pairs, int kblocks, int bn, bool f32_acc) {
   p.n_whole = ntiles;
   p.split = 1;
+  p.halves = 0;
   p.ws = nullptr;
   p.cnt = nullptr;
-  if (getenv("FOPT_GEMM_NO_SPLIT")) return 1;
   const int rem = ntiles % pairs;
   if (rem == 0) return 1;
+  // Without a K split, a last wave that fills at most half the pairs runs as half-width tiles: the
+  // same columns on twice the pairs, in about half the time.
+  auto halves = [&]() {
+    if (ntiles > pairs && 2 * rem <= pairs && !getenv("FOPT_GEMM_NO_HALVES")) {
+      p.n_whole = ntiles - rem;
+      p.halves = 1;
+    }
+    return 1;
+  };
+  if (getenv("FOPT_GEMM_NO_SPLIT")) return halves();
   // Parking and fetching a partial costs about one epilogue (a few microseconds), so the split pays
   // when the ranges it shortens are long: a single part-filled wave, or a long K.
-  if (!(ntiles < pairs ? kblocks >= 16 : kblocks >= 96)) return 1;
+  if (!(ntiles < pairs ? kblocks >= 16 : kblocks >= 96)) return halves();
   // f32 partials: two ranges only, whose sum is the same whichever range finishes last
   const int split = std::min({pairs / rem, kblocks / 4, f32_acc ? 2 : 4});
-  if (split < 2) return 1;
+  if (split < 2) return halves();
   const size_t ws_bytes = (size_t)rem * split * 256 * bn * 4;
   const size_t n_cnt = (size_t)rem * 2 * EPI_WARPS;
   if (ws_bytes > ctx->gemm_ws_bytes) {
@@ -939,8 +977,9 @@ int plan_split(fopt_ctx* ctx, Params& p, int ntiles, int pairs, int kblocks, int
 }
 
 template <bool IS_F16, int BN, int MODE>
-void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, Params p) {
-  constexpr int smem = stages2<BN>() * (128 * BKB + (BN / 2) * BKB) + 1024 + 256 + 2 * EPI_WARPS * (BN / 2) * 4;
+void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& bh, Params p) {
+  constexpr int smem = stages2<BN>() * (128 * BKB + (BN / 2) * BKB) + 1024 + 256 + scale_stage_bytes2<BN>();
+  static_assert(smem <= SMEM_LIMIT, "paired GEMM shared memory");
   static bool attr = false;
   if (!attr) {
     cuda_check(cudaFuncSetAttribute(gemm_tc2_kernel<IS_F16, BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
@@ -951,7 +990,7 @@ void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, Params p
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device);
   const int tiles = (p.M / 256) * (p.N / BN);
   const int split = plan_split(ctx, p, tiles, sms / 2, p.K * (IS_F16 ? 2 : 1) / BKB, BN, IS_F16);
-  const int units = p.n_whole + (tiles - p.n_whole) * split;
+  const int units = p.n_whole + (tiles - p.n_whole) * (p.halves ? 2 : split);
   const int pairs = std::min(units, sms / 2);
   const char* trace_path = getenv("FOPT_GEMM_TRACE");
   p.trace = nullptr;
@@ -969,7 +1008,7 @@ void launch2(fopt_ctx* ctx, const CUtensorMap& a, const CUtensorMap& b, Params p
   attrs[0].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  cuda_check(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<IS_F16, BN, MODE>, a, b, p), "gemm_tc2 launch");
+  cuda_check(cudaLaunchKernelEx(&cfg, gemm_tc2_kernel<IS_F16, BN, MODE>, a, b, bh, p), "gemm_tc2 launch");
   launched(ctx, "gemm_tc2");
   if (trace_path) {  // diagnostics only: append "unit mma0 mma1 epi0 epi1 sm" lines (ns from the first start)
     std::vector<uint64_t> t((size_t)units * 5 + 2 * pairs * 3);
@@ -1066,9 +1105,10 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
   if (pair) bn = pair_tile_n(bn);
   CUtensorMap ma = make_map(a, f16, K, M, lda, pair ? 128 : BM);
   CUtensorMap mb = make_map(b, f16, K, N, ldb, pair ? bn / 2 : bn);
-#define FOPT_GEMM_DISPATCH(F16, MODE)                                \
-  if (pair && bn == 256) launch2<F16, 256, MODE>(ctx, ma, mb, p);    \
-  else if (pair) launch2<F16, 128, MODE>(ctx, ma, mb, p);            \
+  CUtensorMap mbh = pair ? make_map(b, f16, K, N, ldb, bn / 4) : mb;  // half-width tail tiles
+#define FOPT_GEMM_DISPATCH(F16, MODE)                                     \
+  if (pair && bn == 256) launch2<F16, 256, MODE>(ctx, ma, mb, mbh, p);    \
+  else if (pair) launch2<F16, 128, MODE>(ctx, ma, mb, mbh, p);            \
   else if (bn == 256) launch<F16, 256, MODE>(ctx, ma, mb, p);        \
   else launch<F16, 128, MODE>(ctx, ma, mb, p);
   if (f16) {
