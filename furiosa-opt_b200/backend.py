@@ -621,6 +621,21 @@ class B200:
         ep = _ep(3, scale, scale_axis, row_scale=row_scale)
         return self._contract(lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, "bf16", ep, out=out)
 
+    def contraction_swiglu(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, row_scale: Storage,
+                           scale: Storage, scale_axis: str) -> Storage:
+        """The gate and up projections of a SwiGLU and the activation, fused: rhs rows (and `scale`)
+        interleave 128 gate and 128 up channels; each pair is dequantised to bf16 exactly as
+        `contraction_dequant` does, and act = (g * sigmoid(g)) * u is computed in f32 as the
+        elementwise program would. `out_map` names the interleaved [M, N] product; the result is the
+        [M, N / 2] f32 activation. Raises FoptError (UNSUPPORTED) when the fused kernel does not
+        apply (M or N not a multiple of 256)."""
+        ep = _ep(4, scale, scale_axis, row_scale=row_scale)
+        out = Storage(self, "f32", out_map.size // 2, zero=False)
+        check(_lib.lib().fopt_contraction(self.ctx, out.ptr, _lib.DTYPES["f32"], lhs.ptr, rhs.ptr,
+                                          _lib.DTYPES[lhs.dtype], lhs_map.handle, rhs_map.handle, pre_reduce.handle,
+                                          out_map.handle, C.byref(ep)), self.ctx)
+        return out
+
     # ---- gather / scatter (backend/mod.rs:159-206) ----
     def gather(self, src: Storage, dst: Storage, index: Storage, Src: Mapping, Dst: Mapping, payload: Mapping,
                axis: Mapping, Idx: Mapping, scaled: bool = False) -> None:

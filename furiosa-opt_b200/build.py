@@ -25,6 +25,11 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", os.path
           "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
 
 
+# The GEMM's fused SwiGLU epilogue computes the activation with the same device code as the
+# generated elementwise kernels (NVRTC, --fmad=false), so it is compiled without contraction too.
+PER_FILE = {"k_gemm.cu": ["--fmad=false"]}
+
+
 def _sources():
     return sorted(os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cu", ".cpp")))
 
@@ -44,10 +49,10 @@ def _compile(src: str, verbose: bool) -> str:
     obj = os.path.join(OBJ, base + ".o")
     stamp = obj + ".stamp"
     with open(src, "rb") as fh:
-        key = hashlib.sha256(fh.read()).hexdigest()[:16] + _headers_digest()
+        key = hashlib.sha256(fh.read()).hexdigest()[:16] + _headers_digest() + str(PER_FILE.get(os.path.basename(src)))
     if os.path.exists(obj) and os.path.exists(stamp) and open(stamp).read() == key:
         return obj
-    cmd = [NVCC, *ARCH, *COMMON, "-c", src, "-o", obj]
+    cmd = [NVCC, *ARCH, *COMMON, *PER_FILE.get(os.path.basename(src), []), "-c", src, "-o", obj]
     if src.endswith(".cpp"):  # pure host code
         cmd = [NVCC, *COMMON, "-c", src, "-o", obj]
     if verbose:

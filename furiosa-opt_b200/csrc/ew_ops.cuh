@@ -148,6 +148,8 @@ __device__ __forceinline__ unsigned qdiv_fxp_fast(unsigned a, float rq, bool* ok
   const float r = f > 0.5f ? t + copysignf(1.0f, y) : t;
   return *ok ? (unsigned)(int)r : 0u;
 }
+// Sigmoid as the opcode table computes it: 1 / (1 + e^-x), the reciprocal correctly rounded.
+__device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(__fadd_rn(1.0f, expf(-x))); }
 // The per-row factor qdiv_fxp takes: RN(1 / s) scaled by 2^(31 - iw) (exact, or infinite: then every
 // element takes the exact path).
 __device__ __forceinline__ float qdiv_factor(unsigned s, unsigned iw) {
@@ -177,7 +179,7 @@ __device__ __forceinline__ float qdiv_factor(unsigned s, unsigned iw) {
   X(FOPT_OP_NEGEXP, W(expf(-fa)))                                                                         \
   X(FOPT_OP_SQRT, W(__fsqrt_rn(fa)))                                                                      \
   X(FOPT_OP_TANH, W(tanhf(fa)))                                                                           \
-  X(FOPT_OP_SIGMOID, W(__frcp_rn(__fadd_rn(1.0f, expf(-fa)))))                                             \
+  X(FOPT_OP_SIGMOID, W(sigmoid_f(fa)))                                                                     \
   X(FOPT_OP_LOG, W(logf(fa)))                                                                             \
   X(FOPT_OP_SIN, W(sinf(fa)))                                                                             \
   X(FOPT_OP_COS, W(cosf(fa)))                                                                             \

@@ -300,7 +300,12 @@ fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void* src, fopt_
 typedef struct {
   int32_t kind;           /* 0 none; 1 requant i32 -> i8 with per-channel scale; 2 relu;
                              3 dequant i32 -> bf16: FxpToFp -> MulF row_scale[m] -> MulF scale[n] -> cast
-                             (per-token x per-channel W8A8; GEMM-shaped contractions only) */
+                             (per-token x per-channel W8A8; GEMM-shaped contractions only);
+                             4 SwiGLU of interleaved gate / up projections: rhs rows (and scale) alternate
+                             128 gate and 128 up channels; each is dequantised to bf16 as kind 3, then
+                             act = (g * sigmoid(g)) * u in f32 (the MulF / Sigmoid chain) is written to an
+                             [M, N / 2] f32 output (out_map still names the [M, N] product;
+                             M % 256 and N % 256) */
   const float* scale;     /* kind 1, 3: one f32 per coordinate of `scale_axis` */
   const char* scale_axis; /* kind 1, 3: axis name the scale vector runs along (e.g. "N") */
   int32_t int_width;      /* FxpToFp / FpToFxp integer width (31 = plain integers) */

@@ -124,3 +124,47 @@ def test_mnist_int8_graph_replay_bit_exact(b200):
         fb._lib.check(lib.fopt_h2d(b200.ctx, X.ptr, x.ctypes.data, x.nbytes), b200.ctx)
         assert g.launch().to_bytes() == w
     g.close()
+
+
+def test_decoder_block_swiglu_epilogue_bit_exact(b200):
+    """Gate, up and the SwiGLU activation as one GEMM (interleaved weights, the activation computed in
+    the epilogue) give the block the bits of two projections and an elementwise program."""
+    batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+    T, H = batch * seq, Hq * 128
+    W.DecoderBlockW8A8.SWIGLU_EPILOGUE = True
+    try:
+        blk = W.DecoderBlockW8A8(b200, T, H, Hq, Hkv, F, batch, seq, seed=3)
+    finally:
+        W.DecoderBlockW8A8.SWIGLU_EPILOGUE = False
+    assert blk.fuse_swiglu
+    x = fb.dtypes.f32_to_bf16_bits(np.random.default_rng(5).standard_normal(T * H).astype(np.float32))
+    fused = blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_bytes()
+    assert blk.fuse_swiglu  # the fused kernel applied
+    blk.fuse_swiglu = False
+    assert blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_bytes() == fused
+
+
+@pytest.mark.parametrize("M,F,K", [(256, 256, 4096), (512, 2048, 512)])
+def test_swiglu_epilogue_matches_projections(b200, M, F, K):
+    """The fused SwiGLU projection against two dequant projections and the SwiGLU program: one shape
+    whose last wave splits K (parked partials added in the epilogue), one with several waves."""
+    rng = np.random.default_rng(M + F + K)
+    ax = dict(M=M, F=F, G=2 * F, K=K)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+    a = rng.integers(-127, 128, M * K).astype(np.int8)
+    wg = rng.integers(-127, 128, (F, K)).astype(np.int8)
+    wu = rng.integers(-127, 128, (F, K)).astype(np.int8)
+    sg = (rng.uniform(0.5, 1.5, F) / (127 * np.sqrt(K))).astype(np.float32)
+    su = (rng.uniform(0.5, 1.5, F) / (127 * np.sqrt(K))).astype(np.float32)
+    st = rng.uniform(0.001, 0.05, M).astype(np.float32)
+    A, S = b200.from_vec(m("[M, K]"), a, "i8"), b200.from_vec(m("[M]"), st, "f32")
+    Wg, Wu = b200.from_vec(m("[F, K]"), wg.reshape(-1), "i8"), b200.from_vec(m("[F, K]"), wu.reshape(-1), "i8")
+    Sg, Su = b200.from_vec(m("[F]"), sg, "f32"), b200.from_vec(m("[F]"), su, "f32")
+    g = b200.contraction_dequant(A, Wg, m("[M, K]"), m("[F, K]"), m("[M, F, K]"), m("[M, F]"), S, Sg, "F")
+    u = b200.contraction_dequant(A, Wu, m("[M, K]"), m("[F, K]"), m("[M, F, K]"), m("[M, F]"), S, Su, "F")
+    want = b200.zip_with(g, u, W._prog_swiglu(), "f32").to_bytes()
+    wgu = np.stack([wg.reshape(F // 128, 128, K), wu.reshape(F // 128, 128, K)], 1).reshape(2 * F, K)
+    sgu = np.stack([sg.reshape(F // 128, 128), su.reshape(F // 128, 128)], 1).reshape(2 * F)
+    Wgu, Sgu = b200.from_vec(m("[G, K]"), wgu.reshape(-1), "i8"), b200.from_vec(m("[G]"), sgu, "f32")
+    got = b200.contraction_swiglu(A, Wgu, m("[M, K]"), m("[G, K]"), m("[M, G, K]"), m("[M, G]"), S, Sgu, "G")
+    assert got.to_bytes() == want
