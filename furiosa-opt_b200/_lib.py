@@ -51,7 +51,8 @@ class RowPlan(C.Structure):
 
 class Epilogue(C.Structure):
     _fields_ = [("kind", C.c_int32), ("scale", C.c_void_p), ("scale_axis", C.c_char_p), ("int_width", C.c_int32),
-                ("clip_lo", C.c_int32), ("clip_hi", C.c_int32), ("row_scale", C.c_void_p)]
+                ("clip_lo", C.c_int32), ("clip_hi", C.c_int32), ("row_scale", C.c_void_p),
+                ("residual", C.c_void_p)]
 
 
 # (name, restype, argtypes) for every symbol the header declares.

@@ -261,9 +261,10 @@ class Graph:
             pass
 
 
-def _ep(kind=0, scale=None, axis=None, int_width=31, lo=-128, hi=127, row_scale=None):
+def _ep(kind=0, scale=None, axis=None, int_width=31, lo=-128, hi=127, row_scale=None, residual=None):
     e = _lib.Epilogue()
     e.row_scale = row_scale.addr if isinstance(row_scale, Storage) else (row_scale or 0)
+    e.residual = residual.addr if isinstance(residual, Storage) else (residual or 0)
     e.kind = kind
     e.scale = scale.addr if isinstance(scale, Storage) else (scale or 0)
     e.scale_axis = axis.encode() if axis else None
@@ -616,9 +617,14 @@ class B200:
         return self._contract(lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, "i8", ep, out=out)
 
     def contraction_dequant(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, row_scale: Storage,
-                            scale: Storage, scale_axis: str, out=None) -> Storage:
-        """W8A8: i8 x i8 -> i32 -> FxpToFp -> MulF(row_scale[m]) -> MulF(scale[n]) -> bf16, fused."""
-        ep = _ep(3, scale, scale_axis, row_scale=row_scale)
+                            scale: Storage, scale_axis: str, out=None, residual: Optional[Storage] = None) -> Storage:
+        """W8A8: i8 x i8 -> i32 -> FxpToFp -> MulF(row_scale[m]) -> MulF(scale[n]) -> bf16, fused.
+        With `residual` (bf16, laid out as the output), the residual add that follows a projection
+        is fused too: out = bf16(f32(residual) + f32(projection)), the projection rounded to bf16
+        first, as the separate ops do."""
+        if residual is not None and (residual.dtype != "bf16" or residual.n != out_map.size):
+            raise ValueError("contraction_dequant: the residual must be bf16 laid out as the output")
+        ep = _ep(5 if residual is not None else 3, scale, scale_axis, row_scale=row_scale, residual=residual)
         return self._contract(lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, "bf16", ep, out=out)
 
     def contraction_swiglu(self, lhs, rhs, lhs_map, rhs_map, pre_reduce, out_map, row_scale: Storage,

@@ -669,10 +669,11 @@ static std::shared_ptr<FoldKPlan> contraction_plan(fopt_ctx* ctx, fopt_dtype out
     require(acc == FOPT_I32 && out_dtype == FOPT_F32, "SwiGLU epilogue maps an integer contraction to f32");
     require(epilogue->scale && epilogue->scale_axis && epilogue->row_scale,
             "SwiGLU epilogue needs row and channel scale vectors");
-  } else if (ep_kind == 3) {
+  } else if (ep_kind == 3 || ep_kind == 5) {
     require(acc == FOPT_I32 && out_dtype == FOPT_BF16, "dequant epilogue maps an integer contraction to bf16");
     require(epilogue->scale && epilogue->scale_axis && epilogue->row_scale,
             "dequant epilogue needs row and channel scale vectors");
+    require(ep_kind == 3 || epilogue->residual, "residual epilogue needs the residual");
   } else if (ep_kind == 1) {
     require(acc == FOPT_I32, "requant epilogue needs an integer contraction");
     require(out_dtype == FOPT_I8, "requant epilogue commits i8");
@@ -680,7 +681,7 @@ static std::shared_ptr<FoldKPlan> contraction_plan(fopt_ctx* ctx, fopt_dtype out
   } else {
     require(out_dtype == in_dtype || out_dtype == acc, "fopt_contraction: out dtype must be the operand or accumulator type");
   }
-  const bool scaled = ep_kind == 1 || ep_kind == 3 || ep_kind == 4;
+  const bool scaled = ep_kind == 1 || ep_kind == 3 || ep_kind == 4 || ep_kind == 5;
   std::string extra_key = scaled ? std::string(epilogue->scale_axis) : "";
   std::string key = "c|" + lhs_map->key + "|" + rhs_map->key + "|" + pre_reduce->key + "|" + out_map->key + "|" + extra_key;
   {
@@ -711,7 +712,7 @@ static void run_contraction(fopt_ctx* ctx, const FoldKPlan& kp, void* out, fopt_
                             const void* rhs, fopt_dtype in_dtype, int64_t lhs_elems, int64_t rhs_elems,
                             const fopt_epilogue* epilogue) {
   const int ep_kind = epilogue ? epilogue->kind : 0;
-  const bool scaled = ep_kind == 1 || ep_kind == 3 || ep_kind == 4;
+  const bool scaled = ep_kind == 1 || ep_kind == 3 || ep_kind == 4 || ep_kind == 5;
   int64_t M, N, K, lda, ldb, ldd;
   int scale_n = 0;
   if (as_gemm(kp, &M, &N, &K, &lda, &ldb, &ldd, &scale_n) && (!scaled || scale_n)) {
@@ -724,7 +725,7 @@ static void run_contraction(fopt_ctx* ctx, const FoldKPlan& kp, void* out, fopt_
   if (ep_kind == 4)
     throw Fail{FOPT_ERR_UNSUPPORTED, "SwiGLU epilogue needs a GEMM-shaped contraction with M % 256 and N % 256, "
                                      "scales along N, on the paired tensor-core kernel"};
-  if (ep_kind == 3)
+  if (ep_kind == 3 || ep_kind == 5)
     throw Fail{FOPT_ERR_UNSUPPORTED, "dequant epilogue needs a GEMM-shaped contraction ([M, K] x [N, K] -> [M, N], "
                                      "M % 128, K % 128 bytes, N % 128, scales along N)"};
   launch_contraction_generic(ctx, kp, out, out_dtype, lhs, rhs, in_dtype, lhs_elems, rhs_elems, epilogue, nullptr,
@@ -756,7 +757,8 @@ fopt_status fopt_contraction_host(fopt_ctx* ctx, void* host_out, fopt_dtype out_
                                   const fopt_mapping* out_map, const fopt_epilogue* epilogue) {
   return guarded(ctx, [&] {
     require(host_out && host_lhs && host_rhs, "fopt_contraction_host: null argument");
-    require(!epilogue || epilogue->kind != 4, "fopt_contraction_host: the SwiGLU epilogue runs on device storages");
+    require(!epilogue || (epilogue->kind != 4 && epilogue->kind != 5),
+            "fopt_contraction_host: the SwiGLU and residual epilogues run on device storages");
     auto kp = contraction_plan(ctx, out_dtype, in_dtype, lhs_map, rhs_map, pre_reduce, out_map, epilogue);
     const int64_t lhs_elems = lhs_map->m.size(), rhs_elems = rhs_map->m.size(), out_elems = out_map->m.size();
     const size_t lb = (size_t)(lhs_elems * dtype_bits(in_dtype) + 7) / 8, rb = (size_t)(rhs_elems * dtype_bits(in_dtype) + 7) / 8;

@@ -168,6 +168,7 @@ struct Params {
   const float* scale;
   int int_width, clip_lo, clip_hi;
   const float* row_scale;
+  const uint16_t* residual;  // EP_DQ: optional bf16 [M, N] added after the cast (same ldd as D)
   int* err;
   // split of the last wave (paired kernel): tiles [n_whole, ntiles) each run as `split` K-ranges;
   // every range leaves its partial accumulator in ws, and the last range to finish adds them up
@@ -332,6 +333,21 @@ __device__ __forceinline__ void epilogue_store(const Params& p, int row, int col
         if ((b & 0x7fffffffu) <= 0x7f800000u && (b >> 31)) b = 0u;
       }
       packed[j / 2] = bf16x2_rule(__uint_as_float(a), __uint_as_float(b));
+    }
+    if (MODE == EP_DQ && p.residual) {
+      // the residual add that follows the projection: bf16(f32(x) + f32(o)), o the bf16 just formed
+      const uint4* xr = (const uint4*)(p.residual + (int64_t)row * p.ldd + col);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 xv = xr[q];
+        const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t o = packed[4 * q + t], x = xs[t];
+          packed[4 * q + t] = bf16x2_rule(__fadd_rn(__uint_as_float(x << 16), __uint_as_float(o << 16)),
+                                          __fadd_rn(__uint_as_float(x & 0xffff0000u), __uint_as_float(o & 0xffff0000u)));
+        }
+      }
     }
     uint4* dst = (uint4*)(base + ((int64_t)row * p.ldd + col) * 2);
 #pragma unroll
@@ -1144,8 +1160,12 @@ bool launch_gemm_tc(fopt_ctx* ctx, void* out, int out_dt, const void* a, const v
         getenv("FOPT_GEMM_1SM"))
       return false;
     mode = EP_SWIGLU;
-  } else if (ep_kind == 3) {
+  } else if (ep_kind == 3 || ep_kind == 5) {
     if ((uintptr_t)scale % 16 || !p.row_scale || odt != FOPT_BF16) return false;
+    if (ep_kind == 5) {
+      if (!ep->residual || (uintptr_t)ep->residual % 16) return false;
+      p.residual = (const uint16_t*)ep->residual;
+    }
     mode = EP_DQ;
   } else if (ep_kind == 1) {
     if ((uintptr_t)scale % 16) return false;

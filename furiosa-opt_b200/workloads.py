@@ -138,6 +138,8 @@ class DecoderBlockW8A8:
         assert T == batch * seq and H == Hq * 128
         self.be, self.T, self.H, self.Hq, self.Hkv, self.F = be, T, H, Hq, Hkv, F
         self.batch, self.seq = batch, seq
+        # residual adds in the O and down projections' epilogues (off: separate elementwise ops)
+        self.fuse_residual = not os.environ.get("FOPT_NO_RESIDUAL_EPILOGUE")
         self.KV = Hkv * 128
         rng = np.random.default_rng(seed)
         self.ax = dict(T=T, H=H, Q=H, V=self.KV, F=F)
@@ -207,10 +209,22 @@ class DecoderBlockW8A8:
         q = be.zip_with(x_f32, sb, _prog_quant(), "i8")
         return q, s
 
-    def proj(self, q: Storage, s_tok: Storage, w: Storage, s_w: Storage, k_ax: str, n_ax: str) -> Storage:
+    def proj(self, q: Storage, s_tok: Storage, w: Storage, s_w: Storage, k_ax: str, n_ax: str,
+             residual: Storage = None) -> Storage:
         m = self.m
         return self.be.contraction_dequant(q, w, m(f"[T, {k_ax}]"), m(f"[{n_ax}, {k_ax}]"), m(f"[T, {n_ax}, {k_ax}]"),
-                                           m(f"[T, {n_ax}]"), s_tok, s_w, n_ax)
+                                           m(f"[T, {n_ax}]"), s_tok, s_w, n_ax, residual=residual)
+
+    def proj_residual(self, q, s_tok, w, s_w, k_ax, n_ax, x):
+        """x + proj(...), the residual add in the projection's epilogue when `fuse_residual`."""
+        if self.fuse_residual:
+            try:
+                return self.proj(q, s_tok, w, s_w, k_ax, n_ax, residual=x)
+            except FoptError as e:
+                if e.status != FOPT_ERR_UNSUPPORTED:
+                    raise
+                self.fuse_residual = False
+        return self.be.zip_with(x, self.proj(q, s_tok, w, s_w, k_ax, n_ax), _prog_residual(), "bf16")
 
     def forward(self, x: Storage) -> Storage:
         """x: bf16 [T, H] -> bf16 [T, H]."""
@@ -222,8 +236,7 @@ class DecoderBlockW8A8:
         V = self.proj(q, s, self.wv, self.sv, "H", "V")
         att = be.attention(Q, K, V, self.batch, self.seq, self.Hq, self.Hkv, 128, causal=True)
         qa, sa = self.quantize(be.map(att, ops.cast("bf16", "f32"), "f32"), "H")
-        o = self.proj(qa, sa, self.wo, self.so, "H", "Q")
-        h1 = be.zip_with(x, o, _prog_residual(), "bf16")
+        h1 = self.proj_residual(qa, sa, self.wo, self.so, "H", "Q", x)
         h1f = be.map(h1, ops.cast("bf16", "f32"), "f32")
         q2, s2 = self.quantize(self.rmsnorm(h1f, self.g2), "H")
         act = None
@@ -241,8 +254,7 @@ class DecoderBlockW8A8:
             u = self.proj(q2, s2, self.wu, self.su, "H", "F")
             act = be.zip_with(g, u, _prog_swiglu(), "f32")
         q3, s3 = self.quantize(act, "F")
-        d = self.proj(q3, s3, self.wd, self.sd, "F", "Q")
-        return be.zip_with(h1, d, _prog_residual(), "bf16")
+        return self.proj_residual(q3, s3, self.wd, self.sd, "F", "Q", h1)
 
     def gemm_ops(self) -> float:
         """Algorithmic int8 ops of the block's projections."""

@@ -305,12 +305,15 @@ typedef struct {
                              128 gate and 128 up channels; each is dequantised to bf16 as kind 3, then
                              act = (g * sigmoid(g)) * u in f32 (the MulF / Sigmoid chain) is written to an
                              [M, N / 2] f32 output (out_map still names the [M, N] product;
-                             M % 256 and N % 256) */
+                             M % 256 and N % 256);
+                             5 dequant as kind 3, then the residual add that follows it:
+                             out = bf16(f32(residual) + f32(dequant)) (ResidualAdd of two bf16 values) */
   const float* scale;     /* kind 1, 3: one f32 per coordinate of `scale_axis` */
   const char* scale_axis; /* kind 1, 3: axis name the scale vector runs along (e.g. "N") */
   int32_t int_width;      /* FxpToFp / FpToFxp integer width (31 = plain integers) */
   int32_t clip_lo, clip_hi; /* kind 1: Clip bounds before the i8 commit */
-  const float* row_scale; /* kind 3: one f32 per output row (the outer output axis, e.g. the token) */
+  const float* row_scale; /* kind 3, 4, 5: one f32 per output row (the outer output axis, e.g. the token) */
+  const void* residual;   /* kind 5: bf16 values laid out as the output */
 } fopt_epilogue;
 fopt_status fopt_contraction(fopt_ctx* ctx, void* out, fopt_dtype out_dtype, const void* lhs, const void* rhs,
                              fopt_dtype in_dtype, const fopt_mapping* lhs_map, const fopt_mapping* rhs_map,

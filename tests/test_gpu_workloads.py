@@ -168,3 +168,17 @@ def test_swiglu_epilogue_matches_projections(b200, M, F, K):
     Wgu, Sgu = b200.from_vec(m("[G, K]"), wgu.reshape(-1), "i8"), b200.from_vec(m("[G]"), sgu, "f32")
     got = b200.contraction_swiglu(A, Wgu, m("[M, K]"), m("[G, K]"), m("[M, G, K]"), m("[M, G]"), S, Sgu, "G")
     assert got.to_bytes() == want
+
+
+def test_decoder_block_residual_epilogue_bit_exact(b200):
+    """The residual adds folded into the O and down projections' epilogues (the projection rounded
+    to bf16, added to the residual in f32, rounded again) give the block the bits of separate ops."""
+    batch, seq, Hq, Hkv, F = 2, 128, 4, 2, 1024
+    T, H = batch * seq, Hq * 128
+    blk = W.DecoderBlockW8A8(b200, T, H, Hq, Hkv, F, batch, seq, seed=3)
+    x = fb.dtypes.f32_to_bf16_bits(np.random.default_rng(6).standard_normal(T * H).astype(np.float32))
+    assert blk.fuse_residual
+    fused = blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_bytes()
+    assert blk.fuse_residual  # the fused epilogue applied
+    blk.fuse_residual = False
+    assert blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_bytes() == fused
