@@ -393,3 +393,33 @@ def test_row_programs_decline_without_a_reduction(monkeypatch):
     sb = be.relayout(B.Storage(be, "f32", T), fb.Mapping("[T]", ax), fb.Mapping("[T, H]", ax), True)
     be.zip_with(x, sb, Wl._prog_quant(), "i8")
     assert built == [None]
+
+
+def test_row_program_without_room_for_held_values(monkeypatch):
+    """A SwiGLU -> quantisation chain over 32768-wide rows would need 128 registers to hold its
+    activation: the plan holds nothing (the passes recompute it from the leaves) and still
+    compiles."""
+    from furiosa_opt_b200 import workloads as Wl
+    B, be, built = _fake_backend(monkeypatch)
+    T, F = 16, 32768
+    blk = Wl.DecoderBlockW8A8.__new__(Wl.DecoderBlockW8A8)
+    blk.be, blk.T, blk.F = be, T, F
+    blk.ax = dict(T=T, F=F)
+    gate, up = B.Storage(be, "bf16", T * F), B.Storage(be, "bf16", T * F)
+    blk.quantize(be.zip_with(gate, up, Wl._prog_swiglu(), "f32"), "F")
+    plan = built[-1].plan
+    assert (plan.n_leaves, plan.n_held, plan.n_slots, plan.row_len) == (2, 0, 2, F)
+    _nvrtc_compile(_row_source(plan))
+
+
+def test_residual_epilogue_checks_its_operand(monkeypatch):
+    """contraction_dequant's fused residual must be bf16 laid out as the output."""
+    B, be, built = _fake_backend(monkeypatch)
+    ax = dict(M=256, N=256, K=128)
+    m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+    a, w = B.Storage(be, "i8", 256 * 128), B.Storage(be, "i8", 256 * 128)
+    s_row, s_col = B.Storage(be, "f32", 256), B.Storage(be, "f32", 256)
+    for bad in (B.Storage(be, "f32", 256 * 256), B.Storage(be, "bf16", 256 * 128)):
+        with pytest.raises(ValueError):
+            be.contraction_dequant(a, w, m("[M, K]"), m("[N, K]"), m("[M, N, K]"), m("[M, N]"), s_row, s_col, "N",
+                                   residual=bad)
