@@ -224,6 +224,19 @@ fopt_status fopt_alloc_uninit(fopt_ctx* ctx, size_t bytes, void** dptr) {
   });
 }
 
+// Frees device memory outside a capture. A captured graph's allocation is no longer the graph's
+// to release afterwards; one from a graph never launched was never mapped and needs no free.
+static void release_now(fopt_ctx* ctx, void* dptr) {
+  auto it = ctx->graph_mem.find(dptr);
+  if (it != ctx->graph_mem.end()) {
+    fopt_graph* g = it->second;
+    ctx->graph_mem.erase(it);
+    g->owned.erase(dptr);
+    if (!g->launched) return;
+  }
+  cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");
+}
+
 fopt_status fopt_free(fopt_ctx* ctx, void* dptr) {
   if (!ctx) return FOPT_ERR_INVALID;
   return guarded(ctx, [&] {
@@ -235,14 +248,7 @@ fopt_status fopt_free(fopt_ctx* ctx, void* dptr) {
         ctx->deferred_free.push_back(dptr);  // memory from before the capture: released after it
       return;
     }
-    auto it = ctx->graph_mem.find(dptr);
-    if (it != ctx->graph_mem.end()) {  // a graph's allocation: it is no longer the graph's to release
-      fopt_graph* g = it->second;
-      ctx->graph_mem.erase(it);
-      g->owned.erase(dptr);
-      if (!g->launched) return;  // never mapped
-    }
-    cuda_check(cudaFreeAsync(dptr, ctx->stream), "cudaFreeAsync");
+    release_now(ctx, dptr);
   });
 }
 
@@ -280,7 +286,12 @@ fopt_status fopt_capture_end(fopt_ctx* ctx, fopt_graph** out) {
     cudaError_t e = cudaStreamEndCapture(ctx->stream, &g->graph);
     if (e == cudaSuccess)
       e = cudaGraphInstantiateWithFlags(&g->exec, g->graph, cudaGraphInstantiateFlagAutoFreeOnLaunch);
-    for (void* p : ctx->deferred_free) cudaFreeAsync(p, ctx->stream);
+    for (void* p : ctx->deferred_free) {
+      try {
+        release_now(ctx, p);
+      } catch (const Fail&) {
+      }
+    }
     ctx->deferred_free.clear();
     if (e != cudaSuccess) {
       if (g->graph) cudaGraphDestroy(g->graph);

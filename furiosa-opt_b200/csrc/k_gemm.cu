@@ -1013,7 +1013,9 @@ int plan_split(fopt_ctx* ctx, Params& p, int ntiles, int pairs, int kblocks, int
   if (getenv("FOPT_GEMM_NO_SPLIT")) return halves();
   // Parking and fetching a partial costs about one epilogue (a few microseconds), so the split pays
   // when the ranges it shortens are long: a single part-filled wave, or a long K.
-  if (!(ntiles < pairs ? kblocks >= 16 : kblocks >= 96)) return halves();
+  // (at 4096^3 a 2-way split of the last wave measured 62.5 us against 59.7 us for half-width tiles)
+  const int min_kb = getenv("FOPT_GEMM_SPLIT_MIN_KB") ? atoi(getenv("FOPT_GEMM_SPLIT_MIN_KB")) : 96;
+  if (!(ntiles < pairs ? kblocks >= 16 : kblocks >= min_kb)) return halves();
   // f32 partials: two ranges only, whose sum is the same whichever range finishes last
   const int split = std::min({pairs / rem, kblocks / 4, f32_acc ? 2 : 4});
   if (split < 2) return halves();
