@@ -368,9 +368,37 @@ def wl_decoder_tp(fb, be, rank, world, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
                         "gemm_ops": blk.gemm_ops(), "attention_flops": blk.attention_flops()})
 
 
+def bind_to_gpu_cpus(local: int) -> str:
+    """Pins this process to the CPUs NVML reports as local to the GPU (a read-only query), so the
+    pinned host buffers of the end-to-end steps sit on the GPU's NUMA node; host-to-device copies
+    from the other socket's memory cross the inter-socket link. Returns what it did."""
+    if os.environ.get("FOPT_NO_NUMA_BIND"):
+        return "off"
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        try:
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[local]) if visible else local
+            h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, (os.cpu_count() + 63) // 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {w * 64 + b for w, word in enumerate(words) for b in range(64) if word >> b & 1}
+        cpus &= set(range(os.cpu_count()))
+        if not cpus:
+            return "no affinity reported"
+        os.sched_setaffinity(0, cpus)
+        return f"{len(cpus)} GPU-local CPUs"
+    except Exception as e:  # no NVML or no permission: run unbound
+        return f"unbound ({type(e).__name__})"
+
+
 def run_ours(args, rank, world, local):
     import torch
 
+    numa = bind_to_gpu_cpus(local)
     fb = _pkg()
     torch.cuda.set_device(local)
     be = fb.B200(local)
@@ -462,7 +490,8 @@ def run_ours(args, rank, world, local):
             "config": {"workload": wl["workload"], **wl["config"], "l2": "flushed (256 MiB write) between steps",
                        "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
                                        f"tensor-parallel x{world} (NCCL)" if wl.get("scaling") == "strong" else
-                                       f"replicas x{world}") if world > 1 else "1 GPU"},
+                                       f"replicas x{world}") if world > 1 else "1 GPU",
+                       "host_cpus": numa},
             "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
             "wall_s": round(wall, 4)}
     if e2e_ms:
