@@ -423,3 +423,44 @@ def test_residual_epilogue_checks_its_operand(monkeypatch):
         with pytest.raises(ValueError):
             be.contraction_dequant(a, w, m("[M, K]"), m("[N, K]"), m("[M, N, K]"), m("[M, N]"), s_row, s_col, "N",
                                    residual=bad)
+
+
+@pytest.mark.parametrize("case", ["held_warp_per_row", "i32_load_slot", "i8_leaf", "f32_wide"])
+def test_row_program_layouts_compile(monkeypatch, case):
+    """Row plans across the generator's layouts compile for sm_100a: held values with one warp per
+    row (unrolled, no CTA barrier), i32 folds with a LOAD slot and an i16 output, i8 leaves, and
+    f32 leaves at a width with a partial last group of 2048."""
+    from furiosa_opt_b200 import ops, workloads as Wl
+    B, be, built = _fake_backend(monkeypatch)
+    if case == "held_warp_per_row":
+        T, F = 8192, 1024
+        blk = Wl.DecoderBlockW8A8.__new__(Wl.DecoderBlockW8A8)
+        blk.be, blk.T, blk.F, blk.ax = be, T, F, dict(T=T, F=F)
+        gate, up = B.Storage(be, "bf16", T * F), B.Storage(be, "bf16", T * F)
+        blk.quantize(be.zip_with(gate, up, Wl._prog_swiglu(), "f32"), "F")
+        plan = built[-1].plan
+        assert plan.n_held == 1
+        src = _row_source(plan)
+        assert b"NW = 1, RPC = 8" in src
+    else:
+        T, Wd = 64, {"i32_load_slot": 3000, "i8_leaf": 4096, "f32_wide": 6144 + 8}[case]
+        ax = dict(T=T, H=Wd)
+        m = lambda e: fb.Mapping(e, ax)  # noqa: E731
+        if case == "i32_load_slot":
+            A = B.Storage(be, "i32", T * Wd)
+            off = be.relayout(B.Storage(be, "i32", T), m("[T]"), m("[T, H]"), True)
+            p = ops.Prog(2)
+            v = be.zip_with(A, off, p.build(p.emit("ADD_FXP", 0, 1)), "i32")
+            lo = be.reduce(v, "Min", 2**31 - 1, m("[T, H]"), m("[T]"))
+            p = ops.Prog(2)
+            be.zip_with(v, be.relayout(lo, m("[T]"), m("[T, H]"), True), p.build(p.emit("XOR", 0, 1)), "i16")
+        else:
+            dt = "i8" if case == "i8_leaf" else "f32"
+            X = B.Storage(be, dt, T * Wd)
+            xf = be.map(X, ops.cast("i8", "f32") if dt == "i8" else ops.Prog(1).build(0), "f32")
+            mx = be.reduce(be.map(xf, Wl._prog_abs(), "f32"), "Max", 0.0, m("[T, H]"), m("[T]"))
+            sc = be.map(mx, Wl._prog_token_scale(), "f32")
+            be.zip_with(xf, be.relayout(sc, m("[T]"), m("[T, H]"), True), Wl._prog_quant(), "i8")
+        plan = built[-1].plan
+        src = _row_source(plan)
+    _nvrtc_compile(src)
