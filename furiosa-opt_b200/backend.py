@@ -261,6 +261,9 @@ class Graph:
             pass
 
 
+_COMPOSED = {}  # composition signature -> composed program (None: does not fit)
+
+
 def _ep(kind=0, scale=None, axis=None, int_width=31, lo=-128, hi=127, row_scale=None, residual=None):
     e = _lib.Epilogue()
     e.row_scale = row_scale.addr if isinstance(row_scale, Storage) else (row_scale or 0)
@@ -418,14 +421,25 @@ class B200:
                 parts.append(("leaf", leaf_reg(s)))
         if len(leaves) > self.MAX_LEAVES:
             return None
+        # the composed program depends only on the programs and the leaf registers they read
+        key = (bytes(prog), len(leaves),
+               tuple((p[0], p[1]) if p[0] == "leaf" else (p[0], bytes(p[1]), tuple(p[2])) for p in parts))
+        cache = _COMPOSED
+        if key in cache:
+            built = cache[key]
+            return (built, leaves) if built is not None else None
         out = ops.Prog(len(leaves))
         regs = []
         try:
             for part in parts:
                 regs.append(part[1] if part[0] == "leaf" else ops.inline(out, part[1], part[2]))
-            return out.build(ops.inline(out, prog, regs)), leaves
+            built = out.build(ops.inline(out, prog, regs))
         except ValueError:
-            return None
+            built = None
+        if len(cache) >= 4096:
+            cache.clear()
+        cache[key] = built
+        return (built, leaves) if built is not None else None
 
     def _run_ew(self, prog, leaves, out: Storage, origin=None) -> None:
         if self.fuse and self.row_fusion and rowfuse.try_row_program(self, prog, leaves, out, origin):

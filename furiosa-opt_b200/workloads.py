@@ -185,7 +185,12 @@ class DecoderBlockW8A8:
         return {self.H: "H", self.F: "F"}[k]
 
     def m(self, e: str) -> Mapping:
-        return Mapping(e, self.ax)
+        # parsed once per expression and axis table (a forward asks for the same few dozen)
+        cache = self.__dict__.setdefault("_mappings", {})
+        key = (e, tuple(sorted(self.ax.items())))
+        if key not in cache:
+            cache[key] = Mapping(e, self.ax)
+        return cache[key]
 
     # ---- vector-engine steps ----
     def rmsnorm(self, x_f32: Storage, g: Storage) -> Storage:
