@@ -34,6 +34,9 @@ class _NoRow(Exception):
     pass
 
 
+_PROGS = {}  # element-program signature -> composed program
+
+
 def _is_lazy(s, kind):
     return s.lazy is not None and s.lazy[0] == kind
 
@@ -138,7 +141,31 @@ class _Planner:
     # ---- programs ----
     def elem_prog(self, root_prog, root_inputs, n_in, reg_of):
         """Composes the element program of a pass (or of a held value) over n_in input registers;
-        reg_of(node) returns the register of a node that is an input, or None to expand it."""
+        reg_of(node) returns the register of a node that is an input, or None to expand it.
+        Memoised on the tree the program computes (programs and input registers): two graphs with
+        the same tree compute the same function of the same registers."""
+        sigs = {}
+
+        def sig(x):
+            if id(x) not in sigs:
+                r = reg_of(x)
+                if r is not None:
+                    sigs[id(x)] = r
+                else:
+                    prog, inputs = _children(x)
+                    sigs[id(x)] = (bytes(prog), tuple(sig(c) for c in inputs))
+            return sigs[id(x)]
+
+        key = (n_in, bytes(root_prog), tuple(sig(c) for c in root_inputs))
+        if key in _PROGS:
+            return _PROGS[key]
+        built = self._elem_prog(root_prog, root_inputs, n_in, reg_of)
+        if len(_PROGS) >= 4096:
+            _PROGS.clear()
+        _PROGS[key] = built
+        return built
+
+    def _elem_prog(self, root_prog, root_inputs, n_in, reg_of):
         b = ops.Prog(n_in)
         memo = {}
 
