@@ -464,3 +464,56 @@ def test_row_program_layouts_compile(monkeypatch, case):
         plan = built[-1].plan
         src = _row_source(plan)
     _nvrtc_compile(src)
+
+
+def test_composition_cache_returns_the_fresh_composition(monkeypatch):
+    """A memoised composition is the program a fresh composition builds, byte for byte."""
+    from furiosa_opt_b200 import backend as Bk, ops, workloads as Wl
+    B, be, built = _fake_backend(monkeypatch)
+    n = 64
+    x, y = B.Storage(be, "bf16", n), B.Storage(be, "f32", n)
+    xf = be.map(x, ops.cast("bf16", "f32"), "f32")
+    z = be.zip_with(xf, y, Wl._prog_swiglu(), "f32")
+    first = bytes(z.lazy[1])
+    Bk._COMPOSED.clear()
+    again = be.zip_with(be.map(x, ops.cast("bf16", "f32"), "f32"), y, Wl._prog_swiglu(), "f32")
+    assert bytes(again.lazy[1]) == first
+    hit = be.zip_with(be.map(x, ops.cast("bf16", "f32"), "f32"), y, Wl._prog_swiglu(), "f32")
+    assert hit.lazy[1] is again.lazy[1]
+
+
+def test_captured_storages_are_released_by_their_graph(monkeypatch):
+    """A storage allocated while a step is captured frees itself only during that capture; after it
+    ends the graph owns the memory. Storages from outside a capture free normally."""
+    import ctypes as C
+    import itertools
+    from furiosa_opt_b200 import backend as Bk
+    addrs, freed = itertools.count(1), []
+
+    class FakeLib:
+        def _give(self, ctx, nbytes, out):
+            out._obj.value = next(addrs) << 16
+            return 0
+
+        fopt_alloc = fopt_alloc_uninit = _give
+
+        def fopt_free(self, ctx, p):
+            freed.append(p.value)
+            return 0
+
+    monkeypatch.setattr(Bk._lib, "lib", lambda: FakeLib())
+    be = Bk.B200.__new__(Bk.B200)
+    be.ctx, be._capturing = None, object()
+    inside, dies_inside = Bk.Storage(be, "f32", 16), Bk.Storage(be, "f32", 16)
+    a_inside = dies_inside._ptr.value
+    dies_inside.__del__()  # freed during the capture: a free node of the graph
+    assert freed == [a_inside]
+    be._capturing = None
+    inside.__del__()  # outlives the capture: the graph's to release
+    assert freed == [a_inside]
+    outside = Bk.Storage(be, "f32", 16)
+    a_outside = outside._ptr.value
+    outside.__del__()
+    assert freed == [a_inside, a_outside]
+    for s_ in (inside, dies_inside, outside):
+        s_._ptr = C.c_void_p()
