@@ -96,6 +96,7 @@ SIGNATURES = [
     ("fopt_reduce_map", _I32, [C.c_void_p, C.c_void_p, C.POINTER(Program), _I32, C.POINTER(C.c_void_p),
                                C.POINTER(C.c_int), C.POINTER(C.c_int64), C.c_int, C.c_int, C.c_uint32, C.c_void_p,
                                C.c_void_p]),
+    ("fopt_struct_sizes", _I32, [C.POINTER(_SZ), _I32]),
     ("fopt_capture_begin", _I32, [C.c_void_p]),
     ("fopt_capture_end", _I32, [C.c_void_p, C.POINTER(C.c_void_p)]),
     ("fopt_graph_launch", _I32, [C.c_void_p, C.c_void_p]),

@@ -578,6 +578,15 @@ static bool plain_row_reduce(fopt_ctx* ctx, const fopt_mapping* src_map, const f
   return true;
 }
 
+fopt_status fopt_struct_sizes(size_t* sizes, int32_t n) {
+  if (!sizes || n < 4) return FOPT_ERR_INVALID;
+  sizes[0] = sizeof(fopt_program);
+  sizes[1] = sizeof(fopt_epilogue);
+  sizes[2] = sizeof(fopt_row_slot);
+  sizes[3] = sizeof(fopt_row_plan);
+  return FOPT_OK;
+}
+
 fopt_status fopt_row_reduce_shape(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                                   int64_t* rows, int64_t* row_len) {
   bool ok = false;

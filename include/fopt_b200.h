@@ -232,6 +232,10 @@ fopt_status fopt_capture_end(fopt_ctx* ctx, fopt_graph** out);
 fopt_status fopt_graph_launch(fopt_ctx* ctx, fopt_graph* graph);
 fopt_status fopt_graph_destroy(fopt_ctx* ctx, fopt_graph* graph);
 
+/* Diagnostic for bindings: sizes[0..3] = sizeof fopt_program, fopt_epilogue, fopt_row_slot,
+ * fopt_row_plan (n >= 4), so a hand-written binding can check its struct layouts. */
+fopt_status fopt_struct_sizes(size_t* sizes, int32_t n);
+
 /* Whether reducing src_map into dst_map is a plain row reduction (dst cell t folds src cells
  * t W .. t W + W - 1): FOPT_OK with *rows and *row_len filled, FOPT_ERR_UNSUPPORTED otherwise.
  * Host-only: ctx may be NULL. */

@@ -517,3 +517,12 @@ def test_captured_storages_are_released_by_their_graph(monkeypatch):
     assert freed == [a_inside, a_outside]
     for s_ in (inside, dies_inside, outside):
         s_._ptr = C.c_void_p()
+
+
+def test_ctypes_structs_match_the_c_abi():
+    """The Python mirror's ctypes structs have the C ABI's sizes."""
+    import ctypes as C
+    sizes = (C.c_size_t * 4)()
+    assert _lib.lib().fopt_struct_sizes(sizes, 4) == 0
+    assert list(sizes) == [C.sizeof(_lib.Program), C.sizeof(_lib.Epilogue), C.sizeof(_lib.RowSlot),
+                           C.sizeof(_lib.RowPlan)]
