@@ -371,6 +371,12 @@ class B200:
 
     def set_exact_fold(self, exact: bool):
         check(_lib.lib().fopt_set_exact_fold(self.ctx, int(exact)), self.ctx)
+        self._exact_fold = bool(exact)
+
+    @property
+    def exact_fold(self) -> bool:
+        """Whether f32 folds run in the reference's wire order (off by default)."""
+        return getattr(self, "_exact_fold", False)
 
     @property
     def launches(self) -> int:

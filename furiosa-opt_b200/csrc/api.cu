@@ -534,8 +534,8 @@ fopt_status fopt_broadcast_kind(const fopt_mapping* src, const fopt_mapping* dst
 }
 
 // ---- reduce ----
-static std::shared_ptr<FoldKPlan> reduce_plan(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
-                                              int allow_broadcast) {
+static std::shared_ptr<FoldKPlan> reduce_plan_cached(fopt_ctx* ctx, const fopt_mapping* src_map,
+                                                     const fopt_mapping* dst_map, int allow_broadcast) {
   std::string key = "r|" + src_map->key + "|" + dst_map->key + "|" + std::to_string(allow_broadcast);
   if (ctx) {
     std::lock_guard<std::mutex> g(ctx->mu);
@@ -559,7 +559,7 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
   return guarded(ctx, [&] {
     require(out && src && src_map && dst_map, "fopt_reduce: null argument");
     require(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16, "fopt_reduce: dtype must be i32, f32 or bf16");
-    auto kp = reduce_plan(ctx, src_map, dst_map, allow_broadcast);
+    auto kp = reduce_plan_cached(ctx, src_map, dst_map, allow_broadcast);
     launch_reduce(ctx, *kp, out, src, dtype, op, identity_bits, src_map->m.size());
   });
 }
@@ -567,7 +567,7 @@ fopt_status fopt_reduce(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dt
 // A plain row reduction: dst cell t folds src cells t * W .. t * W + W - 1.
 static bool plain_row_reduce(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map, int64_t* rows,
                              int64_t* W) {
-  auto kp = reduce_plan(ctx, src_map, dst_map, 0);
+  auto kp = reduce_plan_cached(ctx, src_map, dst_map, 0);
   const KWalk &o = kp->out, &r = kp->residue;
   if (o.n != 1 || r.n != 1 || o.live[0] != o.extent[0] || r.live[0] != r.extent[0] || r.stride[0][0] != 1 ||
       o.stride[0][0] != r.extent[0] || kp->out_positions != o.extent[0] ||
@@ -901,4 +901,9 @@ extern "C" fopt_status fopt_equal(fopt_ctx* ctx, const void* a, const void* b, s
     cuda_check(cudaStreamSynchronize(ctx->stream), "equal sync");
     *equal = h == 0;
   });
+}
+
+std::shared_ptr<FoldKPlan> fopt::reduce_plan(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                             int allow_broadcast) {
+  return reduce_plan_cached(ctx, src_map, dst_map, allow_broadcast);
 }

@@ -31,6 +31,8 @@ struct RelayoutPlan {
   std::string desc;
 };
 
+std::vector<int64_t> host_deltas(const KWalk& rw);
+
 struct FoldKPlan {
   KWalk out{}, residue{};
   int64_t out_positions = 0, residue_positions = 0, residue_live = 0;
@@ -38,6 +40,17 @@ struct FoldKPlan {
   mutable int64_t* dev_deltas[2] = {nullptr, nullptr};
   mutable int64_t dev_count[2] = {0, 0};
   mutable std::mutex dev_mu;
+  // the live residue deltas of memory 0 in host memory, built once on first request
+  mutable std::vector<int64_t> host_delta;
+  mutable bool host_delta_ready = false;
+  const std::vector<int64_t>& host_residue_deltas() const {
+    std::lock_guard<std::mutex> g(dev_mu);
+    if (!host_delta_ready) {
+      host_delta = host_deltas(residue);
+      host_delta_ready = true;
+    }
+    return host_delta;
+  }
   FoldKPlan() = default;
   FoldKPlan(const FoldKPlan& o)
       : out(o.out), residue(o.residue), out_positions(o.out_positions), residue_positions(o.residue_positions),
@@ -147,7 +160,9 @@ void launch_elementwise(fopt_ctx* ctx, const fopt_program* prog, int n_in, const
                         void* out, fopt_dtype out_dt, int64_t n);
 void launch_reduce(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op, uint32_t ident,
                    int64_t src_elems);
-std::vector<int64_t> host_deltas(const KWalk& rw);
+// The cached reduce plan for a (src, dst) mapping pair (host memory only; nothing is uploaded).
+std::shared_ptr<FoldKPlan> reduce_plan(fopt_ctx* ctx, const fopt_mapping* src_map, const fopt_mapping* dst_map,
+                                       int allow_broadcast);
 void launch_reduce_cells(fopt_ctx* ctx, const FoldKPlan& p, void* out, const void* src, int dtype, int op,
                          uint32_t ident, int64_t src_elems, const int64_t* d_delta, int64_t nd);
 void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, int out_dt, const void* lhs,

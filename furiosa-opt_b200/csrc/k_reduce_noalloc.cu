@@ -18,8 +18,12 @@
 //     that device current); make that first call before any stream capture;
 //   * all calls share the one array, and each call overwrites the part it uses: two calls whose
 //     kernels can overlap on the GPU (different streams, no ordering between them) race on it;
-//   * the fold always runs per output cell in the reference's wire order, so every dtype matches
-//     fopt_reduce with exact fold on (and i32 results match fopt_reduce in either mode).
+//   * the fold always runs per output cell in the reference's wire order. i32 results match
+//     fopt_reduce in either mode, f32 / bf16 Add and Mul match it with exact fold on; for f32 Max / Min
+//     fopt_reduce may fold a long unit-stride row in another order, so the two can differ in the sign
+//     of a zero or in which NaN comes back;
+//   * it cannot be called while a capture is open: the delta upload reads a host vector that a
+//     captured copy would keep pointing at after the call returns.
 #include <mutex>
 
 #include "ctx.hpp"
@@ -54,13 +58,6 @@ int64_t* delta_array(fopt_ctx* ctx) {
   return g_dev_ptr[ctx->device];
 }
 
-std::vector<Mapping> unify2(const Mapping& a, const Mapping& b) {
-  auto table = std::make_shared<AxisTable>();
-  for (auto* m : {&a, &b})
-    for (size_t i = 0; i < m->axes->names.size(); ++i) table->intern(m->axes->names[i], m->axes->sizes[i]);
-  return {parse_mapping(a.to_string(), table), parse_mapping(b.to_string(), table)};
-}
-
 }  // namespace
 }  // namespace fopt
 
@@ -70,38 +67,22 @@ extern "C" fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void*
                                            fopt_reduce_op op, uint32_t identity_bits, const fopt_mapping* src_map,
                                            const fopt_mapping* dst_map, int allow_broadcast) {
   if (!ctx) return FOPT_ERR_INVALID;
-  try {
-    if (!out || !src || !src_map || !dst_map) throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: null argument"};
-    if (!(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16))
-      throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: dtype must be i32, f32 or bf16"};
-    auto u = unify2(src_map->m, dst_map->m);
-    FoldPlan fp;
-    if (!plan_reduce(u[0], u[1], allow_broadcast != 0, fp))
-      throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_reduce_noalloc: mappings are not affine-factorisable"};
-    if ((int)fp.out.wheels.size() > kKWheels || (int)fp.residue.wheels.size() > kKWheels)
-      throw Fail{FOPT_ERR_UNSUPPORTED, "fopt_reduce_noalloc: plan has too many wheels"};
-    FoldKPlan kp;
-    kp.out = to_kwalk(fp.out);
-    kp.residue = to_kwalk(fp.residue);
-    kp.out_positions = fp.out.positions();
-    kp.residue_positions = fp.residue.positions();
-    kp.residue_live = fp.residue.live_positions();
-    if (kp.residue_live > kNoAllocMaxDeltas)
-      throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: the reduce folds " + std::to_string(kp.residue_live) +
+  return guarded(ctx, [&] {
+    require(out && src && src_map && dst_map, "fopt_reduce_noalloc: null argument");
+    require(dtype == FOPT_I32 || dtype == FOPT_F32 || dtype == FOPT_BF16,
+            "fopt_reduce_noalloc: dtype must be i32, f32 or bf16");
+    // The delta upload below reads a host vector; a captured copy node would keep pointing at it.
+    require(!ctx->capture, "fopt_reduce_noalloc: cannot be called while a capture is open (call fopt_reduce)");
+    auto kp = reduce_plan(ctx, src_map, dst_map, allow_broadcast);  // host-side plan, cached per context
+    if (kp->residue_live > kNoAllocMaxDeltas)
+      throw Fail{FOPT_ERR_INVALID, "fopt_reduce_noalloc: the reduce folds " + std::to_string(kp->residue_live) +
                                        " cells per output, above the fixed maximum of " +
                                        std::to_string(kNoAllocMaxDeltas) + "; use fopt_reduce"};
-    std::vector<int64_t> d = host_deltas(kp.residue);
+    const std::vector<int64_t>& d = kp->host_residue_deltas();
     int64_t* dev = delta_array(ctx);
     if (!d.empty())
       cuda_check(cudaMemcpyAsync(dev, d.data(), sizeof(int64_t) * d.size(), cudaMemcpyHostToDevice, ctx->stream),
                  "reduce_noalloc: delta upload");
-    launch_reduce_cells(ctx, kp, out, src, dtype, op, identity_bits, src_map->m.size(), dev, (int64_t)d.size());
-    return FOPT_OK;
-  } catch (const Fail& f) {
-    ctx->err = f.msg;
-    return f.code;
-  } catch (const std::exception& e) {
-    ctx->err = e.what();
-    return FOPT_ERR_INVALID;
-  }
+    launch_reduce_cells(ctx, *kp, out, src, dtype, op, identity_bits, src_map->m.size(), dev, (int64_t)d.size());
+  });
 }
