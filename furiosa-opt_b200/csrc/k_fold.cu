@@ -12,6 +12,7 @@
 #include <algorithm>
 
 #include "ctx.hpp"
+#include "ew_ops.cuh"
 
 namespace fopt {
 namespace {
@@ -68,7 +69,7 @@ __global__ void reduce_cell_kernel(void* __restrict__ out, const void* __restric
     if (walk_offsets<1>(ow, o, &base)) {
       for (int64_t r = 0; r < nd; ++r) {
         int64_t p = base + delta[r];
-        if (p < src_elems) acc = combine(op, dt, acc, load_acc(src, dt, p));
+        if (p >= 0 && p < src_elems) acc = combine(op, dt, acc, load_acc(src, dt, p));
       }
     }
     store_word(out, dt, o, acc);
@@ -123,6 +124,8 @@ __device__ __forceinline__ bool is_int_in(int dt) {
 __device__ __forceinline__ float widen_f(const void* p, int dt, int64_t i) {
   uint32_t w = load_word(p, dt, i);
   if (dt == FOPT_BF16) return F(bf16w_to_f32_bits(w));
+  if (dt == FOPT_F8E4M3) return F(ew::f8e4_to_f32w(w));  // Cast<f32> for f8e4m3 (cast.rs:193-198)
+  if (dt == FOPT_F8E5M2) return F(ew::f8e5_to_f32w(w));  // Cast<f32> for f8e5m2 (cast.rs:207-212)
   return F(w);  // F32 prewidened
 }
 
@@ -169,6 +172,10 @@ __device__ __forceinline__ uint32_t contract_cell(const CArgs& a, int64_t bl, in
       } else {
         res = f32_to_bf16w(res);
       }
+    } else if (a.out_dt == FOPT_F8E4M3 || a.out_dt == FOPT_F8E5M2) {
+      // narrow once per cell through the f8 encoder (cast.rs:200-217), after the commit ReLU if any
+      if (a.ep_kind == 2 && (res & 0x7fffffffu) <= 0x7f800000u && (res >> 31)) res = 0u;
+      res = a.out_dt == FOPT_F8E4M3 ? ew::f32w_to_f8e4(res) : ew::f32w_to_f8e5(res);
     } else if (a.ep_kind == 2) {
       res = W(fmaxf(acc, 0.0f));
     }

@@ -133,10 +133,11 @@ typedef enum {
   FOPT_OP_F32_TO_I32 = 5,     /* `as i32` (truncate, saturate, NaN -> 0) */
   FOPT_OP_FXP_TO_FP = 6,      /* fixedpoint_to_float(a, imm_i = int_width) */
   FOPT_OP_FP_TO_FXP = 7,      /* float_to_fixedpoint(a, imm_i = int_width) */
-  FOPT_OP_F8E4M3_TO_F32 = 8, FOPT_OP_F32_TO_F8E4M3 = 9,
-  FOPT_OP_F8E5M2_TO_F32 = 10, FOPT_OP_F32_TO_F8E5M2 = 11,
+  FOPT_OP_F8E4M3_TO_F32 = 8, FOPT_OP_F32_TO_F8E4M3 = 9,   /* float/f8e4.rs:10-59 */
+  FOPT_OP_F8E5M2_TO_F32 = 10, FOPT_OP_F32_TO_F8E5M2 = 11, /* float/f8e5.rs:10-67 */
   FOPT_OP_I4_SEXT = 12,       /* sign-extend low 4 bits */
   FOPT_OP_I5_SEXT = 13, FOPT_OP_I9_SEXT = 14,
+  FOPT_OP_F4E2M1_TO_F8E4M3 = 15, /* fetch table lookup of an e2m1 nibble (scalar.rs:933-959, cast.rs:48-52) */
   /* Fp unary (semantics.rs:77-92) */
   FOPT_OP_EXP = 20, FOPT_OP_NEGEXP = 21, FOPT_OP_SQRT = 22, FOPT_OP_TANH = 23, FOPT_OP_SIGMOID = 24,
   FOPT_OP_LOG = 25, FOPT_OP_SIN = 26, FOPT_OP_COS = 27,
@@ -285,11 +286,13 @@ fopt_status fopt_row_program_source(const fopt_row_plan* plan, char* buf, size_t
 /* Allocation-free reduce. No counterpart in the reference: it exists for callers that cannot let the
  * library call cudaMalloc / cudaFree (a host runtime that owns the whole device-memory budget through
  * its own allocator, or a latency-critical loop that cannot absorb the device synchronisation a
- * cudaFree implies). Same arguments and results as fopt_reduce with exact fold; its residue table
- * lives in a fixed 256 KiB device array (at most 32768 folded cells per output, larger reduces are
- * rejected with FOPT_ERR_INVALID) that every GPU loading the library keeps until exit. The first call
- * on a device looks the array up; make it before any stream capture. All calls share the array:
- * calls whose kernels may overlap on the GPU race. */
+ * cudaFree implies). Same arguments as fopt_reduce; the fold always runs per output cell in wire
+ * order, so i32 results equal fopt_reduce's and f32 / bf16 Add / Mul equal fopt_reduce's with exact
+ * fold on (f32 Max / Min may differ from fopt_reduce in the sign of a zero or which NaN is kept). Its
+ * residue table lives in a fixed 256 KiB device array (at most 32768 folded cells per output, larger
+ * reduces are rejected with FOPT_ERR_INVALID) that every GPU loading the library keeps until exit.
+ * The first call on a device looks the array up. A call while a capture is open is refused with
+ * FOPT_ERR_INVALID. All calls share the array: calls whose kernels may overlap on the GPU race. */
 fopt_status fopt_reduce_noalloc(fopt_ctx* ctx, void* out, const void* src, fopt_dtype dtype, fopt_reduce_op op,
                                 uint32_t identity_bits, const fopt_mapping* src_map, const fopt_mapping* dst_map,
                                 int allow_broadcast);

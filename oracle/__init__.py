@@ -56,6 +56,18 @@ def lib():
     return _lib
 
 
+F8_OPS = {"f8e4m3_to_f32": 8, "f32_to_f8e4m3": 9, "f8e5m2_to_f32": 10, "f32_to_f8e5m2": 11, "f4e2m1_to_f8e4m3": 15}
+
+
+def f8_convert(kind: str, words) -> np.ndarray:
+    """One of the f8 conversions (float/f8e4.rs, float/f8e5.rs) or the f4e2m1 -> f8e4m3 lookup
+    (scalar.rs:933-959) over an array of 32-bit words (f32 bit patterns or codes); returns uint32."""
+    a = np.ascontiguousarray(np.asarray(words).astype(np.uint32))
+    out = np.empty_like(a)
+    lib().ref_f8_map(F8_OPS[kind], _p(a), _p(out), C.c_int64(a.size))
+    return out
+
+
 def _p(a: np.ndarray):
     return a.ctypes.data_as(C.c_void_p)
 

@@ -83,6 +83,96 @@ static uint32_t f32_to_bf16(uint32_t x) {
   if (e == 0 && m) return x & 0x80000000u;
   return bf16_from_f32_plain(x);
 }
+/* f8e4m3 -> f32 (float/f8e4.rs:10-12 through the 256-entry table at :67-101). The table is the OCP
+ * E4M3 value set: bias 7, 3 mantissa bits, subnormals m * 2^-9, no infinities; both NaN codes
+ * (0x7f, 0xff) decode to the positive quiet NaN 0x7fc00000. Built here from that definition; the
+ * CPU tests compare it entry by entry with the reference's table (tests/golden/f8e4m3_table.json). */
+uint32_t ref_f8e4_to_f32(uint32_t code) {
+  uint32_t s = (code & 0x80u) << 24, e = (code >> 3) & 15u, m = code & 7u;
+  if (e == 15u && m == 7u) return 0x7fc00000u;
+  if (e == 0u) return s | f2u((float)m * 0.001953125f);
+  return s | ((e + 120u) << 23) | (m << 20);
+}
+/* f8_e4_from_f32 (float/f8e4.rs:14-59), step for step: NaN -> 0x7f; the normal range rounds the top
+ * 11 bits (exponent + 3 mantissa bits) to nearest even and saturates at 0x7e (448); exponents
+ * 120..117 are the subnormal codes by explicit thresholds; anything smaller is a signed zero. */
+uint32_t ref_f32_to_f8e4(uint32_t n) {
+  if ((n & 0x7fffffffu) > 0x7f800000u) return 0x7f;
+  uint32_t exp = (n >> 23) & 0xff, man = n & 0x7fffff, absv;
+  if (exp > 127 - 7) {
+    uint32_t valid = (n >> 20) & 0x7ff;
+    uint32_t val = ((n & 0xfffff) + (valid & 1) > 0x80000) ? valid + 1 : valid;
+    absv = val >= ((((127u + 8u) << 3)) | 0x6u) ? 0x7eu : val - ((127u - 7u) << 3);
+  } else if (exp == 127 - 7) {
+    absv = man >= 0x700000 ? 8 : man > 0x500000 ? 7 : man >= 0x300000 ? 6 : man > 0x100000 ? 5 : 4;
+  } else if (exp == 127 - 8) {
+    absv = man >= 0x600000 ? 4 : man > 0x200000 ? 3 : 2;
+  } else if (exp == 127 - 9) {
+    absv = man >= 0x400000 ? 2 : 1;
+  } else if (exp == 127 - 10 && man != 0) {
+    absv = 1;
+  } else {
+    absv = 0;
+  }
+  return (((n >> 31) << 7) | absv) & 0xff;
+}
+/* f8_e5_to_f32 (float/f8e5.rs:10-28): subnormal m * 2^-16, exponent 31 is +-inf / +-NaN (the sign
+ * is kept on NaN too: -NaN is 0xffc00000), else rebias 15 -> 127. */
+uint32_t ref_f8e5_to_f32(uint32_t code) {
+  uint32_t sign = (code >> 7) & 1, exp = (code >> 2) & 0x1f, mant = code & 3;
+  if (exp == 0) {
+    float m = (float)mant / 65536.0f;
+    return f2u(sign ? -m : m);
+  }
+  if (exp == 0x1f) return (sign << 31) | (mant ? 0x7fc00000u : 0x7f800000u);
+  return (sign << 31) | ((exp + 127 - 15) << 23) | (mant << 21);
+}
+/* f8_e5_from_f32 (float/f8e5.rs:30-67), step for step: NaN -> 0x7e; inf and overflow -> +-0x7c;
+ * subnormals round |v| * 2^16 half away from zero and clamp to 3; normals keep 2 mantissa bits and
+ * round half up, carrying into the exponent (and into infinity). */
+uint32_t ref_f32_to_f8e5(uint32_t n) {
+  float v = u2f(n);
+  if (isnan(v)) return 0x7e;
+  uint32_t sign = (n >> 31) ? 0x80u : 0u;
+  float a = fabsf(v);
+  if (isinf(a)) return sign | 0x7c;
+  if (a == 0.0f) return sign;
+  uint32_t an = f2u(a);
+  int32_t unbiased = (int32_t)((an >> 23) & 0xff) - 127;
+  uint32_t man = an & 0x7fffff;
+  int32_t biased = unbiased + 15;
+  if (biased >= 0x1f) return sign | 0x7c;
+  if (biased <= 0) {
+    uint32_t sub = (uint32_t)roundf(a * 65536.0f);
+    return sign | (sub < 3 ? sub : 3);
+  }
+  uint32_t mant2 = man >> 21, e = (uint32_t)biased;
+  if ((man >> 20) & 1) {
+    mant2 += 1;
+    if (mant2 == 4) {
+      mant2 = 0;
+      e += 1;
+      if (e >= 0x1f) return sign | 0x7c;
+    }
+  }
+  return sign | (e << 2) | mant2;
+}
+/* f4e2m1 -> f8e4m3 table lookup (scalar.rs:933-959, cast.rs:48-52): the e2m1 value set {0, 0.5, 1,
+ * 1.5, 2, 3, 4, 6} with sign, encoded as E4M3 (exact: every e2m1 value is an E4M3 value). */
+uint32_t ref_f4e2_to_f8e4(uint32_t nib) {
+  uint32_t s = (nib >> 3) & 1, e = (nib >> 1) & 3, m = nib & 1;
+  float v = e == 0 ? 0.5f * (float)m : (1.0f + 0.5f * (float)m) * (float)(1u << (e - 1));
+  return ref_f32_to_f8e4(f2u(s ? -v : v));
+}
+/* Array form of the four f8 conversions and the f4 lookup, for the tests: which = opcode 8..11, 15. */
+void ref_f8_map(int which, const uint32_t* in, uint32_t* out, int64_t n) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < n; ++i) {
+    uint32_t a = in[i];
+    out[i] = which == 8 ? ref_f8e4_to_f32(a & 0xff) : which == 9 ? ref_f32_to_f8e4(a)
+           : which == 10 ? ref_f8e5_to_f32(a & 0xff) : which == 11 ? ref_f32_to_f8e5(a) : ref_f4e2_to_f8e4(a & 15);
+  }
+}
 /* round_to_nearest_even (float/mod.rs:141-159) */
 static uint32_t rtne(uint32_t input, uint32_t iw, uint32_t ow) {
   uint32_t valid = input & ((1u << iw) - 1);
@@ -167,9 +257,13 @@ void ref_reduce(void* out, const void* src, int dt, int op, uint32_t ident, cons
 
 /* ---- contraction ---- */
 static int is_int(int dt) { return dt == I8 || dt == I4 || dt == I5 || dt == I9 || dt == I16 || dt == I32; }
+/* Cast::cast to the accumulator (cast.rs:193-217): bf16 via bf16_to_f32, f8 via its decode. */
 static float widen_f(const void* p, int dt, int64_t i) {
   uint32_t w = ld(p, dt, i);
-  return dt == BF16 ? u2f(bf16_to_f32(w)) : u2f(w);
+  if (dt == BF16) return u2f(bf16_to_f32(w));
+  if (dt == F8E4M3) return u2f(ref_f8e4_to_f32(w));
+  if (dt == F8E5M2) return u2f(ref_f8e5_to_f32(w));
+  return u2f(w);
 }
 
 /* ep_kind: 0 none, 1 requant (FxpToFp -> MulF scale[sidx] -> FpToFxp -> Clip), 2 relu,
@@ -220,6 +314,10 @@ void ref_contract(void* out, int out_dt, const void* lhs, const void* rhs, int i
         if (out_dt == BF16) {
           if (ep_kind == 2 && !isnan(acc) && (res >> 31)) res = 0;
           else res = f32_to_bf16(res);
+        } else if (out_dt == F8E4M3 || out_dt == F8E5M2) {
+          /* the narrow Cast f32 -> f8 (cast.rs:200-217), after the commit ReLU when there is one */
+          if (ep_kind == 2 && !isnan(acc) && (res >> 31)) res = 0;
+          res = out_dt == F8E4M3 ? ref_f32_to_f8e4(res) : ref_f32_to_f8e5(res);
         } else if (ep_kind == 2) {
           res = f2u(fmaxf(acc, 0.0f));
         }
@@ -242,9 +340,14 @@ static uint32_t op1(int op, uint32_t a, uint32_t b, uint32_t c, int32_t imm) {
     case 5: return isnan(fa) ? 0u : fa >= 2147483648.0f ? (uint32_t)INT32_MAX : fa <= -2147483904.0f ? (uint32_t)INT32_MIN : (uint32_t)(int32_t)fa;
     case 6: return ref_fxp_to_fp(ia, (uint32_t)imm);
     case 7: return (uint32_t)ref_fp_to_fxp(a, (uint32_t)imm);
+    case 8: return ref_f8e4_to_f32(a & 0xff);
+    case 9: return ref_f32_to_f8e4(a);
+    case 10: return ref_f8e5_to_f32(a & 0xff);
+    case 11: return ref_f32_to_f8e5(a);
     case 12: return (uint32_t)((int32_t)(a << 28) >> 28);
     case 13: return (uint32_t)((int32_t)(a << 27) >> 27);
     case 14: return (uint32_t)((int32_t)(a << 23) >> 23);
+    case 15: return ref_f4e2_to_f8e4(a & 15);
     case 20: return f2u(expf(fa));
     case 21: return f2u(expf(-fa));
     case 22: return f2u(sqrtf(fa));

@@ -295,11 +295,9 @@ def test_safetensors_header_and_flat_shape(tmp_path):
         fb.SafeTensors(str(bad))
 
 
-@pytest.mark.skipif(not os.path.exists("/root/reference/furiosa-opt-examples/data/mnist/mnist.safetensors"),
-                    reason="reference tree not present")
 def test_safetensors_reads_reference_mnist_header():
     """The reference example's own weights file parses, with the shapes its test loads them as."""
-    with fb.SafeTensors("/root/reference/furiosa-opt-examples/data/mnist/mnist.safetensors") as st:
+    with fb.SafeTensors(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mnist.safetensors")) as st:
         info = {st.info(k)[0]: st.info(k)[1:3] for k in range(len(st))}
     assert info["hw.fc1.weight"] == ("BF16", [256, 800])
     assert info["hw.fc2.weight"] == ("BF16", [16, 256])
