@@ -1,7 +1,13 @@
 """Benchmark: the furiosa-opt emulator hot path on B200.
 
 Default (headline) workload: config 2, the standalone int8 contraction M=N=K=4096 (i32 accumulate,
-per-channel fp32 requant to i8), one step = one `contraction` call through the backend.
+per-channel fp32 requant to i8), one step = one `contraction` call through the backend. The default
+run also measures the other configs, each as a sub-object of the one JSON line (`configs`): at one
+GPU the bf16 GEMM, config 3 attention, config 4 decoder block, config 1 MNIST MLP and the layout
+move, each with its roofline and its CPU-port baseline; at N > 1 GPUs config 5's all-reduce (bus
+bandwidth at 128 MiB plus a 1 KiB - 1 GiB sweep, against the peer-to-peer bandwidth measured in the
+same run) and a bit-exact self-check of the all-reduce and the chip shuffle. `--headline-only`
+skips them.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm_i8|gemm_bf16|attention|
                   relayout|allreduce|mnist|decoder|decoder_tp] [--impl ours|reference]
 Multi-GPU (torchrun, one rank per GPU): independent replicas of the step ("replicas only": the
@@ -168,25 +174,49 @@ def wl_gemm(fb, be, dtype: str, M=4096, N=4096, K=4096):
                 e2e_api="B200.contraction_host -> fopt_contraction_host (pinned host buffers, row-chunk pipeline)",
                 algo_bytes=None, workload=f"gemm_{dtype}_{M}x{N}x{K}", dtype=dtype,
                 extra={"out_dtype": out_dt, "epilogue": "per-channel requant" if dtype == "i8" else "bf16 narrow"},
-                cpu=lambda rows: cpu_gemm(a, b, scale, dtype, M, N, K, rows),
+                cpu=lambda rows, keep=None: cpu_gemm(a, b, scale, dtype, M, N, K, rows, keep),
+                parity=lambda rows, cpu_bytes: gemm_parity(OUT, cpu_bytes, dtype, rows, N),
                 config={"M": M, "N": N, "K": K, "layout": "lhs [M, K], rhs [N, K], out [M, N]",
                         "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
-def cpu_gemm(a, b, scale, dtype, M, N, K, rows):
+def cpu_gemm(a, b, scale, dtype, M, N, K, rows, keep=None):
+    """The oracle port's per-cell fold over the first `rows` output rows at full K (only the fold is
+    timed: the read plans stand for the reference's sequence() setup). `keep` (a dict) receives the
+    sample's output bytes, which the GPU result is compared with."""
     import oracle
     from oracle import ref_m
 
     ax = dict(M=M, N=N, K=K)
     rl, rr, rp, ro = (ref_m(e, **ax) for e in ("[M, K]", "[N, K]", "[M, N, K]", "[M, N]"))
-    # only the per-cell fold is timed (the read plans correspond to the reference's sequence() setup)
     if dtype == "i8":
-        oracle.contract(a.tobytes(), b.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
-                        scale_axis="N", out_cells=rows * N)
+        out = oracle.contract(a.tobytes(), b.tobytes(), "i8", "i8", rl, rr, rp, ro, ep_kind=1, scale=scale,
+                              scale_axis="N", out_cells=rows * N)
     else:
-        oracle.contract(a.tobytes(), b.tobytes(), "bf16", "bf16", rl, rr, rp, ro, out_cells=rows * N)
+        out = oracle.contract(a.tobytes(), b.tobytes(), "bf16", "bf16", rl, rr, rp, ro, out_cells=rows * N)
     dt = oracle.last_fold_seconds
+    if keep is not None:
+        keep["bytes"] = out
     return 2.0 * rows * N * K / dt, f"{rows} of {M} output rows ({rows * N} cells, full K={K})"
+
+
+def gemm_parity(out_storage, cpu_bytes, dtype, rows, N):
+    """The GPU's first `rows` output rows against the CPU port's bytes for the same rows."""
+    esz = 1 if dtype == "i8" else 2
+    got = out_storage.to_bytes()[: rows * N * esz]
+    if dtype == "i8":
+        same = got == cpu_bytes
+        return {"check": f"first {rows} of the output rows against the CPU port", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+    import numpy as np_
+
+    g = (np_.frombuffer(got, np_.uint16).astype(np_.uint32) << 16).view(np_.float32)
+    w = (np_.frombuffer(cpu_bytes, np_.uint16).astype(np_.uint32) << 16).view(np_.float32)
+    err = np_.abs(g - w)
+    ok = bool(np_.all(err <= 2 ** -7 * np_.abs(w) + 1e-3 * np_.abs(w).max()))
+    return {"check": f"first {rows} output rows against the CPU port (tensor-core sum order)",
+            "max_abs_err": float(err.max()), "max_abs_out": float(np_.abs(w).max()),
+            "result": "within 1 bf16 ulp + 1e-3 max|out|" if ok else "OUT OF TOLERANCE"}
 
 
 def wl_attention(fb, be, S=2048, Hq=32, Hkv=8, D=128):
@@ -203,7 +233,18 @@ def wl_attention(fb, be, S=2048, Hq=32, Hkv=8, D=128):
         return be.attention(Q, Kt, V, 1, S, Hq, Hkv, D, causal=True, out=OUT)
 
     flops = 4.0 * S * S * D * Hq / 2  # causal half
-    return dict(step=step, units=S, unit="tokens/s", scale=1.0, flops=flops, bound="tensor",
+
+    def cpu(_rows=None, keep=None):
+        import oracle
+
+        q1 = q.reshape(S, Hq, D)[:, 0].copy()
+        k1, v1 = k.reshape(S, Hkv, D)[:, 0].copy(), v.reshape(S, Hkv, D)[:, 0].copy()
+        t0 = time.perf_counter()
+        oracle.attention_chain(q1, k1, v1, 1, S, 1, 1, D, True)
+        dt = time.perf_counter() - t0
+        return S / (dt * Hq), f"the reference's attention op chain for 1 of {Hq} query heads (S={S}, causal)"
+
+    return dict(step=step, units=S, unit="tokens/s", scale=1.0, flops=flops, bound="tensor", cpu=cpu,
                 metric="attention prefill tokens/s (Llama-3-8B shape, S=2048, causal)", workload="attention_s2048",
                 dtype="bf16", config={"S": S, "Hq": Hq, "Hkv": Hkv, "D": D, "causal": True})
 
@@ -220,14 +261,32 @@ def wl_relayout(fb, be, R=8192, C=8192):
         be.transpose(Y, X, S, D)
         return Y
 
-    return dict(step=step, units=2.0 * R * C * 2, unit="GB/s", scale=1e9, bound="hbm",
+    def cpu(_rows=None, keep=None):
+        # the oracle's BufStorage::transpose copy loop (OpenMP over destination positions) on a
+        # 2048 x 2048 corner of the same layout; only the copy loop is timed
+        import oracle
+        from oracle import ref_m
+
+        r = c = 2048
+        xs = x.reshape(R, C)[:r, :c].copy()
+        oracle.transpose(bytes(r * c * 2), xs.tobytes(), "bf16", ref_m("[R, C]", R=r, C=c), ref_m("[C, R]", R=r, C=c))
+        dt = oracle.last_transpose_seconds
+        return 2.0 * r * c * 2 / dt, f"the port's transpose loop on a {r} x {c} bf16 tile of the same layout"
+
+    def parity(_rows=None, _b=None):
+        y = np.frombuffer(Y.to_bytes(), np.uint16).reshape(C, R)
+        same = bool(np.array_equal(y, x.reshape(R, C).T))
+        return {"check": "whole output against numpy's transpose", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    return dict(step=step, units=2.0 * R * C * 2, unit="GB/s", scale=1e9, bound="hbm", cpu=cpu, parity=parity,
                 metric="relayout GB/s ([R, C] -> [C, R] bf16, 128 MiB)", workload="relayout_bf16_8192x8192",
                 dtype="bf16", config={"R": R, "C": C})
 
 
-def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096):
+def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096, comm_ready=False):
     """Config 5: all-reduce of an 8x2048x4096 bf16 activation (N(0,1) per rank) over the Chip axis."""
-    if world > 1:
+    if world > 1 and not comm_ready:
         fb.dist.init_comm(be, rank, world)
     rng = np.random.default_rng(100 + rank)
     m = fb.Mapping("[E]", dict(E=count))
@@ -286,7 +345,34 @@ def wl_mnist(fb, be, B=64, I=784, H=128, O=10):
     fwd = lambda: fb.workloads.mnist_int8_forward(be, X, W1, W2, S1, B, I, H, O)  # noqa: E731
     out_bytes = fwd().nbytes
     step, e2e_step, hx, hout = graphed_step(fb, be, fwd, X, out_bytes)
-    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(),
+
+    def cpu(_rows=None, keep=None):
+        # the port's two per-cell folds with the requant epilogue (the same restatement the parity
+        # test pins); only the folds are timed
+        import oracle
+        from oracle import ref_m
+
+        mm = lambda e: ref_m(e, **ax)  # noqa: E731
+        oracle.contract(x.tobytes(), w1.tobytes(), "i8", "i8", mm("[B, I]"), mm("[H, I]"), mm("[B, H, I]"),
+                        mm("[B, H]"), ep_kind=1, scale=s1, scale_axis="H", clip_lo=0, clip_hi=127)
+        t = oracle.last_fold_seconds
+        h = oracle.contract(x.tobytes(), w1.tobytes(), "i8", "i8", mm("[B, I]"), mm("[H, I]"), mm("[B, H, I]"),
+                            mm("[B, H]"), ep_kind=1, scale=s1, scale_axis="H", clip_lo=0, clip_hi=127)
+        t = min(t, oracle.last_fold_seconds)
+        logits = oracle.contract(h, w2.tobytes(), "i8", "i32", mm("[B, H]"), mm("[O, H]"), mm("[B, O, H]"),
+                                 mm("[B, O]"))
+        t += oracle.last_fold_seconds
+        if keep is not None:
+            keep["bytes"] = logits
+        return B / t, f"the whole forward ({B} images), both folds"
+
+    def parity(_rows=None, cpu_bytes=None):
+        got = step().to_bytes()
+        same = got == cpu_bytes
+        return {"check": "logits of the whole batch against the CPU port", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(), cpu=cpu, parity=parity,
                 e2e_api="fopt_h2d -> captured forward (fopt_graph_launch) -> fopt_d2h (pinned host buffers)",
                 units=B, unit="images/s", scale=1.0, bound="latency", flops=2.0 * B * (I * H + H * O),
                 metric="MNIST-shaped int8 MLP forward, images/s (64x784 -> 128 -> 10)", workload="mnist_int8_mlp",
@@ -334,7 +420,27 @@ def wl_decoder(fb, be, batch=8, seq=512, Hq=32, Hkv=8, F=14336):
                     "bf16")
 
     step, e2e_step, hx, hout = graphed_step(fb, be, lambda: blk.forward(X), X, T * H * 2)
-    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(),
+
+    def cpu(_rows=None, keep=None):
+        # the port's per-cell int8 fold (the block's projections are 99.8 % of its operations) on a
+        # 16-token x 1024-channel x K=4096 piece of the gate projection, scaled to the block's
+        # projection operations per token
+        import oracle
+        from oracle import ref_m
+
+        t, n, k = 16, 1024, H
+        ax = dict(T=t, N=n, K=k)
+        mm = lambda e: ref_m(e, **ax)  # noqa: E731
+        wg = blk.host["wg"][0][:n]
+        xq = np.random.default_rng(2).integers(-127, 128, t * k).astype(np.int8)
+        oracle.contract(xq.tobytes(), wg.tobytes(), "i8", "i32", mm("[T, K]"), mm("[N, K]"), mm("[T, N, K]"),
+                        mm("[T, N]"))
+        rate = 2.0 * t * n * k / oracle.last_fold_seconds
+        per_token = blk.gemm_ops() / T
+        return rate / per_token, (f"per-cell int8 fold of a {t} x {n} x {k} projection piece, scaled by the "
+                                  f"block's {per_token / 1e6:.0f} M projection ops per token")
+
+    return dict(step=step, e2e_step=e2e_step, h2d=hx.numel(), d2h=hout.numel(), cpu=cpu,
                 e2e_api="fopt_h2d -> captured block (fopt_graph_launch) -> fopt_d2h (pinned host buffers)",
                 units=T, unit="tokens/s", scale=1.0, bound="tensor", dtype="i8",
                 flops=blk.gemm_ops() + blk.attention_flops(),
@@ -395,6 +501,204 @@ def bind_to_gpu_cpus(local: int) -> str:
         return f"unbound ({type(e).__name__})"
 
 
+def measure(be, wl, stream, flush, steps, warmup, world, local):
+    """W untimed warm-up steps, then exactly `steps` steps, each bracketed by CUDA events on the
+    library's stream with L2 flushed before it (outside the events), clocks sampled throughout; the
+    end-to-end step (host buffers in and out) is timed the same way afterwards. Returns the mean
+    device times, max over ranks."""
+    import torch
+
+    clk = Clocks(local).__enter__()  # sampling runs from before warm-up to the end of the timed steps
+    clk.wait_first_sample()
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            wl["step"]()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        launches0 = be.launches
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        torch.cuda.synchronize()
+        wall0 = time.perf_counter()
+        for i in range(steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            wl["step"]()
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        clk.__exit__()
+        launches = be.launches - launches0
+        durs = [a.elapsed_time(b) for a, b in ev]
+        e2e = 0.0
+        if "e2e_step" in wl:
+            torch.cuda.synchronize()
+            e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                    for _ in range(steps)]
+            for i in range(steps):
+                flush.zero_()
+                e_ev[i][0].record(stream)
+                wl["e2e_step"]()
+                e_ev[i][1].record(stream)
+            torch.cuda.synchronize()
+            e2e = statistics.mean(a.elapsed_time(b) for a, b in e_ev)
+    t = torch.tensor([statistics.mean(durs), e2e], device="cuda", dtype=torch.float64)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return {"ms": float(t[0]), "e2e_ms": float(t[1]), "launches": launches, "clocks": clk.summary(), "wall": wall}
+
+
+def int8_library_peak(stream, n=8192, reps=10):
+    """cuBLASLt's int8 GEMM (torch._int_mm, i32 out) at n^3 on this GPU, best of `reps`: the measured
+    int8 reference the headline GEMM is also reported against."""
+    import torch
+
+    try:
+        with torch.cuda.stream(stream):
+            a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda")
+            b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda").t()  # column-major K x N
+            for _ in range(3):
+                torch._int_mm(a, b)
+            best = None
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                torch._int_mm(a, b)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                ms = e0.elapsed_time(e1)
+                best = ms if best is None else min(best, ms)
+        del a, b
+        return {"tops": round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1), "how": f"torch._int_mm (cuBLASLt) {n}^3, "
+                f"best of {reps}, CUDA events"}
+    except Exception as e:  # an int8 GEMM the library refuses on this build: reported, not fatal
+        return {"tops": None, "how": f"torch._int_mm unavailable ({type(e).__name__})"}
+
+
+def roofline(wl, ms, pk, int8_peak=None):
+    if wl["bound"] == "latency":
+        achieved = wl["flops"] / (ms * 1e-3) / 1e12
+        return {"bound": "latency", "achieved": round(achieved, 4), "peak": None, "unit": "TOPS", "frac": None,
+                "traffic": None, "peak_src": "launch/latency bound (13 M int-ops per forward)"}
+    if wl["bound"] == "nvlink":
+        achieved = wl["units"] / (ms * 1e-3) / 1e9
+        peak = wl.get("link_peak")
+        return {"bound": "nvlink", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 3) if peak else None, "traffic": None,
+                "peak_src": wl.get("link_peak_src", "unmeasured")}
+    if wl["bound"] == "hbm":
+        achieved = wl["units"] / (ms * 1e-3) / 1e9
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None, "peak_src": pk["src"] + " copy"}
+    flops = wl.get("flops", wl["units"])
+    achieved = flops / (ms * 1e-3) / 1e12
+    if wl.get("dtype") == "i8":
+        peak, src = 2 * pk["bf16_tflops"], f"2x {pk['src']} bf16 cuBLAS burst (dense int8 rate = 2x bf16)"
+    else:
+        peak, src = pk["bf16_tflops"], f"{pk['src']} bf16 cuBLAS burst"
+    roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 3), "traffic": None, "peak_src": src}
+    if wl.get("dtype") == "i8" and int8_peak and int8_peak.get("tops"):
+        roof["int8_library_peak"] = int8_peak["tops"]
+        roof["frac_of_int8_library"] = round(achieved / int8_peak["tops"], 3)
+        roof["int8_library_how"] = int8_peak["how"]
+    return roof
+
+
+def report(wl, meas, world, pk, args, int8_peak=None, cpu=True):
+    """The JSON object for one workload: value, roofline, clocks, e2e, CPU baseline, parity."""
+    ms, e2e_ms = meas["ms"], meas["e2e_ms"]
+    agg = world if wl.get("aggregate", True) else 1
+    roof = roofline(wl, ms, pk, int8_peak)
+    tr = TRAFFIC.get(wl["workload"])
+    if tr:
+        roof["traffic"], roof["traffic_unit"], roof["traffic_src"] = tr[0], "bytes per launch (ncu)", tr[1]
+    out = {"metric": wl["metric"], "value": round(agg * wl["units"] / (ms * 1e-3) / wl["scale"], 2),
+           "unit": wl["unit"], "ms_per_step": round(ms, 4), "dtype": wl["dtype"],
+           "config": {"workload": wl["workload"], **wl["config"]}, "roofline": roof,
+           "gpu_launches": meas["launches"], "clocks": meas["clocks"], "wall_s": round(meas["wall"], 4)}
+    if e2e_ms:
+        out["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
+                      "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
+                      "ms_per_step": round(e2e_ms, 4), "api": wl.get("e2e_api", "")}
+    if "cpu" in wl and world == 1 and cpu and not args.no_cpu:
+        keep = {}
+        rate, sample = wl["cpu"](args.cpu_rows, keep)
+        out["cpu_baseline"] = {"value": round(rate / wl["scale"], 6), "unit": wl["unit"], "cores": os.cpu_count(),
+                               "kind": "port", "sample": sample}
+        if "parity" in wl and ("bytes" in keep or wl["workload"].startswith("relayout")):
+            out["parity"] = wl["parity"](args.cpu_rows, keep.get("bytes"))
+    return out
+
+
+def collective_report(fb, be, rank, world, stream, flush, args, local):
+    """Config 5 at N GPUs: the all-reduce of an 8 x 2048 x 4096 bf16 activation (bus bandwidth),
+    the 1 KiB - 1 GiB sweep, the peer-to-peer bandwidth each GPU reaches to its neighbour in the same
+    run (the NVLink roofline's denominator), and a bit-exact self-check of the all-reduce and the
+    chip shuffle (`pattern[target] = source`, memory.rs:657-679)."""
+    import torch
+    import torch.distributed as dist
+
+    fb.dist.init_comm(be, rank, world)
+    # peer-to-peer: every rank sends 1 GiB to rank+1 while receiving from rank-1 (NCCL send/recv)
+    n = 1 << 29
+    sbuf = torch.empty(n, dtype=torch.bfloat16, device="cuda").normal_()
+    rbuf = torch.empty_like(sbuf)
+
+    def ring():
+        ops_ = [dist.P2POp(dist.isend, sbuf, (rank + 1) % world), dist.P2POp(dist.irecv, rbuf, (rank - 1) % world)]
+        for r in dist.batch_isend_irecv(ops_):
+            r.wait()
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            ring()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(5):
+            ring()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / 5], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    p2p = 2 * n / (float(t[0]) * 1e-3) / 1e9
+    del sbuf, rbuf
+    # bit-exact self-check: small integers sum exactly in bf16; the shuffle moves whole slabs
+    cnt = 1 << 20
+    m = fb.Mapping("[E]", dict(E=cnt))
+    vals = [((np.arange(cnt) * (r + 3)) % 17 - 8).astype(np.float32) for r in range(world)]
+    x = be.from_vec(m, fb.dtypes.f32_to_bf16_bits(vals[rank]), "bf16")
+    fb.dist.allreduce(be, x)
+    ar_ok = bool(np.array_equal(fb.dtypes.bf16_bits_to_f32(x.to_numpy()), np.sum(vals, axis=0)))
+    pattern = [(tt + 1) % world for tt in range(world)]
+    src = be.from_vec(m, fb.dtypes.f32_to_bf16_bits(vals[rank]), "bf16")
+    dst = be.zeroed(m, "bf16")
+    fb.dist.chip_shuffle(be, dst, src, pattern)
+    sh_ok = bool(np.array_equal(dst.to_numpy(), fb.dtypes.f32_to_bf16_bits(vals[pattern[rank]])))
+    ok = torch.tensor([int(ar_ok and sh_ok)], device="cuda")
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    # the config-5 all-reduce, timed like every other step
+    wl = wl_allreduce(fb, be, rank, world, comm_ready=True)
+    wl["link_peak"], wl["link_peak_src"] = round(p2p, 1), ("peer-to-peer NCCL send/recv to the neighbouring rank, "
+                                                           "1 GiB, measured in this run (per direction)")
+    meas = measure(be, wl, stream, flush, args.steps, args.warmup, world, local)
+    sweep = allreduce_sweep(fb, be, world, stream)
+    if rank != 0:
+        return None
+    rep = report(wl, meas, world, peaks(), args, cpu=False)
+    rep["self_check"] = {"allreduce_bit_exact": ar_ok, "chip_shuffle_bit_exact": sh_ok,
+                         "all_ranks_ok": bool(int(ok[0]))}
+    rep["sweep"] = sweep
+    rep["peer_to_peer_gbs"] = round(p2p, 1)
+    rep["nccl_ranks"] = world
+    return rep
+
+
+SUB_CONFIGS = ("gemm_bf16", "attention", "decoder", "mnist", "relayout")
+
+
 def run_ours(args, rank, world, local):
     import torch
 
@@ -404,107 +708,58 @@ def run_ours(args, rank, world, local):
     be = fb.B200(local)
     stream = torch.cuda.Stream()
     fb._lib.lib().fopt_set_stream(be.ctx, stream.cuda_stream)
-    wl = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
-          "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
-          "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
-          "decoder": lambda: wl_decoder(fb, be),
-          "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}[args.workload]()
+    make = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
+            "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
+            "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
+            "decoder": lambda: wl_decoder(fb, be),
+            "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}
+    wl = make[args.workload]()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
-    clk = Clocks(local).__enter__()  # sampling runs from before warm-up to the end of the timed steps
-    clk.wait_first_sample()
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            wl["step"]()
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
-        launches0 = be.launches
-        durs = []
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-        if True:
-            torch.cuda.synchronize()
-            wall0 = time.perf_counter()
-            for i in range(args.steps):
-                flush.zero_()
-                ev[i][0].record(stream)
-                wl["step"]()
-                ev[i][1].record(stream)
-            torch.cuda.synchronize()
-            wall = time.perf_counter() - wall0
-        clk.__exit__()
-        launches = be.launches - launches0
-        durs = [a.elapsed_time(b) for a, b in ev]
-        e2e = None
-        if "e2e_step" in wl:
-            torch.cuda.synchronize()
-            e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                    for _ in range(args.steps)]
-            for i in range(args.steps):
-                flush.zero_()
-                e_ev[i][0].record(stream)
-                wl["e2e_step"]()
-                e_ev[i][1].record(stream)
-            torch.cuda.synchronize()
-            e2e_ms = statistics.mean(a.elapsed_time(b) for a, b in e_ev)
-            e2e = e2e_ms
-    ms = statistics.mean(durs)
-    t = torch.tensor([ms, e2e or 0.0], device="cuda", dtype=torch.float64)
-    if world > 1:
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms = float(t[0]), float(t[1])
+    meas = measure(be, wl, stream, flush, args.steps, args.warmup, world, local)
     sweep = allreduce_sweep(fb, be, world, stream) if (args.workload == "allreduce" and world > 1 and args.sweep) else None
-    if rank != 0:
-        return
-    agg = world if wl.get("aggregate", True) else 1
-    value = agg * wl["units"] / (ms * 1e-3) / wl["scale"]
+    extra = not args.headline_only and args.workload == "gemm_i8"
+    int8_peak = int8_library_peak(stream) if args.workload == "gemm_i8" and rank == 0 else None
     pk = peaks()
-    if wl["bound"] == "latency":
-        achieved = wl["flops"] / (ms * 1e-3) / 1e12
-        roof = {"bound": "latency", "achieved": round(achieved, 4), "peak": None, "unit": "TOPS", "frac": None,
-                "traffic": None, "peak_src": "launch/latency bound (13 M int-ops per forward)"}
-    elif wl["bound"] == "nvlink":
-        achieved = wl["units"] / (ms * 1e-3) / 1e9
-        roof = {"bound": "nvlink", "achieved": round(achieved, 1), "peak": 770.0, "unit": "GB/s",
-                "frac": round(achieved / 770.0, 3), "traffic": None,
-                "peak_src": "measured peer copy 770 GB/s per direction (pool figure)"}
-    elif wl["bound"] == "hbm":
-        achieved = wl["units"] / (ms * 1e-3) / 1e9
-        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 3), "traffic": None, "peak_src": pk["src"] + " copy"}
-    else:
-        flops = wl.get("flops", wl["units"])
-        achieved = flops / (ms * 1e-3) / 1e12
-        if wl.get("dtype") == "i8":
-            peak, src = 2 * pk["bf16_tflops"], f"2x {pk['src']} bf16 cuBLAS burst (dense int8 rate = 2x bf16)"
+    line = None
+    if rank == 0:
+        rep = report(wl, meas, world, pk, args, int8_peak)
+        line = {"metric": rep["metric"], "value": rep["value"], "unit": rep["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": rep["ms_per_step"],
+                "higher_is_better": True, "scaling": wl.get("scaling", "weak"), "vs_baseline": None,
+                "dtype": rep["dtype"], "data": "synthetic (seeded)",
+                "config": {**rep["config"], "l2": "flushed (256 MiB write) between steps",
+                           "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
+                                           f"tensor-parallel x{world} (NCCL)" if wl.get("scaling") == "strong" else
+                                           f"replicas x{world}") if world > 1 else "1 GPU",
+                           "host_cpus": numa}}
+        for k in ("roofline", "gpu_launches", "clocks", "wall_s", "e2e", "cpu_baseline", "parity"):
+            if k in rep:
+                line[k] = rep[k]
+        if sweep is not None:
+            line["sweep"] = sweep
+    del wl
+    if extra:
+        configs = {}
+        if world == 1:
+            for name in SUB_CONFIGS:
+                try:
+                    sub = make[name]()
+                    m_ = measure(be, sub, stream, flush, args.steps, args.warmup, world, local)
+                    configs[name] = report(sub, m_, world, pk, args)
+                    del sub
+                except Exception as e:  # one failing sub-config must not hide the headline
+                    configs[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
         else:
-            peak, src = pk["bf16_tflops"], f"{pk['src']} bf16 cuBLAS burst"
-        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 3), "traffic": None, "peak_src": src}
-    tr = TRAFFIC.get(wl["workload"])
-    if tr:
-        roof["traffic"], roof["traffic_unit"], roof["traffic_src"] = tr[0], "bytes per launch (ncu)", tr[1]
-    line = {"metric": wl["metric"], "value": round(value, 2), "unit": wl["unit"], "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": wl.get("scaling", "weak"), "vs_baseline": None, "dtype": wl["dtype"],
-            "data": "synthetic (seeded)",
-            "config": {"workload": wl["workload"], **wl["config"], "l2": "flushed (256 MiB write) between steps",
-                       "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
-                                       f"tensor-parallel x{world} (NCCL)" if wl.get("scaling") == "strong" else
-                                       f"replicas x{world}") if world > 1 else "1 GPU",
-                       "host_cpus": numa},
-            "roofline": roof, "gpu_launches": launches, "clocks": clk.summary(),
-            "wall_s": round(wall, 4)}
-    if e2e_ms:
-        line["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
-                       "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
-                       "ms_per_step": round(e2e_ms, 4), "api": wl.get("e2e_api", "")}
-    if args.workload == "allreduce" and world > 1 and args.sweep:
-        line["sweep"] = sweep
-    if "cpu" in wl and world == 1 and not args.no_cpu:
-        rate, sample = wl["cpu"](args.cpu_rows)
-        line["cpu_baseline"] = {"value": round(rate / wl["scale"], 4), "unit": wl["unit"],
-                                "cores": os.cpu_count(), "kind": "port", "sample": sample}
-    print(json.dumps(line), flush=True)
+            try:
+                rep = collective_report(fb, be, rank, world, stream, flush, args, local)
+                if rank == 0:
+                    configs["allreduce"] = rep
+            except Exception as e:
+                configs["allreduce"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        if line is not None:
+            line["configs"] = configs
+    if line is not None:
+        print(json.dumps(line), flush=True)
 
 
 def run_reference(args, rank, world):
@@ -543,6 +798,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=512)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="allreduce: add the 1 KiB - 1 GiB size sweep")
+    ap.add_argument("--headline-only", action="store_true", help="skip the other configs' sub-objects")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

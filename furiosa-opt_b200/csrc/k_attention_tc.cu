@@ -174,6 +174,7 @@ struct Params {
   float scale_log2;  // scale * log2(e)
   float eps;
   int* err;
+  int pv_wait;      // 1: issue S_t(j+1) only after PV_t(j) has completed (FOPT_ATTN_PV_WAIT, for comparison)
   uint64_t* trace;  // diagnostics (FOPT_ATTN_TRACE): per CTA 40 stamps, see attention_tc2_kernel
 };
 
@@ -446,8 +447,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 //   warps 2-5  softmax of query tile 0, warps 6-9 of tile 1: one thread per row reads its scores from
 //              TMEM, keeps the running max / sum, rescales its O row when the max grows, and writes
 //              the bf16 probabilities back over the first 64 columns of its S row (tcgen05.st).
-// While one tile's softmax runs, the tensor cores work on the other tile. P_t shares S_t's columns,
-// so S_t(j+1) is issued only after PV_t(j) has completed.
+// While one tile's softmax runs, the tensor cores work on the other tile. P_t shares S_t's columns;
+// S_t(j+1) is issued right behind PV_t(j), which the tensor pipe runs first (MMAs of one issuing
+// thread execute in order).
 // TMEM columns: S0 [0, 128), S1 [128, 256), O0 [256, 384), O1 [384, 512).
 // ---------------------------------------------------------------------------------------------
 constexpr int THREADS2 = 320;
@@ -592,8 +594,11 @@ __global__ void __launch_bounds__(THREADS2, 1)
           commit(smem_u32(&v_empty[j % STAGES]));
           if (solo) commit(smem_u32(&v_empty[j % STAGES]));
           if (j + 1 <= last) {
-            // S_t(j+1) overwrites the columns PV_t(j) reads P_t from: wait for it, and for K_{j+1}
-            ok = mbar_wait(smem_u32(&pv_done[t]), j & 1, abort_flag, p.err, 315) &&
+            // S_t(j+1) overwrites the columns PV_t(j) reads P_t from. MMAs issued by one thread run
+            // in issue order (tcgen05.mma -> tcgen05.mma is implicitly pipelined), so PV_t(j) has
+            // read P_t before S_t(j+1) writes there, and the issuer goes on to the other tile's PV
+            // instead of waiting for PV_t(j) to finish.
+            ok = (!p.pv_wait || mbar_wait(smem_u32(&pv_done[t]), j & 1, abort_flag, p.err, 315)) &&
                  mbar_wait(smem_u32(&k_full[(j + 1) % STAGES]), ((j + 1) / STAGES) & 1, abort_flag, p.err, 316);
             if (!ok) break;
             fence_after();
@@ -669,7 +674,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
       const float sum = ((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7]));
       l = l * alpha + sum;
       m = mnew;
-      // S_t(j) was issued after PV_t(j - 1) completed, so the O row is stable here
+      // S_t(j) was issued after PV_t(j - 1), and s_full's commit tracks every earlier MMA of the
+      // issuer, so PV_t(j - 1) has completed and the O row is stable here
       if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -802,6 +808,7 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
   p.scale_log2 = scale * 1.4426950408889634f;
   p.eps = eps;
   p.err = ctx->dev_err;
+  p.pv_wait = getenv("FOPT_ATTN_PV_WAIT") != nullptr;
   constexpr int smem = 2 * TILE + STAGES * 2 * TILE + 1024 + 256;
   static bool attr = false;
   if (!attr) {

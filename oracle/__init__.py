@@ -43,6 +43,7 @@ def build() -> str:
 
 _lib = None
 last_fold_seconds = 0.0  # duration of the last ref_contract fold (the timed CPU loop)
+last_transpose_seconds = 0.0  # duration of the last ref_transpose copy loop
 
 
 def lib():
@@ -132,7 +133,10 @@ def transpose(dst: bytes, src: bytes, dtype: str, Src: RefMapping, Dst: RefMappi
     pos = np.where(st == 0, pos, -1).astype(np.int64)
     out = _buf(dst)
     s = _buf(src)
+    global last_transpose_seconds
+    t0 = time.perf_counter()
     lib().ref_transpose(_p(out), _p(s), DT[dtype], _p(pos), C.c_int64(n), C.c_int64(src_base), C.c_int64(dst_base))
+    last_transpose_seconds = time.perf_counter() - t0
     return out.tobytes()
 
 
@@ -246,4 +250,22 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, B: int, S: int, Hq: i
     o = np.zeros(B * S * Hq * D, np.uint16)
     q, k, v = (np.ascontiguousarray(x, np.uint16) for x in (q, k, v))
     lib().ref_attention(_p(o), _p(q), _p(k), _p(v), B, S, Hq, Hkv, D, C.c_float(scale), int(causal), C.c_float(eps))
+    return o
+
+
+SQRT_HEAD_DIM = 11.313708  # attention.rs:9, sqrt(128) as the reference writes it
+
+
+def attention_chain(q: np.ndarray, k: np.ndarray, v: np.ndarray, B: int, S: int, Hq: int, Hkv: int, D: int,
+                    causal: bool = True, chunk: int = 512, sqrt_d: float = SQRT_HEAD_DIM,
+                    eps: float = 6.25e-8) -> np.ndarray:
+    """The reference's chunked attention op chain (attention.rs:32-392): bf16 logits divided by
+    sqrt(D), max before masking, Min mask, EPS per chunk, bf16 weights, 16-key bf16 partials, bf16
+    online rescale, final division. Returns bf16 bits [B, S, Hq, D]."""
+    if S > 4096 * 1024 or min(chunk, S) > 4096 or D > 256:
+        raise ValueError("attention_chain: chunk <= 4096 and D <= 256")
+    o = np.zeros(B * S * Hq * D, np.uint16)
+    q, k, v = (np.ascontiguousarray(x, np.uint16) for x in (q, k, v))
+    lib().ref_attention_chain(_p(o), _p(q), _p(k), _p(v), B, S, Hq, Hkv, D, C.c_float(sqrt_d), int(causal),
+                              C.c_float(eps), int(chunk))
     return o

@@ -213,6 +213,9 @@ static int32_t sat64(int64_t v) { return v < INT32_MIN ? INT32_MIN : v > INT32_M
 /* ---- transpose ---- */
 void ref_transpose(void* dst, const void* src, int dt, const int64_t* src_pos, int64_t n_pos, int64_t src_base,
                    int64_t dst_base) {
+  /* parallel over destination positions, as rayon's dst chunks (buf.rs:164-198); 4-bit types share
+   * bytes between neighbours, so they run serially */
+#pragma omp parallel for schedule(static) if (bits_of(dt) >= 8 && n_pos >= 65536)
   for (int64_t q = 0; q < n_pos; ++q) {
     if (src_pos[q] < 0) continue;
     st(dst, dt, dst_base + q, ld(src, dt, src_base + src_pos[q]));
@@ -435,4 +438,71 @@ void ref_attention(uint16_t* o, const uint16_t* q, const uint16_t* k, const uint
         for (int d = 0; d < D; ++d) orow[d] = (uint16_t)(f32_to_bf16(f2u(acc[d] / (l + eps))) >> 16);
       }
     }
+}
+
+/* The reference's chunked attention chain for one query row against keys [0, S) of one kv head,
+ * furiosa-opt-examples/src/transformer/kernel/attention.rs, per key chunk of `chunk` keys:
+ *   qk_scaled  (:32-74)   logit = bf16(sum_d q*k / SQRT_HEAD_DIM), SQRT_HEAD_DIM = 11.313708 (D = 128)
+ *   row_max    (:77-95)   m_c = max of the chunk's bf16 logits, masked keys included
+ *   forward    (:252-365) m = max(m_old, m_c); alpha = exp(m_old - m)
+ *   masked_exp (:98-138)  e_t = min(exp(logit_t - m), mask_t), mask 1.0 (visible) or 0.0 (masked)
+ *   row_sum    (:141-159) s_c = sum_t e_t + EPS (EPS = 6.25e-8, added per chunk); s = s_old*alpha + s_c
+ *   weighted_sum (:162-221) w_t = bf16(e_t); per 16-key slice a bf16 partial sum_t w_t v_t, then the
+ *              slices summed in f32 and rounded to bf16
+ *   out        out = bf16(bf16(out_old * alpha) + result); the first chunk stores result, m_c, s_c
+ *   norm       (:370-392) bf16(out / s)
+ * Sums inside a chunk run in key order (the engine's intra-slice order is not observable beyond
+ * f32 rounding). Causal prefill is the decode chain once per query row i, with mask_t = (t <= i). */
+static float bf16r(float x) { return u2f(f32_to_bf16(f2u(x))); }
+void ref_attention_chain(uint16_t* o, const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int S, int Hq,
+                         int Hkv, int D, float sqrt_d, int causal, float eps, int chunk) {
+#pragma omp parallel for collapse(3) schedule(dynamic)
+  for (int b = 0; b < B; ++b)
+    for (int i = 0; i < S; ++i)
+      for (int h = 0; h < Hq; ++h) {
+        float out[256], res[256], part[256], logit[4096];
+        int hk = h / (Hq / Hkv);
+        const uint16_t* qr = q + (((int64_t)b * S + i) * Hq + h) * D;
+        float m = 0.0f, ssum = 0.0f;
+        for (int c0 = 0; c0 < S; c0 += chunk) {
+          int c1 = c0 + chunk < S ? c0 + chunk : S;
+          float mc = -INFINITY;
+          for (int t = c0; t < c1; ++t) {
+            const uint16_t* kr = k + (((int64_t)b * S + t) * Hkv + hk) * D;
+            float acc = 0.0f;
+            for (int d = 0; d < D; ++d) acc += u2f((uint32_t)qr[d] << 16) * u2f((uint32_t)kr[d] << 16);
+            logit[t - c0] = bf16r(acc / sqrt_d);
+            mc = logit[t - c0] > mc ? logit[t - c0] : mc;
+          }
+          float mnew = c0 == 0 ? mc : (mc > m ? mc : m);
+          float alpha = c0 == 0 ? 1.0f : expf(m - mnew);
+          float sc = 0.0f;
+          for (int d = 0; d < D; ++d) res[d] = 0.0f;
+          for (int s0 = c0; s0 < c1; s0 += 16) {
+            for (int d = 0; d < D; ++d) part[d] = 0.0f;
+            for (int t = s0; t < s0 + 16 && t < c1; ++t) {
+              float mask = (!causal || t <= i) ? 1.0f : 0.0f;
+              float e = expf(logit[t - c0] - mnew);
+              e = e < mask ? e : mask;
+              sc += e;
+              float w = bf16r(e);
+              const uint16_t* vr = v + (((int64_t)b * S + t) * Hkv + hk) * D;
+              for (int d = 0; d < D; ++d) part[d] += w * u2f((uint32_t)vr[d] << 16);
+            }
+            for (int d = 0; d < D; ++d) res[d] += bf16r(part[d]);
+          }
+          sc += eps;
+          for (int d = 0; d < D; ++d) res[d] = bf16r(res[d]);
+          if (c0 == 0) {
+            for (int d = 0; d < D; ++d) out[d] = res[d];
+            ssum = sc;
+          } else {
+            for (int d = 0; d < D; ++d) out[d] = bf16r(bf16r(out[d] * alpha) + res[d]);
+            ssum = ssum * alpha + sc;
+          }
+          m = mnew;
+        }
+        uint16_t* orow = o + (((int64_t)b * S + i) * Hq + h) * D;
+        for (int d = 0; d < D; ++d) orow[d] = (uint16_t)(f32_to_bf16(f2u(out[d] / ssum)) >> 16);
+      }
 }

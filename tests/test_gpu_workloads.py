@@ -59,6 +59,62 @@ def test_decoder_block_w8a8(b200):
     assert err.mean() <= 0.003 * scale, f"mean abs err {err.mean()}"
 
 
+def test_decoder_block_config4_shape(b200):
+    """Config 4 at its own shape: Llama-3-8B W8A8 block (hidden 4096, FFN 14336, 32 / 8 heads) over
+    8 x 512 tokens on the GPU. Under the causal mask the first 64 tokens of each sequence depend on
+    nothing later, so the oracle runs the block on those 8 x 64 tokens and they are compared. f32
+    folds run in wire order (exact-fold mode) on both sides.
+
+    Two comparisons, errors printed:
+      * the oracle given the kernel's own attention output: every other step is the same chain, so
+        the outputs agree bit for bit except where CUDA's expf and libm's differ by an ulp inside
+        SiLU and move an activation across an int8 rounding boundary: at most 0.1 % of the
+        elements, each by at most 2 bf16 ulps of max |out|;
+      * the oracle end to end (f32 online-softmax attention): the attention outputs differ by a bf16
+        ulp in places, and a bf16 ulp of an activation is half an int8 step at the top of its
+        range, so about half the block's int8 activations after attention can move by one step.
+        Each move changes a projection output by one step times one weight; the sums stay within 4
+        bf16 ulps of max |out| at every element and 2^-10 max |out| on average."""
+    batch, seq, Hq, Hkv, F = 8, 512, 32, 8, 14336
+    T, H, keep = batch * seq, Hq * 128, 64
+    was = b200.exact_fold
+    b200.set_exact_fold(True)
+    captured = {}
+    attention = b200.attention
+
+    def keep_attention(*a, **k):
+        captured["att"] = attention(*a, **k)
+        return captured["att"]
+
+    try:
+        b200.attention = keep_attention
+        blk = W.DecoderBlockW8A8(b200, T, H, Hq, Hkv, F, batch, seq, seed=3)
+        rng = np.random.default_rng(5)
+        x = fb.dtypes.f32_to_bf16_bits(rng.standard_normal(T * H).astype(np.float32))
+        got = fb.dtypes.bf16_bits_to_f32(blk.forward(b200.from_vec(blk.m("[T, H]"), x, "bf16")).to_numpy())
+        att = captured["att"].to_numpy()
+    finally:
+        del b200.attention
+        b200.set_exact_fold(was)
+    first = lambda a: a.reshape(batch, seq, H)[:, :keep].reshape(-1)  # noqa: E731
+    got, att, xs = first(got), first(att), first(x)
+    assert np.all(np.isfinite(got))
+    for label, override in (("kernel attention", att), ("end to end", None)):
+        want = fb.dtypes.bf16_bits_to_f32(R.decoder_ref(xs, blk.host, batch * keep, H, Hq, Hkv, F, batch, keep,
+                                                         att_override=override)).reshape(-1)
+        err = np.abs(got - want)
+        scale = np.max(np.abs(want))
+        nd = np.count_nonzero(err)
+        print(f"decoder block 8x512, first {keep} tokens per sequence, oracle with {label}: max |out| {scale:.4g}, "
+              f"max abs err {err.max():.4g}, mean abs err {err.mean():.3g}, {nd} of {err.size} elements differ")
+        if override is not None:
+            assert nd <= err.size // 1000, nd
+            assert err.max() <= 2 * 2 ** -8 * scale, f"max abs err {err.max()} vs max |out| {scale}"
+        else:
+            assert err.max() <= 4 * 2 ** -8 * scale, f"max abs err {err.max()} vs max |out| {scale}"
+            assert err.mean() <= 2 ** -10 * scale, f"mean abs err {err.mean()}"
+
+
 def test_decoder_block_tensor_parallel_one_rank_bit_exact(b200):
     """The tensor-parallel block on one rank: its row-parallel projections take the i32 sums then
     dequantise elementwise, and its quantisation scales pass through the (one-rank) max all-reduce;
