@@ -69,3 +69,21 @@ def chip_shuffle(backend, dst, src, pattern) -> None:
     arr = (C.c_int32 * len(pattern))(*pattern)
     dst._will_write()
     check(_lib.lib().fopt_chip_shuffle(backend.ctx, dst.ptr, src.ptr, src.nbytes, arr, len(pattern)), backend.ctx)
+
+
+def chip_shuffle_local(backend, src, chips: int, pattern):
+    """`dm_chip_shuffle` / `hbm_chip_shuffle` when every chip's slab lives in one storage (the Chip
+    axis outermost, as the reference's single-process tensors hold it, memory.rs:1211-1233): a fresh
+    storage whose slab t is src's slab pattern[t]. Slabs are contiguous, so each moves as one
+    device-to-device copy."""
+    from .backend import Storage
+    if sorted(pattern) != list(range(chips)) or len(pattern) != chips:
+        raise ValueError("chip shuffle pattern must be a permutation of the chips")
+    if src.nbytes % chips:
+        raise ValueError("chip shuffle: the storage does not split into equal chip slabs")
+    slab = src.nbytes // chips
+    out = Storage(backend, src.dtype, src.n, zero=False)
+    for t, s in enumerate(pattern):
+        check(_lib.lib().fopt_d2d(backend.ctx, C.c_void_p(out.addr + t * slab), C.c_void_p(src.addr + s * slab), slab),
+              backend.ctx)
+    return out
