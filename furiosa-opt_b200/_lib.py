@@ -124,6 +124,8 @@ SIGNATURES = [
     ("fopt_allreduce_op", _I32, [_VP, _VP, _I64, C.c_int, C.c_int]),
     ("fopt_allreduce", _I32, [_VP, _VP, _I64, C.c_int]),
     ("fopt_chip_shuffle", _I32, [_VP, _VP, _VP, _SZ, C.POINTER(_I32), _I32]),
+    ("fopt_chip_shuffle_plan", _I32, [C.POINTER(_I32), _I32, _I32, C.POINTER(_I32), C.POINTER(_I32),
+                                      C.POINTER(_I32)]),
 ]
 
 _lib = None

@@ -10,6 +10,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "ctx.hpp"
 
@@ -149,20 +150,38 @@ fopt_status fopt_allreduce(fopt_ctx* ctx, void* buf, int64_t count, fopt_dtype d
   return fopt_allreduce_op(ctx, buf, count, dtype, FOPT_RED_ADD);
 }
 
+fopt_status fopt_chip_shuffle_plan(const int32_t* pattern, int32_t nranks, int32_t rank, int32_t* sends,
+                                   int32_t* n_sends, int32_t* recv_from) {
+  if (!pattern || !sends || !n_sends || !recv_from || nranks <= 0 || rank < 0 || rank >= nranks) return FOPT_ERR_INVALID;
+  std::vector<int> seen(nranks, 0);
+  for (int t = 0; t < nranks; ++t) {
+    if (pattern[t] < 0 || pattern[t] >= nranks || seen[pattern[t]]++) return FOPT_ERR_INVALID;  // a permutation
+  }
+  int k = 0;
+  for (int t = 0; t < nranks; ++t)
+    if (pattern[t] == rank && t != rank) sends[k++] = t;
+  *n_sends = k;
+  *recv_from = pattern[rank];
+  return FOPT_OK;
+}
+
 fopt_status fopt_chip_shuffle(fopt_ctx* ctx, void* dst, const void* src, size_t bytes, const int32_t* pattern,
                               int32_t nranks) {
   return guard(ctx, [&] {
     if (!ctx->nccl_comm || nranks != ctx->nranks) throw Fail{FOPT_ERR_INVALID, "fopt_chip_shuffle: communicator size"};
+    std::vector<int32_t> sends(nranks);
+    int32_t n_sends = 0, from = 0;
+    if (fopt_chip_shuffle_plan(pattern, nranks, ctx->rank, sends.data(), &n_sends, &from) != FOPT_OK)
+      throw Fail{FOPT_ERR_INVALID, "fopt_chip_shuffle: pattern must be a permutation of the ranks"};
     auto& a = nccl();
-    int me = ctx->rank;
     nccl_check(a.GroupStart(), "ncclGroupStart");
-    for (int t = 0; t < nranks; ++t)
-      if (pattern[t] == me && t != me)
-        nccl_check(a.Send(src, bytes, ncclInt8, t, (ncclComm_t)ctx->nccl_comm, ctx->stream), "ncclSend");
-    int from = pattern[me];
-    if (from != me) nccl_check(a.Recv(dst, bytes, ncclInt8, from, (ncclComm_t)ctx->nccl_comm, ctx->stream), "ncclRecv");
+    for (int i = 0; i < n_sends; ++i)
+      nccl_check(a.Send(src, bytes, ncclInt8, sends[i], (ncclComm_t)ctx->nccl_comm, ctx->stream), "ncclSend");
+    if (from != ctx->rank)
+      nccl_check(a.Recv(dst, bytes, ncclInt8, from, (ncclComm_t)ctx->nccl_comm, ctx->stream), "ncclRecv");
     nccl_check(a.GroupEnd(), "ncclGroupEnd");
-    if (from == me && dst != src) cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream), "self copy");
+    if (from == ctx->rank && dst != src)
+      cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream), "self copy");
   });
 }
 

@@ -15,12 +15,15 @@ from ._lib import check
 
 def shuffle_peers(pattern, rank: int):
     """For `pattern[target] = source`: the ranks this rank sends its slab to, and the rank it receives
-    from (itself when it keeps its own slab). Mirrors fopt_chip_shuffle's grouping."""
+    from (itself when it keeps its own slab). The plan fopt_chip_shuffle runs (fopt_chip_shuffle_plan)."""
     n = len(pattern)
-    if sorted(pattern) != list(range(n)):
+    arr = (C.c_int32 * n)(*pattern)
+    sends = (C.c_int32 * max(n, 1))()
+    ns, frm = C.c_int32(), C.c_int32()
+    st = _lib.lib().fopt_chip_shuffle_plan(arr, n, rank, sends, C.byref(ns), C.byref(frm))
+    if st != 0:
         raise ValueError("chip shuffle pattern must be a permutation of the chips")
-    sends = [t for t in range(n) if pattern[t] == rank and t != rank]
-    return sends, pattern[rank]
+    return [sends[i] for i in range(ns.value)], frm.value
 
 
 def exchange_unique_id(rank: int, world: int, broadcast) -> bytes:

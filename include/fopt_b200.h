@@ -376,6 +376,11 @@ fopt_status fopt_allreduce_op(fopt_ctx* ctx, void* buf, int64_t count, fopt_dtyp
  * target whose source it is and receives the slab of pattern[rank]. */
 fopt_status fopt_chip_shuffle(fopt_ctx* ctx, void* dst, const void* src, size_t bytes, const int32_t* pattern,
                               int32_t nranks);
+/* The peer plan fopt_chip_shuffle runs for `rank` (host only, no communicator): the targets it sends
+ * its slab to (sends[0 .. *n_sends), capacity nranks) and the rank it receives from. FOPT_ERR_INVALID
+ * unless pattern is a permutation of 0 .. nranks - 1. */
+fopt_status fopt_chip_shuffle_plan(const int32_t* pattern, int32_t nranks, int32_t rank, int32_t* sends,
+                                   int32_t* n_sends, int32_t* recv_from);
 
 #ifdef __cplusplus
 }

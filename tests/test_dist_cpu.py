@@ -1,8 +1,16 @@
-"""Host-side multi-rank logic on CPU: 2 gloo ranks (no GPU). Checks the chip-shuffle peer plan is
-consistent across ranks and that the NCCL-id rendezvous path delivers rank 0's bytes everywhere."""
+"""Host-side multi-rank logic on CPU: gloo ranks (no GPU) running the library's own host code.
+
+  * the chip-shuffle peer plan (fopt_chip_shuffle_plan, the plan fopt_chip_shuffle executes over
+    NCCL) drives a real exchange of slabs between 4 gloo ranks, which must realise
+    `pattern[target] = source` (memory.rs:657-679, cluster_chip_shuffle_slice.rs:5-19);
+  * the communicator rendezvous (dist.exchange_unique_id with the library's fopt_comm_unique_id on
+    rank 0) delivers rank 0's id to every rank;
+  * the bench's max-over-ranks timing reduction.
+"""
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch.multiprocessing as mp
 
@@ -24,11 +32,14 @@ def test_shuffle_peers_plan():
         assert recv == pattern[r]
         for t in sends:
             assert plans[t][1] == r
+    assert fb.dist.shuffle_peers([0, 1, 2, 3], 2) == ([], 2)
     with pytest.raises(ValueError):
         fb.dist.shuffle_peers([0, 0, 1, 2], 0)
+    with pytest.raises(ValueError):
+        fb.dist.shuffle_peers([0, 1, 4, 2], 0)
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, pattern, q):
     import torch
     import torch.distributed as dist
 
@@ -40,26 +51,38 @@ def _worker(rank, world, port, q):
         dist.broadcast(t, 0)
         buf[:] = bytes(t.tolist())
 
-    # the id exchange without NCCL: rank 0 contributes a known pattern in place of a real id
-    buf = bytearray(range(128)) if rank == 0 else bytearray(128)
-    bcast(buf)
+    uid = fb.dist.exchange_unique_id(rank, world, bcast)
+    # the chip shuffle plan, executed with gloo point-to-point in place of NCCL
+    slab = torch.from_numpy((np.arange(4096, dtype=np.int32) + 100000 * rank))
+    out = torch.zeros_like(slab)
+    sends, frm = fb.dist.shuffle_peers(pattern, rank)
+    reqs = [dist.isend(slab, t) for t in sends]
+    if frm != rank:
+        dist.recv(out, frm)
+    else:
+        out.copy_(slab)
+    for r in reqs:
+        r.wait()
     t = torch.tensor([float(rank + 1)])
     dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the bench's max-over-ranks timing reduction
-    q.put((rank, bytes(buf), float(t)))
+    q.put((rank, uid, out.numpy().copy(), float(t)))
     dist.destroy_process_group()
 
 
-def test_gloo_rendezvous_two_ranks():
+@pytest.mark.parametrize("world,pattern", [(2, [1, 0]), (4, [1, 2, 3, 0]), (4, [2, 1, 3, 0])])
+def test_gloo_ranks_run_the_library_plan(world, pattern):
     ctx = mp.get_context("fork")  # no CUDA state in this process
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, pattern, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=120) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, buf, mx in got:
-        assert buf == bytes(range(128))
-        assert mx == 2.0
+    uids = {uid for _, uid, _, _ in got}
+    assert len(uids) == 1 and len(next(iter(uids))) == 128 and any(next(iter(uids)))
+    for rank, _, out, mx in got:
+        assert np.array_equal(out, np.arange(4096, dtype=np.int32) + 100000 * pattern[rank])
+        assert mx == float(world)
