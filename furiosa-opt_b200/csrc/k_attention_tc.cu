@@ -4,14 +4,15 @@
 // row_sum + EPS, weighted_sum, online rescale, norm).
 //
 // One CTA per (batch, query head, 128-row query block); 192 threads:
-//   warp 0   TMA producer: Q once, then K and V^T tiles (128 keys) into a 2-stage ring;
+//   warp 0   TMA producer: Q once, then K and V tiles (128 keys) into a 2-stage ring;
 //   warp 1   TMEM owner and single-thread MMA issuer: S_j = Q K_j^T (M=N=K=128, bf16 -> f32) into one of
 //            two TMEM S buffers, then O += P_j V_j into the TMEM O accumulator;
 //   warps 2-5 softmax: one thread per query row reads its 128 scores from TMEM (no cross-thread
 //            reduction), keeps the running max / sum in registers, rescales its O row in TMEM when the
 //            max grows, and writes P_j (bf16) into shared memory in the UMMA K-major 128B-swizzle layout.
 // S_{j+1} is issued before waiting for P_j, so the QK^T of the next block overlaps this block's
-// softmax. V is transposed once per call (V^T [B, Hkv, D, S]) so both MMAs read K-major operands.
+// softmax. V is read in its own [B, S, Hkv, D] layout: the PV product takes it as an MN-major B
+// operand (D contiguous), so no transposed copy is made.
 // Every wait is bounded (~2 s of %globaltimer) and reports through the context's device error word.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -108,6 +109,19 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
   d |= (uint64_t)2 << 61;
   return d;
 }
+// V [keys, D] as the PV product's B operand read MN-major (D contiguous) straight from its natural
+// layout: each 64-wide half of D is one TMA box of 128 keys x 128 bytes, 128-byte swizzled in 8-key
+// atoms. Leading byte offset = the distance between the two D halves (one box), stride byte offset =
+// the distance between 8-key atoms (1024 bytes); a 16-key MMA step starts 16 x 128 bytes further on.
+__device__ __forceinline__ uint64_t vdesc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFF) >> 4);
+  d |= (uint64_t)(16384 >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+constexpr uint32_t kIdescBMajorMN = 1u << 16;  // instruction descriptor: B operand MN-major
 __device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -175,7 +189,7 @@ struct Params {
   float eps;
   int* err;
   int pv_wait;      // 1: issue S_t(j+1) only after PV_t(j) has completed (FOPT_ATTN_PV_WAIT, for comparison)
-  uint64_t* trace;  // diagnostics (FOPT_ATTN_TRACE): per CTA 40 stamps, see attention_tc2_kernel
+  uint64_t* trace;  // diagnostics (FOPT_ATTN_TRACE): per CTA 128 stamps, see attention_tc2_kernel
 };
 
 // 2^x on the special-function unit (relative error ~2^-22; the scores' bf16 rounding dominates).
@@ -219,12 +233,12 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) { return bf16x
 
 __global__ void __launch_bounds__(THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                        const __grid_constant__ CUtensorMap tmVt, Params p) {
+                        const __grid_constant__ CUtensorMap tmV, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;                       // 32 KiB
   uint8_t* sP = smem + TILE;                // 32 KiB
-  uint8_t* sKV = smem + 2 * TILE;           // STAGES x (K tile + V^T tile)
+  uint8_t* sKV = smem + 2 * TILE;           // STAGES x (K tile + V tile)
   uint64_t* bars = (uint64_t*)(smem + 2 * TILE + STAGES * 2 * TILE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
@@ -238,10 +252,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = p.S / BQ;
-  // heaviest (last) query blocks first under causal masking
-  const int qb = nqb - 1 - (int)(blockIdx.x % nqb);
-  const int h = (int)((blockIdx.x / nqb) % p.Hq);
-  const int b = (int)(blockIdx.x / (nqb * p.Hq));
+  // longest work first across the grid (the last query blocks under causal masking)
+  const int bh = (int)(blockIdx.x % (p.B * p.Hq));
+  const int qb = nqb - 1 - (int)(blockIdx.x / (p.B * p.Hq));
+  const int h = bh % p.Hq;
+  const int b = bh / p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
   const int nkb = p.causal ? qb + 1 : p.S / BK;
 
@@ -288,8 +303,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t* sV = sK + TILE;
         tma3(smem_u32(sK), &tmK, fb, 0, hk, row0 + j * BK);
         tma3(smem_u32(sK + CHUNK), &tmK, fb, 64, hk, row0 + j * BK);
-        tma3(smem_u32(sV), &tmVt, fb, j * BK, 0, b * p.Hkv + hk);
-        tma3(smem_u32(sV + CHUNK), &tmVt, fb, j * BK + 64, 0, b * p.Hkv + hk);
+        tma3(smem_u32(sV), &tmV, fb, 0, hk, row0 + j * BK);
+        tma3(smem_u32(sV + CHUNK), &tmV, fb, 64, hk, row0 + j * BK);
       }
     }
   } else if (warp == 1) {
@@ -321,7 +336,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
-          mma_bf16(tO, sdesc(smem_u32(sP) + off), sdesc(sV + off), idesc, (j | k) != 0);
+          mma_bf16(tO, sdesc(smem_u32(sP) + off), vdesc(sV + 2048 * k), idesc | kIdescBMajorMN, (j | k) != 0);
         }
         commit(smem_u32(&kv_empty[st]));
         commit(smem_u32(o_done));
@@ -440,7 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Two query tiles per CTA (ping-pong), P kept in tensor memory.
 //
 // One CTA per (batch, query head, pair of adjacent 128-row query blocks); 320 threads:
-//   warp 0     TMA producer: both Q tiles once, then K and V^T tiles into a 2-stage ring that both
+//   warp 0     TMA producer: both Q tiles once, then K and V tiles into a 2-stage ring that both
 //              query tiles read;
 //   warp 1     TMEM owner and MMA issuer, in the order S0(0) S1(0) | PV0(j) S0(j+1) PV1(j) S1(j+1) ...:
 //              S_t = Q_t K^T into TMEM, and O_t += P_t V with P_t read from TMEM (the A operand);
@@ -463,11 +478,11 @@ __device__ __forceinline__ void mma_bf16_ta(uint32_t d, uint32_t a_tmem, uint64_
 
 __global__ void __launch_bounds__(THREADS2, 1)
     attention_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                         const __grid_constant__ CUtensorMap tmVt, const __grid_constant__ CUtensorMap tmO, Params p) {
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sQ = smem;               // 2 x 32 KiB (tile t at sQ + t * TILE)
-  uint8_t* sKV = smem + 2 * TILE;   // STAGES x (K tile + V^T tile)
+  uint8_t* sKV = smem + 2 * TILE;   // STAGES x (K tile + V tile)
   uint64_t* bars = (uint64_t*)(smem + 2 * TILE + STAGES * 2 * TILE);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;  // K and V of a stage are released separately: K after both S MMAs
@@ -482,13 +497,16 @@ __global__ void __launch_bounds__(THREADS2, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int npair = p.S / (2 * BQ);
-  // heaviest (last) query blocks first under causal masking
-  const int qp = npair - 1 - (int)(blockIdx.x % npair);
-  const int h = (int)((blockIdx.x / npair) % p.Hq);
-  const int b = (int)(blockIdx.x / (npair * p.Hq));
+  // Longest work first across the whole grid: the B * Hq heaviest pairs (the last query blocks under
+  // causal masking) take the lowest block indices, then the next heaviest, and so on, so the blocks
+  // the hardware schedules last, as SMs free up, are the shortest.
+  const int bh = (int)(blockIdx.x % (p.B * p.Hq));
+  const int qp = npair - 1 - (int)(blockIdx.x / (p.B * p.Hq));
+  const int h = bh % p.Hq;
+  const int b = bh / p.Hq;
   const int hk = h / (p.Hq / p.Hkv);
   const int qb0 = 2 * qp;  // tile t covers query block qb0 + t
-  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 40 : nullptr;
+  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 128 : nullptr;
   if (tr && threadIdx.x == 0) tr[0] = gtimer();
   // last key block of each tile (inclusive)
   const int last0 = p.causal ? qb0 : p.S / BK - 1;
@@ -542,8 +560,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
         if (!mbar_wait(smem_u32(&v_empty[st]), ph, abort_flag, p.err, 319)) break;
         const uint32_t vb = smem_u32(&v_full[st]);
         mbar_expect_tx(vb, TILE);
-        tma3(smem_u32(sV), &tmVt, vb, j * BK, 0, b * p.Hkv + hk);
-        tma3(smem_u32(sV + CHUNK), &tmVt, vb, j * BK + 64, 0, b * p.Hkv + hk);
+        tma3(smem_u32(sV), &tmV, vb, 0, hk, row0 + j * BK);
+        tma3(smem_u32(sV + CHUNK), &tmV, vb, 64, hk, row0 + j * BK);
       }
     }
   } else if (warp == 1) {
@@ -565,8 +583,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
         const uint32_t sV = smem_u32(sKV + (j % STAGES) * 2 * TILE + TILE);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32);
-          mma_bf16_ta(tmem + 256 + t * 128, tmem + t * 128 + 8 * k, sdesc(sV + off), idesc, (j | k) != 0);
+          mma_bf16_ta(tmem + 256 + t * 128, tmem + t * 128 + 8 * k, vdesc(sV + 2048 * k), idesc | kIdescBMajorMN,
+                      (j | k) != 0);
         }
         commit(smem_u32(&pv_done[t]));
       };
@@ -588,7 +606,9 @@ __global__ void __launch_bounds__(THREADS2, 1)
                mbar_wait(smem_u32(&v_full[j % STAGES]), (j / STAGES) & 1, abort_flag, p.err, 320);
           if (!ok) break;
           fence_after();
+          if (tr && t == 0 && j < 14) tr[80 + 3 * j] = gtimer();
           issue_pv(t, j);
+          if (tr && t == 0 && j < 14) tr[81 + 3 * j] = gtimer();
           // the K and V "empty" barriers take one commit per tile per block (two from tile 1 for the
           // block tile 0 does not use)
           commit(smem_u32(&v_empty[j % STAGES]));
@@ -603,6 +623,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
             if (!ok) break;
             fence_after();
             issue_s(t, j + 1);
+            if (tr && t == 0 && j < 14) tr[82 + 3 * j] = gtimer();
             commit(smem_u32(&k_empty[(j + 1) % STAGES]));
             if (t == 1 && j + 1 > last0) commit(smem_u32(&k_empty[(j + 1) % STAGES]));
           }
@@ -627,8 +648,8 @@ __global__ void __launch_bounds__(THREADS2, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       fence_after();
-      const bool tracer = tr && t == 0 && r == 0 && j < 17;
-      if (tracer) tr[1 + 2 * j] = gtimer();
+      const bool tracer = tr && r == 0 && j < 17;
+      if (tracer) tr[40 * t + 1 + 2 * j] = gtimer();
       uint32_t s[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) tld32(tS + c * 32, s + 32 * c);
@@ -692,7 +713,7 @@ __global__ void __launch_bounds__(THREADS2, 1)
       tst_wait();
       fence_before();
       mbar_arrive(smem_u32(&p_ready[t]));
-      if (tracer) tr[2 + 2 * j] = gtimer();
+      if (tracer) tr[40 * t + 2 + 2 * j] = gtimer();
     }
     if (tr && t == 0 && r == 0) tr[35] = gtimer();
     if (ok) {
@@ -741,17 +762,6 @@ __global__ void __launch_bounds__(THREADS2, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
-// V [B, S, Hkv, D] -> V^T [B, Hkv, D, S] (32 x 32 tiles through shared memory)
-__global__ void transpose_v_kernel(uint16_t* __restrict__ vt, const uint16_t* __restrict__ v, int S, int Hkv) {
-  __shared__ uint16_t tile[32][34];
-  const int bh = blockIdx.z, b = bh / Hkv, hk = bh % Hkv;
-  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  for (int i = threadIdx.y; i < 32; i += 8)
-    tile[i][threadIdx.x] = v[(((int64_t)b * S + s0 + i) * Hkv + hk) * D + d0 + threadIdx.x];
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += 8)
-    vt[(((int64_t)b * Hkv + hk) * D + d0 + i) * S + s0 + threadIdx.x] = tile[threadIdx.x][i];
-}
 
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -789,15 +799,10 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
   using namespace attn;
   if (Dh != 128 || S % 128 || getenv("FOPT_ATTN_NO_TC")) return false;
   if ((uintptr_t)q % 16 || (uintptr_t)k % 16 || (uintptr_t)v % 16 || (uintptr_t)o % 16) return false;
-  // V^T into context scratch
-  const size_t vt_bytes = (size_t)B * Hkv * D * S * 2;
-  uint16_t* vt = (uint16_t*)scratch(ctx, vt_bytes);
-  transpose_v_kernel<<<dim3(S / 32, D / 32, B * Hkv), dim3(32, 8), 0, ctx->stream>>>(vt, (const uint16_t*)v, S, Hkv);
-  launched(ctx, "attention_transpose_v");
   const uint64_t rows = (uint64_t)B * S;
   CUtensorMap mq = map3(q, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 128);
   CUtensorMap mk = map3(k, D, Hkv, rows, (uint64_t)D * 2, (uint64_t)Hkv * D * 2, 1, 128);
-  CUtensorMap mv = map3(vt, S, D, (uint64_t)B * Hkv, (uint64_t)S * 2, (uint64_t)D * S * 2, 128, 1);
+  CUtensorMap mv = map3(v, D, Hkv, rows, (uint64_t)D * 2, (uint64_t)Hkv * D * 2, 1, 128);
   Params p{};
   p.O = (uint16_t*)o;
   p.B = B;
@@ -822,24 +827,24 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
     const int64_t blocks = (int64_t)B * Hq * (S / 256);
     const char* trace_path = getenv("FOPT_ATTN_TRACE");
     if (trace_path) {
-      cuda_check(cudaMallocAsync((void**)&p.trace, blocks * 40 * 8, ctx->stream), "trace alloc");
-      cuda_check(cudaMemsetAsync(p.trace, 0, blocks * 40 * 8, ctx->stream), "trace clear");
+      cuda_check(cudaMallocAsync((void**)&p.trace, blocks * 128 * 8, ctx->stream), "trace alloc");
+      cuda_check(cudaMemsetAsync(p.trace, 0, blocks * 128 * 8, ctx->stream), "trace clear");
     }
     CUtensorMap mo = map3(o, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 32);
     attention_tc2_kernel<<<(unsigned)blocks, THREADS2, smem, ctx->stream>>>(mq, mk, mv, mo, p);
     launched(ctx, "attention_tc2");
     if (trace_path) {  // diagnostics only: one line per CTA, stamps in ns from the earliest entry
-      std::vector<uint64_t> t((size_t)blocks * 40);
+      std::vector<uint64_t> t((size_t)blocks * 128);
       cuda_check(cudaMemcpyAsync(t.data(), p.trace, t.size() * 8, cudaMemcpyDeviceToHost, ctx->stream), "trace copy");
       cuda_check(cudaStreamSynchronize(ctx->stream), "trace sync");
       cudaFreeAsync(p.trace, ctx->stream);
       uint64_t t0 = ~0ull;
-      for (int64_t c = 0; c < blocks; ++c) t0 = std::min(t0, t[c * 40]);
+      for (int64_t c = 0; c < blocks; ++c) t0 = std::min(t0, t[c * 128]);
       if (FILE* f = fopen(trace_path, "a")) {
         fprintf(f, "# blocks=%lld S=%d\n", (long long)blocks, S);
         for (int64_t c = 0; c < blocks; ++c) {
           fprintf(f, "%lld", (long long)c);
-          for (int k = 0; k < 40; ++k) fprintf(f, " %lld", t[c * 40 + k] ? (long long)(t[c * 40 + k] - t0) : -1LL);
+          for (int k = 0; k < 128; ++k) fprintf(f, " %lld", t[c * 128 + k] ? (long long)(t[c * 128 + k] - t0) : -1LL);
           fprintf(f, "\n");
         }
         fclose(f);
