@@ -299,6 +299,68 @@ def wl_relayout(fb, be, R=8192, C=8192):
                 dtype="bf16", config={"R": R, "C": C})
 
 
+def wl_relayout_padded(fb, be, R=1 << 20, D=61):
+    """The padded-row move [R, D] -> [R, D # 64] (f32, 244 MiB live each way): a whole-row pitch
+    change whose dead cells the move must leave alone (buf.rs:257-313 skips padding)."""
+    rng = np.random.default_rng(2)
+    ax = dict(R=R, D=D)
+    S, Dm = fb.Mapping("[R, D]", ax), fb.Mapping("[R, D # 64]", ax)
+    x = rng.standard_normal(R * D).astype(np.float32)
+    X = be.from_vec(S, x, "f32")
+    Y = be.zeroed(Dm, "f32")
+
+    def step():
+        be.transpose(Y, X, S, Dm)
+        return Y
+
+    def parity(_rows=None, _b=None):
+        y = Y.to_numpy().reshape(R, 64)
+        same = bool(np.array_equal(y[:, :D], x.reshape(R, D)) and not y[:, D:].any())
+        return {"check": "live cells against the source, dead cells untouched", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    live = 4.0 * R * D
+    return dict(step=step, units=2.0 * live, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
+                cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
+                metric="padded-row relayout GB/s ([R, D] -> [R, D # 64] f32, D = 61)",
+                workload="relayout_padded_f32", dtype="f32", config={"R": R, "D": D, "bytes": "live read + live write"})
+
+
+def wl_elementwise(fb, be, n=64 << 20):
+    """A generated zip program (f32 a * b + a, 64 Mi elements: 768 MiB moved, well above L2)."""
+    rng = np.random.default_rng(3)
+    m = fb.Mapping("[E]", dict(E=n))
+    a = be.from_vec(m, rng.standard_normal(n).astype(np.float32), "f32")
+    b = be.from_vec(m, rng.standard_normal(n).astype(np.float32), "f32")
+    p_ = fb.ops.Prog(2)
+    prog = p_.build(p_.emit("ADDF", p_.emit("MULF", 0, 1), 0))
+    OUT = be.zeroed(m, "f32")
+    lib = fb._lib.lib()
+    ptrs = (C.c_void_p * 2)(a.addr, b.addr)
+    dts = (C.c_int32 * 2)(fb._lib.DTYPES["f32"], fb._lib.DTYPES["f32"])
+
+    def step():
+        fb._lib.check(lib.fopt_elementwise(be.ctx, C.byref(prog), 2, ptrs, dts, OUT.ptr, fb._lib.DTYPES["f32"], n),
+                      be.ctx)
+        return OUT
+
+    def parity(_rows=None, _b=None):
+        import oracle
+
+        k = 1 << 16
+        ga, gb = a.to_numpy()[:k], b.to_numpy()[:k]
+        want = oracle.elementwise([(32, 2, 0, 1, 0, 0), (30, 3, 2, 0, 0, 0)], 3, [ga.tobytes(), gb.tobytes()],
+                                  ["f32", "f32"], "f32", k)
+        same = OUT.to_bytes()[: 4 * k] == want
+        return {"check": f"first {k} elements against the oracle", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    return dict(step=step, units=12.0 * n, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
+                cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
+                metric="generated elementwise program GB/s (f32 a * b + a, 64 Mi elements)",
+                workload="elementwise_f32_zip", dtype="f32", config={"elements": n, "bytes": "2 reads + 1 write"})
+
+
 def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096, comm_ready=False):
     """Config 5: all-reduce of an 8x2048x4096 bf16 activation (N(0,1) per rank) over the Chip axis."""
     if world > 1 and not comm_ready:
@@ -636,13 +698,15 @@ def report(wl, meas, world, pk, args, int8_peak=None, cpu=True):
         out["e2e"] = {"value": round(world * wl["units"] / (e2e_ms * 1e-3) / wl["scale"], 2), "unit": wl["unit"],
                       "h2d_bytes_per_step": wl["h2d"], "d2h_bytes_per_step": wl["d2h"],
                       "ms_per_step": round(e2e_ms, 4), "api": wl.get("e2e_api", "")}
+    keep = {}
     if "cpu" in wl and world == 1 and cpu and not args.no_cpu:
-        keep = {}
         rate, sample = wl["cpu"](args.cpu_rows, keep)
-        out["cpu_baseline"] = {"value": round(rate / wl["scale"], 6), "unit": wl["unit"], "cores": os.cpu_count(),
-                               "kind": "port", "sample": sample}
-        if "parity" in wl and ("bytes" in keep or wl["workload"].startswith("relayout")):
-            out["parity"] = wl["parity"](args.cpu_rows, keep.get("bytes"))
+        if rate == rate:  # a sampled CPU baseline (NaN: none for this workload)
+            out["cpu_baseline"] = {"value": round(rate / wl["scale"], 6), "unit": wl["unit"],
+                                   "cores": os.cpu_count(), "kind": "port", "sample": sample}
+    if "parity" in wl and cpu and not args.no_cpu and (
+            "bytes" in keep or wl["workload"].startswith(("relayout", "elementwise"))):
+        out["parity"] = wl["parity"](args.cpu_rows, keep.get("bytes"))
     return out
 
 
@@ -711,7 +775,7 @@ def collective_report(fb, be, rank, world, stream, flush, args, local):
     return rep
 
 
-SUB_CONFIGS = ("gemm_bf16", "attention", "decoder", "mnist", "relayout")
+SUB_CONFIGS = ("gemm_bf16", "attention", "decoder", "mnist", "relayout", "relayout_padded", "elementwise")
 
 
 def run_ours(args, rank, world, local):
@@ -726,7 +790,8 @@ def run_ours(args, rank, world, local):
     make = {"gemm_i8": lambda: wl_gemm(fb, be, "i8"), "gemm_bf16": lambda: wl_gemm(fb, be, "bf16"),
             "attention": lambda: wl_attention(fb, be), "relayout": lambda: wl_relayout(fb, be),
             "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
-            "decoder": lambda: wl_decoder(fb, be),
+            "decoder": lambda: wl_decoder(fb, be), "relayout_padded": lambda: wl_relayout_padded(fb, be),
+            "elementwise": lambda: wl_elementwise(fb, be),
             "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}
     wl = make[args.workload]()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
