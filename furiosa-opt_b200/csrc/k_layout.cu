@@ -347,6 +347,43 @@ __global__ void relayout_walk64(T* __restrict__ dst, const T* __restrict__ src, 
   }
 }
 
+// ---- padded rows from a dense source: [rows, L] -> [rows, E # ...], E > L, 4-byte elements ----
+// A CTA stages kPadRows source rows (one contiguous run of kPadRows * L elements) in shared memory
+// with aligned 16-byte loads, so every source byte is read from DRAM once, then writes the live
+// cells of its destination rows one element per thread (a warp stores 128 contiguous bytes). Dead
+// cells are not touched, as the reference skips them.
+constexpr int kPadRows = 32;
+__global__ void __launch_bounds__(256) relayout_pad_rows(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
+                                                         int64_t rows, int L, int E, FastDiv e_div,
+                                                         int64_t src_base, int64_t dst_base, int64_t src_elems) {
+  extern __shared__ uint4 pad_buf4[];
+  uint32_t* buf = (uint32_t*)pad_buf4;
+  for (int64_t r0 = (int64_t)blockIdx.x * kPadRows; r0 < rows; r0 += (int64_t)gridDim.x * kPadRows) {
+    const int nr = (int)(rows - r0 < kPadRows ? rows - r0 : kPadRows);
+    const int64_t s0 = src_base + r0 * L, s1 = s0 + (int64_t)nr * L;  // elements [s0, s1)
+    const int64_t a0 = s0 & ~(int64_t)3;                                // aligned to 16 bytes
+    const int off = (int)(s0 - a0);
+    const int nvec = (int)((s1 - a0 + 3) >> 2);
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      const int64_t e = a0 + 4 * (int64_t)v;
+      if (e + 4 <= src_elems) {
+        pad_buf4[v] = *((const uint4*)src + (e >> 2));
+      } else {  // the source's last partial vector: element by element, inside the allocation
+#pragma unroll
+        for (int k = 0; k < 4; ++k) buf[4 * v + k] = e + k < src_elems ? src[e + k] : 0u;
+      }
+    }
+    __syncthreads();
+    const int total = nr * E;
+    uint32_t* drow = dst + dst_base + r0 * E;
+    for (int q = threadIdx.x; q < total; q += blockDim.x) {
+      const uint32_t i = fdiv(e_div, (uint32_t)q), c = (uint32_t)q - i * (uint32_t)E;
+      if ((int)c < L) drow[q] = buf[off + (int)i * L + (int)c];
+    }
+    __syncthreads();
+  }
+}
+
 // ---- rows path: a warp per row of the innermost wheel (partially live rows, e.g. padded widths) ----
 template <typename T>
 __global__ void relayout_rows(T* __restrict__ dst, const T* __restrict__ src, KWalk32 outer, uint32_t rows, uint32_t e0,
@@ -607,6 +644,25 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
                                                      src_base, dst_base, nt0, ntj, batches);
     launched(ctx, "relayout_tile");
     return;
+  }
+  // padded rows from a dense source (the shared-memory staged kernel above)
+  if constexpr (sizeof(T) == 4) {
+    const bool dense_rows = w.n == 2 && w.stride[0][0] == 1 && w.live[0] < w.extent[0] &&
+                            w.live[1] == w.extent[1] && w.stride[0][1] == w.live[0] && (uintptr_t)src % 16 == 0 &&
+                            w.extent[0] < (1 << 20) && w.extent[1] * w.extent[0] < (1ll << 40) &&
+                            !getenv("FOPT_RELAYOUT_NO_PADROWS");
+    if (dense_rows) {
+      const int64_t rows = w.extent[1];
+      const int L = (int)w.live[0], E = (int)w.extent[0];
+      const size_t sm = ((size_t)kPadRows * L + 8) * 4;
+      if (sm <= 48 * 1024) {
+        const int64_t blocks = std::min<int64_t>((rows + kPadRows - 1) / kPadRows, 148 * 16);
+        relayout_pad_rows<<<(int)blocks, 256, sm, st>>>((uint32_t*)d, (const uint32_t*)s, rows, L, E,
+                                                        make_fastdiv((uint32_t)E), src_base, dst_base, src_elems);
+        launched(ctx, "relayout_pad_rows");
+        return;
+      }
+    }
   }
   KWalk32 w32;
   if (w.n >= 2 && w.extent[0] >= 16 && to_kwalk32(w, w32) && p.positions < (1ll << 31)) {

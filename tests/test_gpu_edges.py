@@ -85,3 +85,38 @@ def test_reduce_degenerate_shapes(b200):
         got = b200.reduce(b200.from_vec(S, v, "i32"), "Add", 0, S, D).to_bytes()
         want = oracle.reduce(v.tobytes(), "i32", 0, 0, ref_m(src_e, **ax), ref_m(dst_e, **ax))
         assert got == want, src_e
+
+
+@pytest.mark.parametrize("dtype", ["f32", "i32"])
+@pytest.mark.parametrize("R,D,E", [(1000, 61, 64), (33, 7, 8), (4097, 100, 128)])
+def test_padded_rows_keep_dead_cells(b200, dtype, R, D, E):
+    """[R, D] -> [R, D # E] onto a canvas: live cells from the source, dead cells keep the canvas
+    (buf.rs:257-313 writes only live destination positions); ragged row counts."""
+    ax = dict(R=R, D=D)
+    S, Dm = fb.Mapping("[R, D]", ax), fb.Mapping(f"[R, D # {E}]", ax)
+    rng = np.random.default_rng(R + D)
+    x = rng.integers(-2 ** 31, 2 ** 31, R * D, dtype=np.int64).astype(np.int32)
+    canvas = rng.integers(-2 ** 31, 2 ** 31, R * E, dtype=np.int64).astype(np.int32)
+    if dtype == "f32":
+        x, canvas = x.view(np.float32), canvas.view(np.float32)
+    dst = b200.from_vec(Dm, canvas, dtype)
+    b200.transpose(dst, b200.from_vec(S, x, dtype), S, Dm)
+    got = np.frombuffer(dst.to_bytes(), np.int32).reshape(R, E)
+    want = canvas.view(np.int32).reshape(R, E).copy()
+    want[:, :D] = x.view(np.int32).reshape(R, D)
+    assert np.array_equal(got, want)
+
+
+def test_padded_rows_from_a_source_window(b200):
+    """The same move reading a window of a larger source (rows 5.. of [R2, D]): the staged kernel's
+    first aligned vector starts before the window."""
+    R2, R, D, E = 300, 200, 61, 64
+    base = fb.Mapping("[R, D]", dict(R=R2, D=D))
+    win = fb.Mapping("[R, D]", dict(R=R, D=D))
+    Dm = fb.Mapping(f"[R, D # {E}]", dict(R=R, D=D))
+    x = np.arange(R2 * D, dtype=np.int32)
+    dst = b200.zeroed(Dm, "i32")
+    b200.transpose(dst, b200.from_vec(base, x, "i32"), win, Dm, src_offset={"R": 5}, src_map=base)
+    got = dst.to_numpy().reshape(R, E)
+    assert np.array_equal(got[:, :D], x.reshape(R2, D)[5:5 + R])
+    assert not got[:, D:].any()
