@@ -404,3 +404,67 @@ def test_attention_two_chunks_scalar_reference(b200):
     print(f"attention two chunks: max abs err {diff.max():.3g} (test bound 0.12 + 0.12 |expected|)")
     assert np.all(diff <= 0.12 + 0.12 * np.abs(want.reshape(-1)))
     assert np.all(np.abs(mx.to_numpy() - want_max) < 0.1)
+
+
+# ---- reshape_tests.rs (src/reshape.rs): a relabel of the DM layout across chip / cluster / slice ---
+@pytest.mark.parametrize("variant", ["seven_axes", "four_axes"])
+def test_reshape(b200, variant):
+    ax = dict(A=256, B=4096)
+    host = M("[A, B]", **ax)
+    hbm_map = M("[A / 4 % 4, A / 16, A % 4, B]", **ax)
+    hbm2_map = M("[A / 4 % 4, A % 4, B, A / 16]", **ax)
+    dm_map = M("[A / 4 % 4, A / 2 % 2, B % 16, B / 16 % 16, B / 256, A % 2, A / 16]", **ax)
+    t = b200.to_hbm(np.arange(256 * 4096, dtype=np.int32), host, "i32", hbm_map)
+    t = b200.relayout(t, hbm_map, hbm2_map)
+    dm = b200.relayout(t, hbm2_map, dm_map)
+    if variant == "seven_axes":
+        ax2 = dict(C=4, D=2, E=16, F=16, G=16, H=2, I=16)
+        out_map = M("[C, D, E, F, G, H, I]", **ax2)
+    else:
+        ax2 = dict(C=4, D=2, E=256, F=512)
+        out_map = M("[C, D, E, F]", **ax2)
+    reshaped = b200.reshape(dm, dm_map, out_map)      # `unsafe { dm_tensor.reshape() }`: wire order kept
+    got = reshaped.to_numpy()
+    x = np.arange(256 * 4096, dtype=np.int64)
+    a4 = x // (2 * 16 * 16 * 16 * 2 * 16)
+    a2 = x % (2 * 16 * 16 * 16 * 2 * 16) // (16 * 16 * 16 * 2 * 16)
+    b1 = x % (16 * 16 * 16 * 2 * 16) // (16 * 16 * 2 * 16)
+    b16 = x % (16 * 16 * 2 * 16) // (16 * 2 * 16)
+    b256 = x % (16 * 2 * 16) // (2 * 16)
+    a1 = x % (2 * 16) // 16
+    a16 = x % 16
+    want = (a16 * 16 + a4 * 4 + a2 * 2 + a1) * 4096 + (b256 * 256 + b16 * 16 + b1)
+    assert np.array_equal(got, want.astype(np.int32))
+
+
+# ---- memset_tests.rs (src/memset.rs): a whole-region fill, then a DM relayout that reads it ------
+MEMSETS = [("i32", 0, np.int32), ("i8", -1, np.int8), ("i16", 300, np.int16), ("f32", 1.5, np.float32),
+           ("bf16", 1.0, None), ("f8e4m3", 1.0, None), ("i4", -1, np.int8), ("bf16", 3.0, None)]
+
+
+@pytest.mark.parametrize("case", range(len(MEMSETS)))
+def test_memset(b200, case):
+    dt, value, npdt = MEMSETS[case]
+    ax = dict(A=256, B=128)
+    hbm, dm = M("[A, B]", **ax), M("[1 # 2, A, B]", **ax)          # Dm<D>: cluster m![1 # 2], slice [A], [B]
+    relaid = M("[1 # 2, 1 # 2, A / 2, A % 2, B]", **ax)             # Relaid<D>
+    out_map = M("[A / 2, A % 2, B]", **ax)
+    n = 256 * 128
+    rng = np.random.default_rng(case)
+    if dt == "bf16":
+        inp, fill = dtypes.f32_to_bf16_bits(rng.uniform(2, 100, n).astype(np.float32)), dtypes.f32_to_bf16_bits(
+            np.array([value], np.float32))[0]
+    elif dt == "f8e4m3":
+        inp = oracle.f8_convert("f32_to_f8e4m3", np.full(n, 2.0, np.float32).view(np.uint32)).astype(np.uint8)
+        fill = int(oracle.f8_convert("f32_to_f8e4m3", np.array([value], np.float32).view(np.uint32))[0])
+    elif dt == "i4":
+        inp, fill = (np.arange(n) % 7).astype(np.int8), np.int8(value)
+    else:
+        inp, fill = (np.arange(n) % 50 + 1).astype(npdt), npdt(value)
+    store_dt = np.uint8 if dt == "f8e4m3" else (np.uint16 if dt == "bf16" else np.asarray(inp).dtype)
+    d = b200.relayout(b200.from_vec(hbm, inp, dt), hbm, dm)                  # to_dm
+    splat = b200.from_vec(dm, np.full(dm.size, fill, dtype=store_dt), dt)    # Tensor::splat(value)
+    b200.transpose(d, splat, dm, dm, allow_broadcast=True)                    # memset: fill the live cells
+    r = b200.relayout(d, dm, relaid)                                          # dm.to_dm(): reads the fill
+    got = b200.from_hbm(b200.relayout(r, relaid, out_map), out_map, dt)       # to_hbm, to_host
+    assert np.array_equal(got, np.full(n, fill, dtype=store_dt)), dt
