@@ -468,3 +468,133 @@ def test_memset(b200, case):
     r = b200.relayout(d, dm, relaid)                                          # dm.to_dm(): reads the fill
     got = b200.from_hbm(b200.relayout(r, relaid, out_map), out_map, dt)       # to_hbm, to_host
     assert np.array_equal(got, np.full(n, fill, dtype=store_dt)), dt
+
+
+# ---- fetch_commit_tests.rs (src/fetch_commit.rs): i8 [A, B] -> fetch_cast i32 -> [B, A] -----------
+def test_fetch_commit_simple(b200):
+    ax = dict(A=4096, B=8)
+    hbm = M("[A, B]", **ax)
+    dm = M("[1 # 2, A / 16, A / 8 % 2, A % 8, B]", **ax)          # Cluster m![1 # 2], [A / 16], [A/8%2, A%8, B]
+    x = (np.arange(32768) % 256).astype(np.uint8).view(np.int8)   # (0..32768) as i8
+    d = b200.relayout(b200.from_vec(hbm, x, "i8"), hbm, dm)
+    c = b200.map(d, ops.cast("i8", "i32"), "i32")                 # fetch_cast::<i32>, collect, commit
+    out = b200.relayout(c, dm, M("[B, A]", **ax))                 # to_hbm::<m![B, A]>
+    a, b = np.meshgrid(np.arange(4096), np.arange(8))            # out[b, a] = ((a * 8 + b) as i8) as i32
+    want = ((a * 8 + b) % 256).astype(np.uint8).view(np.int8).astype(np.int32).reshape(-1)
+    assert np.array_equal(out.to_numpy(), want)
+
+
+# ---- view_tests.rs (src/view.rs): three tile moves rotate each row of B by two -------------------
+def test_view_simpl(b200):
+    ax = dict(A=512, B=8)
+    hbm, dm = M("[A, B]", **ax), M("[A / 256, A % 256, B]", **ax)
+    inp = b200.relayout(b200.from_vec(hbm, np.arange(4096, dtype=np.int32), "i32"), hbm, dm)
+    out = b200.zeroed(dm, "i32")
+    for size, s, d in ((4, 0, 2), (2, 4, 6), (2, 6, 0)):
+        b200.transpose(out, inp, M(f"[A / 256, A % 256, B = {size} # 8]", **ax),
+                       M(f"[A / 256, A % 256, B = {size} #{{!}} 8]", **ax), src_offset={"B": s}, dst_offset={"B": d},
+                       src_map=dm, dst_map=dm)
+    got = b200.relayout(out, dm, hbm).to_numpy()
+    want = np.array([8 * a + i for a in range(512) for i in (6, 7, 0, 1, 2, 3, 4, 5)], np.int32)
+    assert np.array_equal(got, want)
+
+
+def test_view_nested(b200):
+    """view_nested (view.rs:41-67): a full copy, then a nested tile (132 of 264 of 528) copied onto
+    itself; the output equals the input."""
+    ax = dict(A=512, B=528)
+    hbm, dm = M("[A, B]", **ax), M("[A / 256, A % 256, B]", **ax)
+    x = np.random.default_rng(5).integers(-2**31, 2**31 - 1, 512 * 528).astype(np.int32)
+    inp = b200.relayout(b200.from_vec(hbm, x, "i32"), hbm, dm)
+    out = b200.zeroed(dm, "i32")
+    b200.transpose(out, inp, dm, dm)
+    b200.transpose(out, inp, M("[A / 256, A % 256, B = 132 # 528]", **ax),
+                   M("[A / 256, A % 256, B = 132 #{!} 528]", **ax), src_offset={"B": 0}, dst_offset={"B": 0},
+                   src_map=dm, dst_map=dm)
+    assert np.array_equal(b200.relayout(out, dm, hbm).to_numpy(), x)
+
+
+# ---- param_tests.rs (src/param.rs): a tuple / struct parameter passes through DM unchanged --------
+def test_param_passthrough(b200):
+    ax = dict(A=4096, B=8)
+    hbm, dm = M("[A, B]", **ax), M("[1 # 2, A / 16, A / 8 % 2, A % 8, B]", **ax)
+    x = (np.arange(32768) % 256).astype(np.uint8).view(np.int8)
+    out = b200.relayout(b200.relayout(b200.from_vec(hbm, x, "i8"), hbm, dm), dm, hbm)
+    assert np.array_equal(out.to_numpy(), x)
+
+
+# ---- runtime_if_tests.rs (src/runtime_if.rs): the two arms write input + 1 and input + 2 ---------
+def test_runtime_if_two_outputs(b200):
+    ax = dict(W=1024)
+    hbm, dm = M("[W]", **ax), M("[1, W / 4, W % 4]", **ax)        # Cluster m![1], Slice [W / 4], [W % 4]
+    collect = M("[1, W / 4, W % 4 # 8]", **ax)                     # collect::<m![1], m![W % 4 # 8]>
+    x = np.arange(1024, dtype=np.int32)
+    d = b200.relayout(b200.from_vec(hbm, x, "i32"), hbm, dm)
+    outs = []
+    for c in (1, 2):                                              # if i == 0 { +1 } else { +2 }
+        v = b200.map(b200.relayout(d, dm, collect), ops.with_const_i32(ops.FXP_BINARY, "AddFxp", c), "i32")
+        view = b200.zeroed(dm, "i32")
+        b200.transpose(view, v, collect, dm)                      # commit_trim::<m![W % 4]>, commit_view
+        outs.append(b200.relayout(view, dm, hbm).to_numpy())
+    assert np.array_equal(outs[0], x + 1) and np.array_equal(outs[1], x + 2)
+
+
+# ---- runtime_if_scalar_tests.rs (src/runtime_if_scalar.rs): a runtime tile index copies both halves
+def test_runtime_if_scalar_index(b200):
+    ax = dict(A=512, B=32)
+    hbm, dm = M("[A, B]", **ax), M("[A / 256, A % 256, B]", **ax)
+    x = (np.arange(512 * 32) % 256).astype(np.uint8).view(np.int8)
+    inp = b200.relayout(b200.from_vec(hbm, x, "i8"), hbm, dm)
+    out = b200.zeroed(dm, "i8")
+    for i in range(2):
+        off = 0 if i == 0 else 16
+        b200.transpose(out, inp, M("[A / 256, A % 256, B = 16 # 32]", **ax),
+                       M("[A / 256, A % 256, B = 16 #{!} 32]", **ax), src_offset={"B": off}, dst_offset={"B": off},
+                       src_map=dm, dst_map=dm)
+    assert np.array_equal(b200.relayout(out, dm, hbm).to_numpy(), x)
+
+
+# ---- host_tile_view_tests.rs (src/host_tile_view.rs): move one row of a table to another ---------
+@pytest.mark.parametrize("moves", [[(3, 5)], [(0, 63), (32, 32), (63, 0), (3, 5)]])
+def test_host_tile_move(b200, moves):
+    ax = dict(C=64, H=64)
+    base = M("[C, H]", **ax)
+    table = dtypes.f32_to_bf16_bits(np.repeat(np.arange(64, dtype=np.float32), 64))   # row r holds r
+    src = b200.from_vec(base, table, "bf16")
+    out = b200.from_vec(base, dtypes.f32_to_bf16_bits(np.full(64 * 64, -1.0, np.float32)), "bf16")
+    for s, d in moves:                                            # tile::<m![C], 1, SmallRow(Mut)>(row)
+        b200.transpose(out, src, M("[1 # 64, H]", **ax), M("[1 #{!} 64, H]", **ax), src_offset={"C": s},
+                       dst_offset={"C": d}, src_map=base, dst_map=base)
+    got = dtypes.bf16_bits_to_f32(out.to_numpy()).reshape(64, 64)
+    for r in range(64):
+        want = next((float(s) for s, d in moves if d == r), -1.0)
+        assert np.all(got[r] == want), f"row {r}"
+
+
+# ---- memory_op_tests.rs (src/memory_op.rs) --------------------------------------------------------
+def test_dm_relayout(b200):
+    """dm_relayout: [A, B] -> DM [1 # 2, A, B] -> DM [1 # 2, 1 # 2, A / 2, A % 2, B] -> HBM
+    [A / 2, A % 2, B], whose order is the input's (the example's test only runs it)."""
+    ax = dict(A=256, B=4096)
+    hbm = M("[A, B]", **ax)
+    dm, relaid = M("[1 # 2, A, B]", **ax), M("[1 # 2, 1 # 2, A / 2, A % 2, B]", **ax)
+    out_map = M("[A / 2, A % 2, B]", **ax)
+    x = np.arange(256 * 4096, dtype=np.int32)
+    r = b200.relayout(b200.relayout(b200.from_vec(hbm, x, "i32"), hbm, dm), dm, relaid)
+    assert np.array_equal(b200.relayout(r, relaid, out_map).to_numpy(), x)
+
+
+def test_commit_view_bottom_pad(b200):
+    """commit_view_bottom_pad: an 8-wide [T, Q % 56 = 8] tensor committed into the first 8 of 56
+    columns of a [T % 32, Q % 56] DM tile; the other 48 columns stay unwritten."""
+    ax = dict(T=512, Q=896)
+    hin = M("[T, Q % 56 = 8]", **ax)
+    din = M("[1 # 2, T / 32 # 256, T % 32, Q % 56 = 8]", **ax)
+    dres = M("[1 # 2, T / 32 # 256, T % 32, Q % 56]", **ax)
+    x = np.random.default_rng(42).random(512 * 8).astype(np.float32)
+    d = b200.relayout(b200.from_vec(hin, x, "f32"), hin, din)
+    res = b200.zeroed(dres, "f32")
+    b200.transpose(res, d, din, M("[1 # 2, T / 32 # 256, T % 32, Q % 56 = 8 #{!} 56]", **ax),
+                   src_offset={}, dst_offset={"Q": 0}, src_map=din, dst_map=dres)
+    got = b200.relayout(res, dres, M("[T, Q % 56]", **ax)).to_numpy().reshape(512, 56)
+    assert np.array_equal(got[:, :8], x.reshape(512, 8)) and np.all(got[:, 8:] == 0)
