@@ -58,6 +58,7 @@ struct Jit {
   CUresult (*get_fn)(CUfunction*, CUmodule, const char*) = nullptr;
   CUresult (*launch)(CUfunction, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, unsigned, CUstream,
                      void**, void**) = nullptr;
+  CUresult (*set_attr)(CUfunction, int, int) = nullptr;
 };
 
 template <typename T>
@@ -88,7 +89,7 @@ Jit& jit() {
     SYM(destroy, "nvrtcDestroyProgram");
 #undef SYM
     bool drv = driver_sym("cuModuleLoadData", &j.load) && driver_sym("cuModuleGetFunction", &j.get_fn) &&
-               driver_sym("cuLaunchKernel", &j.launch);
+               driver_sym("cuLaunchKernel", &j.launch) && driver_sym("cuFuncSetAttribute", &j.set_attr);
     j.ok = drv && j.create && j.compile && j.cubin_size && j.cubin && j.destroy;
   });
   return j;
@@ -559,8 +560,15 @@ struct RowLayout {
   unsigned keep_raw = 0, later_leaves = 0, held_leaves = 0;
   std::vector<int> pass_slot;  // FOLD slot index per pass, -1 for the final program
   bool unrolled = false;       // slots and groups unrolled (held values in registers)
+  int held_reg_groups = 0;     // groups g = i * KC + kc < this hold their values in registers, the rest in shared memory
+  size_t held_smem = 0;        // dynamic shared memory bytes of the held values kept there
   bool ok = false;
 };
+
+// Registers a thread gives to held values before the rest go to shared memory (FOPT_ROW_HELD_REGS
+// overrides). SwiGLU + quantise over 14336-wide rows: all 56 in registers holds 2 rows per SM
+// (161 us at 4096 rows); 8 registers and 48 KB of shared memory per row hold 4 (112 us).
+constexpr int kHeldRegWords = 8;
 
 RowLayout row_layout(const fopt_row_plan& P) {
   RowLayout L;
@@ -593,6 +601,18 @@ RowLayout row_layout(const fopt_row_plan& P) {
   // enough warps to hide latency: about 48 a SM over the 148 SMs
   while (L.tpr < 256 && P.rows * (L.tpr / 32) < 148 * 48) L.tpr *= 2;
   L.spt = 256 / L.tpr;
+  // Held values beyond a register budget go to shared memory ([group][element][thread], one bank
+  // per lane): a row's activation then takes fewer registers and more rows stay resident per SM.
+  const int groups = L.spt * L.KC;
+  L.held_reg_groups = groups;
+  if (L.unrolled && nH > 0) {
+    static const int budget = [] {
+      const char* e = getenv("FOPT_ROW_HELD_REGS");
+      return e ? atoi(e) : kHeldRegWords;
+    }();
+    L.held_reg_groups = std::min(groups, budget / (nH * 8));
+    L.held_smem = (size_t)(groups - L.held_reg_groups) * nH * 8 * 256 * sizeof(unsigned);
+  }
   L.ok = true;
   return L;
 }
@@ -619,7 +639,7 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
   o << "struct RowArgs { const void* in[8]; long long b[8]; const void* ld[8]; void* so[8]; void* out; long long rows; };\n"
     << "extern \"C\" __global__ void __launch_bounds__(256) fopt_row_gen(const RowArgs a) {\n"
     << "  constexpr long long RL = " << W << "LL;\n  constexpr int KC = " << KC << ", SPT = " << SPT
-    << ", NW = " << NW << ", RPC = " << RPC << ";\n"
+    << ", NW = " << NW << ", RPC = " << RPC << ", NR = " << L.held_reg_groups << ";\n  (void)NR;\n"
     << "  __shared__ unsigned part[" << std::max<size_t>(1, L.pass_slot.size() - 1) << "][RPC][8];\n"
     << "  const int t = threadIdx.x % " << TPR << ", rr = threadIdx.x / " << TPR
     << ", lane = t & 31, w = t >> 5;\n  (void)lane; (void)w; (void)rr;\n"
@@ -632,10 +652,22 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
   for (int k = 0; k < nL; ++k)
     if (L.keep_raw >> k & 1) o << "    unsigned raw" << k << "[SPT][KC][" << raw_words(P.leaf_dtype[k]) << "];\n";
   for (int h = 0; h < nH; ++h) o << "    unsigned hv" << h << "[SPT][KC][8];\n";
+  if (L.held_smem) {
+    o << "    extern __shared__ unsigned held_smem[];\n";
+    for (int h = 0; h < nH; ++h)
+      o << "    unsigned* const hs" << h << " = held_smem + " << h << " * (SPT * KC - NR) * 2048 + threadIdx.x;\n";
+  }
   for (int j = 0; j < nS; ++j) o << "    unsigned s" << j << " = 0u;\n";
   std::string names[16];
   for (int k = 0; k < nL; ++k) names[k] = "x" + std::to_string(k) + "[e]";
-  for (int h = 0; h < nH; ++h) names[nL + h] = "hv" + std::to_string(h) + "[i][kc][e]";
+  // group g = i * KC + kc is a compile-time constant once the loops unroll, so each read and write
+  // below resolves to a register or to a shared-memory word
+  auto held_at = [&](int h) {
+    const std::string hs = std::to_string(h);
+    if (!L.held_smem) return "hv" + hs + "[i][kc][e]";
+    return "(i * KC + kc < NR ? hv" + hs + "[i][kc][e] : hs" + hs + "[((i * KC + kc < NR) ? 0 : i * KC + kc - NR) * 2048 + e * 256])";
+  };
+  for (int h = 0; h < nH; ++h) names[nL + h] = held_at(h);
   for (int j = 0; j < nS; ++j) names[nL + nH + j] = "s" + std::to_string(j);
   std::string snames[16];
   for (int j = 0; j < nS; ++j) snames[j] = "s" + std::to_string(j);
@@ -684,7 +716,12 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
       for (int h = 0; h < nH; ++h) {
         std::string ret;
         if (!emit_program_vec(o, *P.held[h], names, nL, &ret, "h" + std::to_string(h) + "_")) return false;
-        o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) hv" << h << "[i][kc][e] = " << ret << ";\n";
+        if (!L.held_smem)
+          o << "#pragma unroll\n      for (int e = 0; e < 8; ++e) hv" << h << "[i][kc][e] = " << ret << ";\n";
+        else
+          o << "      if (i * KC + kc < NR) {\n#pragma unroll\n      for (int e = 0; e < 8; ++e) hv" << h << "[i][kc][e] = "
+            << ret << ";\n      } else {\n#pragma unroll\n      for (int e = 0; e < 8; ++e) hs" << h
+            << "[(i * KC + kc - NR) * 2048 + e * 256] = " << ret << ";\n      }\n";
       }
     }
     std::string ret;
@@ -934,9 +971,13 @@ bool launch_row_jit(fopt_ctx* ctx, const fopt_row_plan& P) {
   args.out = P.out;
   args.rows = P.rows;
   void* params[] = {(void*)&args};
-  const int rpc = 256 / row_layout(P).tpr;
+  const RowLayout L = row_layout(P);
+  const int rpc = 256 / L.tpr;
   const unsigned grid = (unsigned)std::min<int64_t>((P.rows + rpc - 1) / rpc, 1 << 30);
-  CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, 0, (CUstream)ctx->stream, params, nullptr);
+  if (L.held_smem &&
+      jit().set_attr(fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, (int)L.held_smem) != CUDA_SUCCESS)
+    throw Fail{FOPT_ERR_CUDA, "row program shared memory attribute refused"};
+  CUresult r = jit().launch(fn, grid, 1, 1, 256, 1, 1, (unsigned)L.held_smem, (CUstream)ctx->stream, params, nullptr);
   if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "row program launch failed"};
   ctx->launches++;
   g_jit_launches.fetch_add(1, std::memory_order_relaxed);
