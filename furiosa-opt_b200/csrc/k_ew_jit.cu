@@ -645,8 +645,10 @@ std::string generate_row(const fopt_row_plan& P, const int* folds) {
     << ", lane = t & 31, w = t >> 5;\n  (void)lane; (void)w; (void)rr;\n"
     << "  void* const out = a.out;\n  (void)out;\n";
   for (int k = 0; k < nL; ++k)
-    o << "  const void* const in" << k << " = a.in[" << k << "]; const long long b" << k << " = a.b[" << k
-      << "]; (void)b" << k << ";\n";
+    // the broadcast divisor is part of the kernel's key, so it is a constant here (a power of two
+    // becomes a shift or a mask instead of a 64-bit division per group)
+    o << "  const void* const in" << k << " = a.in[" << k << "]; constexpr long long b" << k << " = "
+      << (P.leaf_bcast[k] < 0 ? -P.leaf_bcast[k] : P.leaf_bcast[k]) << "LL; (void)b" << k << ";\n";
   o << "  for (long long row0 = (long long)blockIdx.x * RPC; row0 < a.rows; row0 += (long long)gridDim.x * RPC) {\n"
     << "    const long long row = row0 + rr;\n    const bool live = row < a.rows;\n";
   for (int k = 0; k < nL; ++k)
@@ -799,7 +801,7 @@ std::string row_key(const fopt_row_plan& P, const int* folds) {
   };
   std::string key = "row|" + std::to_string(P.row_len) + "|" + std::to_string(P.out_dtype) + "|";
   for (int k = 0; k < P.n_leaves; ++k)
-    key += std::to_string(P.leaf_dtype[k]) + "/" + std::to_string(P.leaf_bcast[k] == 0 ? 0 : P.leaf_bcast[k] > 0 ? 1 : 2) + ",";
+    key += std::to_string(P.leaf_dtype[k]) + "/" + std::to_string(P.leaf_bcast[k]) + ",";
   key += "|";
   for (int h = 0; h < P.n_held; ++h) key += prog_bytes(P.held[h]) + "#";
   key += "|";
