@@ -87,15 +87,18 @@ __host__ __device__ inline uint32_t f32_to_bf16w(uint32_t x) {
 #ifdef __CUDACC__
 // Two f32 -> packed bf16x2 under the reference's rule (float/bf16.rs): one round-to-nearest-even
 // conversion instruction, which agrees with the rule except on f32 subnormals (the rule flushes them
-// to signed zero) and NaN (the rule returns 0x7fc0). Those inputs, an exponent field of 0 or 255, take
-// the bit-level path; zeros and infinities land there too and convert the same either way.
+// to signed zero) and NaN (the rule returns 0x7fc0); selects on each half's exponent field put those
+// two classes right without a branch (a branch to the bit-level rule cost an epilogue about as much as
+// its stores).
 __device__ __forceinline__ uint32_t bf16x2_rule(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
-  if (((((a >> 23) + 1) & 0xfeu) == 0) | ((((b >> 23) + 1) & 0xfeu) == 0))
-    r = (f32_to_bf16w(a) >> 16) | (f32_to_bf16w(b) & 0xffff0000u);
-  return r;
+  uint32_t l = (a & 0x7f800000u) ? (r & 0xffffu) : ((a >> 16) & 0x8000u);
+  l = (a & 0x7fffffffu) > 0x7f800000u ? 0x7fc0u : l;
+  uint32_t h = (b & 0x7f800000u) ? (r & 0xffff0000u) : (b & 0x80000000u);
+  h = (b & 0x7fffffffu) > 0x7f800000u ? 0x7fc00000u : h;
+  return l | h;
 }
 #endif
 
