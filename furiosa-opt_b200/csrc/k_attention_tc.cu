@@ -763,6 +763,392 @@ __global__ void __launch_bounds__(THREADS2, 1)
 }
 
 
+// ---------------------------------------------------------------------------------------------
+// Persistent kernel: one query tile at a time per CTA, S and O double-buffered in tensor memory,
+// each row's softmax split over two threads.
+//
+// One CTA per SM. CTA c takes the query tiles c, 2G - 1 - c, 2G + c, ... of the longest-first
+// order (G CTAs, the tile list walked back and forth so that every CTA gets about the same number
+// of key blocks). The key blocks of all of a CTA's tiles form one sequence g = 0, 1, 2, ...: S(g)
+// goes to S buffer g % 2, and the K / V ring, the S buffers and their barriers run on g across
+// tile boundaries, so the next tile's first QK^T runs while this tile finishes. 352 threads:
+//   warp 0     TMA producer of Q (per tile, once the previous tile's last S has read the Q buffer)
+//              and of K tiles into a 3-stage ring; warp 10 produces V tiles into a 2-stage ring;
+//   warp 1     TMEM owner and MMA issuer, in the order S(0) S(1) | PV(g) S(g + 2) ...; PV of tile
+//              t accumulates into O buffer t % 2, after the epilogue of tile t - 2 has read it;
+//   warps 2-9  softmax: warp w reads TMEM lanes 32 (w % 4) .. + 31 (rows), warps 2-5 columns 0-63
+//              and warps 6-9 columns 64-127 of each score row. The two threads of a row exchange
+//              their partial maxima through shared memory (a 64-thread named barrier per lane
+//              quarter), keep their own running sums, and write their 32 packed bf16 probability
+//              words over the first 64 columns of the row's S buffer; PV reads P from there. At the
+//              end of a tile they normalise the O row and store it (128 bytes per thread).
+// TMEM columns: O [0, 128), S buffers [128, 256) and [256, 384), Q buffers [384, 448) and [448, 512).
+// Q is the QK^T's A operand in tensor memory: with both operands in shared memory the 128 x 128
+// MMA steps were bound by shared-memory reads (about 140 cycles each against about 95 with A in
+// tensor memory).
+// ---------------------------------------------------------------------------------------------
+constexpr int THREADS3 = 352;
+constexpr int KST3 = 3, VST3 = 2;  // K and V ring depths
+
+
+__device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+// The k-th query tile of CTA c among `total` (longest first), or -1.
+__device__ __forceinline__ int tile_of(int k, int c, int G, int total) {
+  const int i = k * G + ((k & 1) ? G - 1 - c : c);
+  return i < total ? i : -1;
+}
+
+__global__ void __launch_bounds__(THREADS3, 1)
+    attention_tc3_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO, Params p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;                   // 32 KiB
+  uint8_t* sKr = smem + TILE;           // KST3 K tiles
+  uint8_t* sVr = sKr + KST3 * TILE;     // VST3 V tiles
+  float* xch = (float*)(sVr + VST3 * TILE);  // [2 parities][2 halves][128 rows]
+  float* xl = xch + 2 * 2 * BQ;                                // [2 halves][128 rows] row sums
+  uint64_t* bars = (uint64_t*)(xl + 2 * BQ);
+  uint64_t* q_full = bars;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
+  uint64_t* k_empty = k_full + KST3;
+  uint64_t* v_full = k_empty + KST3;
+  uint64_t* v_empty = v_full + VST3;
+  uint64_t* s_full = v_empty + VST3;  // [2] per S buffer
+  uint64_t* p_ready = s_full + 2;        // [2] per S buffer
+  uint64_t* pv_done = p_ready + 2;       // [2] PV(g) completes pv_done[g % 2]
+  uint64_t* o_free = pv_done + 2;        // the epilogue has read O
+  uint64_t* q_tm = o_free + 1;           // [2] per TMEM Q buffer: the softmax threads have written it
+  uint32_t* tmem_slot = (uint32_t*)(q_tm + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = p.S / BQ, BH = p.B * p.Hq, total = BH * nq, G = (int)gridDim.x, c = (int)blockIdx.x;
+  auto tile_geo = [&](int idx, int& b, int& h, int& qb, int& last) {
+    const int bh = idx % BH;
+    qb = nq - 1 - idx / BH;
+    h = bh % p.Hq;
+    b = bh / p.Hq;
+    last = p.causal ? qb : p.S / BK - 1;
+  };
+  uint64_t* tr = p.trace ? p.trace + (int64_t)blockIdx.x * 128 : nullptr;  // diagnostics (FOPT_ATTN_TRACE)
+  if (tr && threadIdx.x == 0) tr[0] = gtimer();
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(q_full), 1);
+    mbar_init(smem_u32(q_empty), 256);
+    mbar_init(smem_u32(o_free), 256);
+    for (int s = 0; s < KST3; ++s) {
+      mbar_init(smem_u32(&k_full[s]), 1);
+      mbar_init(smem_u32(&k_empty[s]), 1);
+    }
+    for (int s = 0; s < VST3; ++s) {
+      mbar_init(smem_u32(&v_full[s]), 1);
+      mbar_init(smem_u32(&v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&s_full[t]), 1);
+      mbar_init(smem_u32(&p_ready[t]), 256);
+      mbar_init(smem_u32(&pv_done[t]), 1);
+      mbar_init(smem_u32(&q_tm[t]), 256);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int k = 0, idx; ok && (idx = tile_of(k, c, G, total)) >= 0; ++k) {
+        int b, h, qb, last;
+        tile_geo(idx, b, h, qb, last);
+        const int hk = h / (p.Hq / p.Hkv), row0 = b * p.S;
+        // the previous tile's last S has read the Q buffer
+        if (k > 0 && !(ok = mbar_wait(smem_u32(q_empty), (k - 1) & 1, abort_flag, p.err, 341))) break;
+        const uint32_t qf = smem_u32(q_full);
+        mbar_expect_tx(qf, TILE);
+        tma3(smem_u32(sQ), &tmQ, qf, 0, h, row0 + qb * BQ);
+        tma3(smem_u32(sQ + CHUNK), &tmQ, qf, 64, h, row0 + qb * BQ);
+        for (int j = 0; j <= last; ++j, ++g) {
+          const int st = g % KST3;
+          const uint32_t ph = ((g / KST3) & 1) ^ 1;
+          uint8_t* sK = sKr + st * TILE;
+          if (!(ok = mbar_wait(smem_u32(&k_empty[st]), ph, abort_flag, p.err, 331))) break;
+          const uint32_t kb = smem_u32(&k_full[st]);
+          mbar_expect_tx(kb, TILE);
+          tma3(smem_u32(sK), &tmK, kb, 0, hk, row0 + j * BK);
+          tma3(smem_u32(sK + CHUNK), &tmK, kb, 64, hk, row0 + j * BK);
+        }
+      }
+    }
+  } else if (warp == 10) {
+    // V producer: V tiles free up only after their PV, so they run on their own thread and the K
+    // loads above are never held behind them
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int k = 0, idx; ok && (idx = tile_of(k, c, G, total)) >= 0; ++k) {
+        int b, h, qb, last;
+        tile_geo(idx, b, h, qb, last);
+        const int hk = h / (p.Hq / p.Hkv), row0 = b * p.S;
+        for (int j = 0; j <= last; ++j, ++g) {
+          const int st = g % VST3;
+          const uint32_t ph = ((g / VST3) & 1) ^ 1;
+          uint8_t* sV = sVr + st * TILE;
+          if (!(ok = mbar_wait(smem_u32(&v_empty[st]), ph, abort_flag, p.err, 332))) break;
+          const uint32_t vb = smem_u32(&v_full[st]);
+          mbar_expect_tx(vb, TILE);
+          tma3(smem_u32(sV), &tmV, vb, 0, hk, row0 + j * BK);
+          tma3(smem_u32(sV + CHUNK), &tmV, vb, 64, hk, row0 + j * BK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                             ((uint32_t)(128 >> 4) << 24);
+      // The global block sequence: block g belongs to tile tk[g], is key block jg[g] of it; the
+      // issuer walks it with two cursors (the next S to issue runs two blocks ahead of the PV).
+      struct Cursor {
+        int k = 0, idx = -1, j = 0, last = -1, g = 0;
+      };
+      const int G_ = G, c_ = c, total_ = total;
+      auto first = [&](Cursor& u) {
+        u.k = 0;
+        u.g = 0;
+        u.j = 0;
+        u.idx = tile_of(0, c_, G_, total_);
+        if (u.idx >= 0) {
+          int b, h, qb;
+          tile_geo(u.idx, b, h, qb, u.last);
+        }
+      };
+      auto next = [&](Cursor& u) {
+        ++u.g;
+        if (++u.j > u.last) {
+          u.j = 0;
+          ++u.k;
+          u.idx = tile_of(u.k, c_, G_, total_);
+          if (u.idx >= 0) {
+            int b, h, qb;
+            tile_geo(u.idx, b, h, qb, u.last);
+          }
+        }
+      };
+      bool ok = true;
+      // S(g) = Q K^T into buffer g % 2; the first S of a tile waits for its Q, the last releases Q
+      auto issue_s = [&](const Cursor& u) -> bool {
+        if (u.j == 0 && !mbar_wait(smem_u32(&q_tm[u.k & 1]), (u.k >> 1) & 1, abort_flag, p.err, 333)) return false;
+        if (!mbar_wait(smem_u32(&k_full[u.g % KST3]), (u.g / KST3) & 1, abort_flag, p.err, 334)) return false;
+        fence_after();
+        // descriptors of the tile bases; a k-step adds its offset (in 16-byte units) to the start
+        // address field, which stays below 2^14 units for any shared-memory address
+        const uint64_t kd = sdesc(smem_u32(sKr + (u.g % KST3) * TILE));
+        const uint32_t dS = tmem + 128 + (u.g & 1) * 128, qa = tmem + 384 + (u.k & 1) * 64;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32) >> 4;
+          mma_bf16_ta(dS, qa + 8 * k, kd + off, idesc, k != 0);
+        }
+        commit(smem_u32(&s_full[u.g & 1]));
+        commit(smem_u32(&k_empty[u.g % KST3]));
+        return true;
+      };
+      Cursor sc, pc;
+      first(sc);
+      first(pc);
+      for (int i = 0; ok && i < 2 && sc.idx >= 0; ++i) {
+        ok = issue_s(sc);
+        next(sc);
+      }
+      for (; ok && pc.idx >= 0; next(pc)) {
+        const int g = pc.g;
+        // PV of a tile's first block overwrites O: the previous tile's epilogue has read it
+        if (pc.j == 0 && pc.k >= 1 && !(ok = mbar_wait(smem_u32(o_free), (pc.k - 1) & 1, abort_flag, p.err, 342)))
+          break;
+        ok = mbar_wait(smem_u32(&p_ready[g & 1]), (g >> 1) & 1, abort_flag, p.err, 335) &&
+             mbar_wait(smem_u32(&v_full[g % VST3]), (g / VST3) & 1, abort_flag, p.err, 336);
+        if (!ok) break;
+        fence_after();
+        const bool mtr = tr && pc.k == 0 && pc.j < 16;
+        if (mtr) tr[50 + 3 * pc.j] = gtimer();
+        const uint64_t vd = vdesc(smem_u32(sVr + (g % VST3) * TILE));
+        const uint32_t pa = tmem + 128 + (g & 1) * 128, dO = tmem;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_bf16_ta(dO, pa + 8 * k, vd + (uint64_t)(128 * k), idesc | kIdescBMajorMN, (pc.j | k) != 0);
+        commit(smem_u32(&pv_done[g & 1]));
+        commit(smem_u32(&v_empty[g % VST3]));
+        if (mtr) tr[51 + 3 * pc.j] = gtimer();
+        // S(g + 2) overwrites the buffer PV(g) reads P(g) from; MMAs of one issuing thread run in
+        // issue order, so PV(g) has read it first
+        if (sc.idx >= 0) {
+          ok = issue_s(sc);
+          next(sc);
+          if (mtr) tr[52 + 3 * pc.j] = gtimer();
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- softmax: two threads per query row ----------------
+    const int quarter = warp & 3;
+    const int hf = (warp - 2) >> 2;      // column half
+    const int r = quarter * 32 + lane;   // row within the tile = TMEM lane
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    // Q of tile k from its shared-memory tile (128-byte swizzled rows) into TMEM Q buffer k % 2, the
+    // A operand of the tile's QK^T: this thread's 64 columns of its row, as 32 packed bf16 words
+    auto q_to_tmem = [&](int k) -> bool {
+      if (!mbar_wait(smem_u32(q_full), k & 1, abort_flag, p.err, 343)) return false;
+      uint32_t w[32];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 v = *(const uint4*)(sQ + hf * CHUNK + r * 128 + ((u ^ (r & 7)) << 4));
+        w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
+      }
+      tst32(tmem + 384 + (k & 1) * 64 + lane_base + hf * 32, w);
+      tst_wait();
+      fence_before();
+      mbar_arrive(smem_u32(&q_tm[k & 1]));
+      mbar_arrive(smem_u32(q_empty));  // the shared-memory Q tile may take the next tile's Q
+      return true;
+    };
+    bool ok = q_to_tmem(0);
+    ok = __all_sync(0xffffffffu, ok);
+    int g = 0;
+    for (int k = 0, idx; ok && (idx = tile_of(k, c, G, total)) >= 0; ++k) {
+      int b, h, qb, last;
+      tile_geo(idx, b, h, qb, last);
+      const uint32_t tO = tmem + lane_base + hf * 64;
+      const int g0 = g;
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j <= last; ++j, ++g) {
+        const uint32_t tS = tmem + 128 + (g & 1) * 128 + lane_base;
+        ok = mbar_wait(smem_u32(&s_full[g & 1]), (g >> 1) & 1, abort_flag, p.err, 338);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        fence_after();
+        const bool tracer = tr && r == 0 && hf == 0 && k == 0 && j < 16;
+        if (tracer) tr[1 + 2 * j] = gtimer();
+        uint32_t s[64];
+        tld32(tS + hf * 64, s);
+        tld32(tS + hf * 64 + 32, s + 32);
+        tld_wait();
+        if (p.causal && j == qb) {
+#pragma unroll
+          for (int cc = 0; cc < 64; ++cc)
+            if (hf * 64 + cc > r) s[cc] = __float_as_uint(-INFINITY);
+        }
+        float mx8[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) mx8[q] = fmaxf(__uint_as_float(s[2 * q]), __uint_as_float(s[2 * q + 1]));
+#pragma unroll
+        for (int cc = 16; cc < 64; cc += 16)
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            mx8[q] = max3f(mx8[q], __uint_as_float(s[cc + 2 * q]), __uint_as_float(s[cc + 2 * q + 1]));
+        const float mxh = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
+        // the partner thread's partial maximum; the barrier also orders both threads' S reads before
+        // either writes P over the buffer's first 64 columns
+        xch[((g & 1) * 2 + hf) * BQ + r] = mxh;
+        bar_pair(1 + quarter);
+        const float mx = fmaxf(mxh, xch[((g & 1) * 2 + (hf ^ 1)) * BQ + r]) * p.scale_log2;
+        // lazy rescaling, as in the two-tile kernel: both threads of a row take the same decisions
+        const float mnew = mx > m + 8.0f ? mx : m;
+        const float alpha = ex2(m - mnew);
+        const uint64_t scale2 = pack_f32x2(p.scale_log2, p.scale_log2), neg2 = pack_f32x2(-mnew, -mnew);
+        uint64_t sum2[4] = {0, 0, 0, 0};
+        uint32_t* pk = s;
+#pragma unroll
+        for (int cc = 0; cc < 64; cc += 2) {
+          float x0, x1;
+          unpack_f32x2(fma_f32x2(pack_f32x2(__uint_as_float(s[cc]), __uint_as_float(s[cc + 1])), scale2, neg2), x0,
+                       x1);
+          const float p0 = ex2(x0), p1 = ex2(x1);
+          sum2[(cc >> 1) & 3] = add_f32x2(sum2[(cc >> 1) & 3], pack_f32x2(p0, p1));
+          pk[cc / 2] = pack_bf16x2(p0, p1);
+        }
+        float sa[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) unpack_f32x2(sum2[q], sa[2 * q], sa[2 * q + 1]);
+        l = l * alpha + (((sa[0] + sa[1]) + (sa[2] + sa[3])) + ((sa[4] + sa[5]) + (sa[6] + sa[7])));
+        m = mnew;
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+          // S(g) was issued before PV(g - 1): wait for PV(g - 1) before touching O
+          ok = mbar_wait(smem_u32(&pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, abort_flag, p.err, 339);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          fence_after();
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            uint32_t o[32];
+            tld32(tO + cc * 32, o);
+            tld_wait_regs(o);
+#pragma unroll
+            for (int q = 0; q < 32; ++q) o[q] = __float_as_uint(__uint_as_float(o[q]) * alpha);
+            tst32(tO + cc * 32, o);
+          }
+        }
+        tst32(tS + hf * 32, pk);
+        tst_wait();
+        fence_before();
+        mbar_arrive(smem_u32(&p_ready[g & 1]));
+        if (tracer) tr[2 + 2 * j] = gtimer();
+      }
+      if (!ok) break;
+      // the next tile's Q: its buffer was last read by tile k - 1's QK^T, which has completed
+      if (tile_of(k + 1, c, G, total) >= 0) {
+        ok = __all_sync(0xffffffffu, q_to_tmem(k + 1));
+        if (!ok) break;
+      }
+      // the tile's last two PVs, each on its own barrier
+      for (int gg = (g - 2 < g0 ? g0 : g - 2); ok && gg < g; ++gg) {
+        ok = mbar_wait(smem_u32(&pv_done[gg & 1]), (gg >> 1) & 1, abort_flag, p.err, 340);
+        ok = __all_sync(0xffffffffu, ok);
+      }
+      if (!ok) break;
+      fence_after();
+      xl[hf * BQ + r] = l;
+      bar_pair(1 + quarter);
+      const float inv = 1.0f / ((l + xl[(hf ^ 1) * BQ + r]) + p.eps);
+      uint32_t o[64];
+      tld32(tO, o);
+      tld32(tO + 32, o + 32);
+      tld_wait();
+      // O buffer k % 2 is free for tile k + 2; the row sums may be rewritten after this barrier
+      fence_before();
+      mbar_arrive(smem_u32(o_free));
+      bar_pair(1 + quarter);
+      // each thread stores its 64 columns (128 contiguous bytes of its output row)
+      uint4* dst = (uint4*)(p.O + (((int64_t)b * p.S + qb * BQ + r) * p.Hq + h) * D + hf * 64);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)  // columns 8 u .. 8 u + 7
+        dst[u] = make_uint4(pack_bf16(__uint_as_float(o[8 * u]) * inv, __uint_as_float(o[8 * u + 1]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * u + 2]) * inv, __uint_as_float(o[8 * u + 3]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * u + 4]) * inv, __uint_as_float(o[8 * u + 5]) * inv),
+                            pack_bf16(__uint_as_float(o[8 * u + 6]) * inv, __uint_as_float(o[8 * u + 7]) * inv));
+      if (tr && r == 0 && hf == 0 && k == 0) tr[36] = gtimer();
+    }
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (tr && threadIdx.x == 64) tr[42] = gtimer();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -790,6 +1176,25 @@ CUtensorMap map3(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64
                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw Fail{FOPT_ERR_CUDA, "cuTensorMapEncodeTiled (attention) failed"};
   return m;
+}
+
+// Diagnostics only (FOPT_ATTN_TRACE): one line per CTA, its 128 stamps in ns from the earliest entry.
+void dump_trace(fopt_ctx* ctx, uint64_t* trace, int64_t blocks, int S, const char* path) {
+  std::vector<uint64_t> t((size_t)blocks * 128);
+  cuda_check(cudaMemcpyAsync(t.data(), trace, t.size() * 8, cudaMemcpyDeviceToHost, ctx->stream), "trace copy");
+  cuda_check(cudaStreamSynchronize(ctx->stream), "trace sync");
+  cudaFreeAsync(trace, ctx->stream);
+  uint64_t t0 = ~0ull;
+  for (int64_t c = 0; c < blocks; ++c) t0 = std::min(t0, t[c * 128]);
+  if (FILE* f = fopen(path, "a")) {
+    fprintf(f, "# blocks=%lld S=%d\n", (long long)blocks, S);
+    for (int64_t c = 0; c < blocks; ++c) {
+      fprintf(f, "%lld", (long long)c);
+      for (int k = 0; k < 128; ++k) fprintf(f, " %lld", t[c * 128 + k] ? (long long)(t[c * 128 + k] - t0) : -1LL);
+      fprintf(f, "\n");
+    }
+    fclose(f);
+  }
 }
 
 }  // namespace attn
@@ -823,6 +1228,28 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
                "attention smem attribute");
     attr = true;
   }
+  if (getenv("FOPT_ATTN_SPLIT_ROWS")) {
+    constexpr int smem3 = (1 + KST3 + VST3) * TILE + 1024 + 3 * 2 * BQ * 4 + 256;
+    static bool attr3 = false;
+    if (!attr3) {
+      cuda_check(cudaFuncSetAttribute(attention_tc3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem3),
+                 "attention smem attribute");
+      attr3 = true;
+    }
+    static int sms = 0;
+    if (!sms) cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ctx->device), "SM count");
+    const int64_t blocks = std::min<int64_t>((int64_t)B * Hq * (S / 128), sms);  // persistent: one CTA per SM
+    const char* trace_path = getenv("FOPT_ATTN_TRACE");
+    if (trace_path) {
+      cuda_check(cudaMallocAsync((void**)&p.trace, blocks * 128 * 8, ctx->stream), "trace alloc");
+      cuda_check(cudaMemsetAsync(p.trace, 0, blocks * 128 * 8, ctx->stream), "trace clear");
+    }
+    CUtensorMap mo = map3(o, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 32);
+    attention_tc3_kernel<<<(unsigned)blocks, THREADS3, smem3, ctx->stream>>>(mq, mk, mv, mo, p);
+    launched(ctx, "attention_tc3");
+    if (trace_path) dump_trace(ctx, p.trace, blocks, S, trace_path);
+    return true;
+  }
   if ((S / 128) % 2 == 0 && !getenv("FOPT_ATTN_ONE_TILE")) {
     const int64_t blocks = (int64_t)B * Hq * (S / 256);
     const char* trace_path = getenv("FOPT_ATTN_TRACE");
@@ -833,23 +1260,7 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
     CUtensorMap mo = map3(o, D, Hq, rows, (uint64_t)D * 2, (uint64_t)Hq * D * 2, 1, 32);
     attention_tc2_kernel<<<(unsigned)blocks, THREADS2, smem, ctx->stream>>>(mq, mk, mv, mo, p);
     launched(ctx, "attention_tc2");
-    if (trace_path) {  // diagnostics only: one line per CTA, stamps in ns from the earliest entry
-      std::vector<uint64_t> t((size_t)blocks * 128);
-      cuda_check(cudaMemcpyAsync(t.data(), p.trace, t.size() * 8, cudaMemcpyDeviceToHost, ctx->stream), "trace copy");
-      cuda_check(cudaStreamSynchronize(ctx->stream), "trace sync");
-      cudaFreeAsync(p.trace, ctx->stream);
-      uint64_t t0 = ~0ull;
-      for (int64_t c = 0; c < blocks; ++c) t0 = std::min(t0, t[c * 128]);
-      if (FILE* f = fopen(trace_path, "a")) {
-        fprintf(f, "# blocks=%lld S=%d\n", (long long)blocks, S);
-        for (int64_t c = 0; c < blocks; ++c) {
-          fprintf(f, "%lld", (long long)c);
-          for (int k = 0; k < 128; ++k) fprintf(f, " %lld", t[c * 128 + k] ? (long long)(t[c * 128 + k] - t0) : -1LL);
-          fprintf(f, "\n");
-        }
-        fclose(f);
-      }
-    }
+    if (trace_path) dump_trace(ctx, p.trace, blocks, S, trace_path);
     return true;
   }
   const int64_t blocks = (int64_t)B * Hq * (S / 128);

@@ -511,14 +511,17 @@ def test_gather_rejects_negative_index(b200):
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
-@pytest.fixture(params=["paired", "one_tile"])
+@pytest.fixture(params=["paired", "one_tile", "split_rows"])
 def attn_kernel(request, monkeypatch):
     """S % 256 == 0 runs the two-query-tile tcgen05 kernel, or with FOPT_ATTN_ONE_TILE the one-tile
-    kernel (which also serves odd block counts)."""
+    kernel (which also serves odd block counts), or with FOPT_ATTN_SPLIT_ROWS the persistent kernel
+    with two threads per row."""
+    monkeypatch.delenv("FOPT_ATTN_ONE_TILE", raising=False)
+    monkeypatch.delenv("FOPT_ATTN_SPLIT_ROWS", raising=False)
     if request.param == "one_tile":
         monkeypatch.setenv("FOPT_ATTN_ONE_TILE", "1")
-    else:
-        monkeypatch.delenv("FOPT_ATTN_ONE_TILE", raising=False)
+    elif request.param == "split_rows":
+        monkeypatch.setenv("FOPT_ATTN_SPLIT_ROWS", "1")
     return request.param
 
 
