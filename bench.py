@@ -264,6 +264,25 @@ def wl_attention(fb, be, S=2048, Hq=32, Hkv=8, D=128):
                                       "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
+def graph_step(be, issue):
+    """A step that runs `issue` once eagerly (plans built, kernels compiled), then captures it as a
+    CUDA graph and replays that: the timed region holds the kernels, not the host's work of issuing
+    them (FOPT_NO_GRAPH=1 issues every step from the host)."""
+    state = {}
+
+    def step():
+        if os.environ.get("FOPT_NO_GRAPH"):
+            return issue()
+        if "graph" not in state:
+            if not state.get("eager"):
+                state["eager"] = True
+                return issue()
+            state["graph"] = be.capture(issue)
+        return state["graph"].launch()
+
+    return step
+
+
 def wl_relayout(fb, be, R=8192, C=8192):
     rng = np.random.default_rng(1)
     ax = dict(R=R, C=C)
@@ -272,9 +291,11 @@ def wl_relayout(fb, be, R=8192, C=8192):
     X = be.from_vec(S, x, "bf16")
     Y = be.zeroed(D, "bf16")
 
-    def step():
+    def issue():
         be.transpose(Y, X, S, D)
         return Y
+
+    step = graph_step(be, issue)
 
     def cpu(_rows=None, keep=None):
         # the oracle's BufStorage::transpose copy loop (OpenMP over destination positions) on a
@@ -296,7 +317,7 @@ def wl_relayout(fb, be, R=8192, C=8192):
 
     return dict(step=step, units=2.0 * R * C * 2, unit="GB/s", scale=1e9, bound="hbm", cpu=cpu, parity=parity,
                 metric="relayout GB/s ([R, C] -> [C, R] bf16, 128 MiB)", workload="relayout_bf16_8192x8192",
-                dtype="bf16", config={"R": R, "C": C})
+                dtype="bf16", config={"R": R, "C": C, "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
 def wl_relayout_padded(fb, be, R=1 << 20, D=61):
@@ -309,9 +330,11 @@ def wl_relayout_padded(fb, be, R=1 << 20, D=61):
     X = be.from_vec(S, x, "f32")
     Y = be.zeroed(Dm, "f32")
 
-    def step():
+    def issue():
         be.transpose(Y, X, S, Dm)
         return Y
+
+    step = graph_step(be, issue)
 
     def parity(_rows=None, _b=None):
         y = Y.to_numpy().reshape(R, 64)
@@ -323,7 +346,8 @@ def wl_relayout_padded(fb, be, R=1 << 20, D=61):
     return dict(step=step, units=2.0 * live, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
                 cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
                 metric="padded-row relayout GB/s ([R, D] -> [R, D # 64] f32, D = 61)",
-                workload="relayout_padded_f32", dtype="f32", config={"R": R, "D": D, "bytes": "live read + live write"})
+                workload="relayout_padded_f32", dtype="f32", config={"R": R, "D": D, "bytes": "live read + live write",
+                                                      "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
 def wl_elementwise(fb, be, n=64 << 20):
@@ -339,10 +363,12 @@ def wl_elementwise(fb, be, n=64 << 20):
     ptrs = (C.c_void_p * 2)(a.addr, b.addr)
     dts = (C.c_int32 * 2)(fb._lib.DTYPES["f32"], fb._lib.DTYPES["f32"])
 
-    def step():
+    def issue():
         fb._lib.check(lib.fopt_elementwise(be.ctx, C.byref(prog), 2, ptrs, dts, OUT.ptr, fb._lib.DTYPES["f32"], n),
                       be.ctx)
         return OUT
+
+    step = graph_step(be, issue)
 
     def parity(_rows=None, _b=None):
         import oracle
@@ -358,7 +384,8 @@ def wl_elementwise(fb, be, n=64 << 20):
     return dict(step=step, units=12.0 * n, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
                 cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
                 metric="generated elementwise program GB/s (f32 a * b + a, 64 Mi elements)",
-                workload="elementwise_f32_zip", dtype="f32", config={"elements": n, "bytes": "2 reads + 1 write"})
+                workload="elementwise_f32_zip", dtype="f32",
+                config={"elements": n, "bytes": "2 reads + 1 write", "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
 def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096, comm_ready=False):
@@ -578,6 +605,24 @@ def bind_to_gpu_cpus(local: int) -> str:
         return f"unbound ({type(e).__name__})"
 
 
+class L2Flush:
+    """Between timed steps: write a 256 MiB buffer (more than the 126 MB L2), then read another
+    256 MiB buffer, so that L2 holds none of the step's data and no dirty lines: without the read,
+    the write-back of the flush's own last 126 MB would land inside the next timed step."""
+
+    HOW = "flushed between steps (256 MiB written, then 256 MiB of another buffer read)"
+
+    def __init__(self):
+        import torch
+
+        self.w = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.r = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.amax()
+
+
 def measure(be, wl, stream, flush, steps, warmup, world, local):
     """W untimed warm-up steps, then exactly `steps` steps, each bracketed by CUDA events on the
     library's stream with L2 flushed before it (outside the events), clocks sampled throughout; the
@@ -598,7 +643,7 @@ def measure(be, wl, stream, flush, steps, warmup, world, local):
         torch.cuda.synchronize()
         wall0 = time.perf_counter()
         for i in range(steps):
-            flush.zero_()
+            flush()
             ev[i][0].record(stream)
             wl["step"]()
             ev[i][1].record(stream)
@@ -613,7 +658,7 @@ def measure(be, wl, stream, flush, steps, warmup, world, local):
             e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                     for _ in range(steps)]
             for i in range(steps):
-                flush.zero_()
+                flush()
                 e_ev[i][0].record(stream)
                 wl["e2e_step"]()
                 e_ev[i][1].record(stream)
@@ -794,7 +839,7 @@ def run_ours(args, rank, world, local):
             "elementwise": lambda: wl_elementwise(fb, be),
             "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}
     wl = make[args.workload]()
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")  # > 126 MB L2
+    flush = L2Flush()
     meas = measure(be, wl, stream, flush, args.steps, args.warmup, world, local)
     sweep = allreduce_sweep(fb, be, world, stream) if (args.workload == "allreduce" and world > 1 and args.sweep) else None
     extra = not args.headline_only and args.workload == "gemm_i8"
@@ -807,7 +852,7 @@ def run_ours(args, rank, world, local):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": rep["ms_per_step"],
                 "higher_is_better": True, "scaling": wl.get("scaling", "weak"), "vs_baseline": None,
                 "dtype": rep["dtype"], "data": "synthetic (seeded)",
-                "config": {**rep["config"], "l2": "flushed (256 MiB write) between steps",
+                "config": {**rep["config"], "l2": L2Flush.HOW,
                            "parallelism": (f"chip axis x{world} (NCCL)" if wl["bound"] == "nvlink" else
                                            f"tensor-parallel x{world} (NCCL)" if wl.get("scaling") == "strong" else
                                            f"replicas x{world}") if world > 1 else "1 GPU",
