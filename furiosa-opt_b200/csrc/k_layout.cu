@@ -350,12 +350,16 @@ __global__ void relayout_walk64(T* __restrict__ dst, const T* __restrict__ src, 
 // ---- padded rows from a dense source: [rows, L] -> [rows, E # ...], E > L, 4-byte elements ----
 // A CTA stages kPadRows source rows (one contiguous run of kPadRows * L elements) in shared memory
 // with aligned 16-byte loads, so every source byte is read from DRAM once, then writes the live
-// cells of its destination rows one element per thread (a warp stores 128 contiguous bytes). Dead
-// cells are not touched, as the reference skips them.
-constexpr int kPadRows = 32;
+// cells of its destination rows (16-byte vectors when the rows are aligned, else one element per
+// thread). Dead cells are not touched, as the reference skips them.
+constexpr int kPadRowsDefault = 32;
+// VEC: the destination rows start on 16-byte boundaries (E % 4 == 0, aligned base), so each thread
+// writes one 16-byte vector of a row: whole vectors with one store, the vector across the live width
+// element by element (its dead cells stay untouched).
+template <bool VEC>
 __global__ void __launch_bounds__(256) relayout_pad_rows(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
                                                          int64_t rows, int L, int E, FastDiv e_div,
-                                                         int64_t src_base, int64_t dst_base, int64_t src_elems) {
+                                                         int64_t src_base, int64_t dst_base, int64_t src_elems, int kPadRows) {
   extern __shared__ uint4 pad_buf4[];
   uint32_t* buf = (uint32_t*)pad_buf4;
   for (int64_t r0 = (int64_t)blockIdx.x * kPadRows; r0 < rows; r0 += (int64_t)gridDim.x * kPadRows) {
@@ -374,11 +378,27 @@ __global__ void __launch_bounds__(256) relayout_pad_rows(uint32_t* __restrict__ 
       }
     }
     __syncthreads();
-    const int total = nr * E;
     uint32_t* drow = dst + dst_base + r0 * E;
-    for (int q = threadIdx.x; q < total; q += blockDim.x) {
-      const uint32_t i = fdiv(e_div, (uint32_t)q), c = (uint32_t)q - i * (uint32_t)E;
-      if ((int)c < L) drow[q] = buf[off + (int)i * L + (int)c];
+    if constexpr (VEC) {
+      const int nv = E >> 2, total = nr * nv;  // e_div divides by nv here
+      for (int q = threadIdx.x; q < total; q += blockDim.x) {
+        const uint32_t i = fdiv(e_div, (uint32_t)q);
+        const int c = 4 * (int)((uint32_t)q - i * (uint32_t)nv);
+        const uint32_t* sp = buf + off + (int)i * L + c;
+        if (c + 4 <= L) {
+          ((uint4*)drow)[q] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (c + k < L) drow[4 * q + k] = sp[k];
+        }
+      }
+    } else {
+      const int total = nr * E;
+      for (int q = threadIdx.x; q < total; q += blockDim.x) {
+        const uint32_t i = fdiv(e_div, (uint32_t)q), c = (uint32_t)q - i * (uint32_t)E;
+        if ((int)c < L) drow[q] = buf[off + (int)i * L + (int)c];
+      }
     }
     __syncthreads();
   }
@@ -654,11 +674,20 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
     if (dense_rows) {
       const int64_t rows = w.extent[1];
       const int L = (int)w.live[0], E = (int)w.extent[0];
+      // 64 rows a CTA where they fit in 48 KB (D = 61 f32: 0.76 of the copy rate against 0.72 with 32
+      // rows, 0.66 with 16 and 0.67 with 128), else 32
+      const int kPadRows = ((size_t)64 * L + 8) * 4 <= 48 * 1024 ? 64 : kPadRowsDefault;
       const size_t sm = ((size_t)kPadRows * L + 8) * 4;
       if (sm <= 48 * 1024) {
         const int64_t blocks = std::min<int64_t>((rows + kPadRows - 1) / kPadRows, 148 * 16);
-        relayout_pad_rows<<<(int)blocks, 256, sm, st>>>((uint32_t*)d, (const uint32_t*)s, rows, L, E,
-                                                        make_fastdiv((uint32_t)E), src_base, dst_base, src_elems);
+        if (E % 4 == 0 && dst_base % 4 == 0 && (uintptr_t)d % 16 == 0 && !getenv("FOPT_RELAYOUT_NO_PADVEC"))
+          relayout_pad_rows<true><<<(int)blocks, 256, sm, st>>>((uint32_t*)d, (const uint32_t*)s, rows, L, E,
+                                                                make_fastdiv((uint32_t)(E / 4)), src_base, dst_base,
+                                                                src_elems, kPadRows);
+        else
+          relayout_pad_rows<false><<<(int)blocks, 256, sm, st>>>((uint32_t*)d, (const uint32_t*)s, rows, L, E,
+                                                                 make_fastdiv((uint32_t)E), src_base, dst_base,
+                                                                 src_elems, kPadRows);
         launched(ctx, "relayout_pad_rows");
         return;
       }
