@@ -140,15 +140,16 @@ std::string store_vec(int dt) {
     case 32:
       return "{ uint4* q = (uint4*)out + (base >> 2); q[0] = make_uint4(r[0], r[1], r[2], r[3]); "
              "q[1] = make_uint4(r[4], r[5], r[6], r[7]); }\n";
-    case 16:
+    case 16:  // one byte permute per pair: the bf16's high halves, or the 16-bit integers' low halves
       if (dt == FOPT_BF16)
-        return "{ *((uint4*)out + (base >> 3)) = make_uint4((r[0] >> 16) | (r[1] & 0xffff0000u), (r[2] >> 16) | "
-               "(r[3] & 0xffff0000u), (r[4] >> 16) | (r[5] & 0xffff0000u), (r[6] >> 16) | (r[7] & 0xffff0000u)); }\n";
-      return "{ *((uint4*)out + (base >> 3)) = make_uint4((r[0] & 0xffffu) | (r[1] << 16), (r[2] & 0xffffu) | "
-             "(r[3] << 16), (r[4] & 0xffffu) | (r[5] << 16), (r[6] & 0xffffu) | (r[7] << 16)); }\n";
-    default:
-      return "{ unsigned h0 = 0, h1 = 0; for (int j = 0; j < 4; ++j) { h0 |= (r[j] & 0xffu) << (8 * j); "
-             "h1 |= (r[j + 4] & 0xffu) << (8 * j); } *((uint2*)out + (base >> 3)) = make_uint2(h0, h1); }\n";
+        return "{ *((uint4*)out + (base >> 3)) = make_uint4(__byte_perm(r[0], r[1], 0x7632), __byte_perm(r[2], r[3], "
+               "0x7632), __byte_perm(r[4], r[5], 0x7632), __byte_perm(r[6], r[7], 0x7632)); }\n";
+      return "{ *((uint4*)out + (base >> 3)) = make_uint4(__byte_perm(r[0], r[1], 0x5410), __byte_perm(r[2], r[3], "
+             "0x5410), __byte_perm(r[4], r[5], 0x5410), __byte_perm(r[6], r[7], 0x5410)); }\n";
+    default:  // low bytes of four words into one: two permutes to byte pairs, one to join them
+      return "{ const unsigned h0 = __byte_perm(__byte_perm(r[0], r[1], 0x0040), __byte_perm(r[2], r[3], 0x0040), "
+             "0x5410), h1 = __byte_perm(__byte_perm(r[4], r[5], 0x0040), __byte_perm(r[6], r[7], 0x0040), 0x5410); "
+             "*((uint2*)out + (base >> 3)) = make_uint2(h0, h1); }\n";
   }
 }
 
