@@ -782,13 +782,13 @@ __global__ void __launch_bounds__(THREADS2, 1)
 //              quarter), keep their own running sums, and write their 32 packed bf16 probability
 //              words over the first 64 columns of the row's S buffer; PV reads P from there. At the
 //              end of a tile they normalise the O row and store it (128 bytes per thread).
-// TMEM columns: O [0, 128), S buffers [128, 256) and [256, 384), Q buffers [384, 448) and [448, 512).
-// Q is the QK^T's A operand in tensor memory: with both operands in shared memory the 128 x 128
-// MMA steps were bound by shared-memory reads (about 140 cycles each against about 95 with A in
-// tensor memory).
+// TMEM columns: O [0, 128), S buffers [128, 256), [256, 384) and [384, 512). With three S buffers
+// S(g + 3) is issued right behind PV(g), so the S a softmax needs next has been computed one softmax
+// period earlier; with two, it waited behind PV(g - 1) on every block.
 // ---------------------------------------------------------------------------------------------
 constexpr int THREADS3 = 352;
 constexpr int KST3 = 3, VST3 = 2;  // K and V ring depths
+constexpr int NSB = 3;             // S buffers in tensor memory
 
 
 __device__ __forceinline__ void bar_pair(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
@@ -816,12 +816,11 @@ __global__ void __launch_bounds__(THREADS3, 1)
   uint64_t* k_empty = k_full + KST3;
   uint64_t* v_full = k_empty + KST3;
   uint64_t* v_empty = v_full + VST3;
-  uint64_t* s_full = v_empty + VST3;  // [2] per S buffer
-  uint64_t* p_ready = s_full + 2;        // [2] per S buffer
-  uint64_t* pv_done = p_ready + 2;       // [2] PV(g) completes pv_done[g % 2]
-  uint64_t* o_free = pv_done + 2;        // the epilogue has read O
-  uint64_t* q_tm = o_free + 1;           // [2] per TMEM Q buffer: the softmax threads have written it
-  uint32_t* tmem_slot = (uint32_t*)(q_tm + 2);
+  uint64_t* s_full = v_empty + VST3;    // [NSB] per S buffer
+  uint64_t* p_ready = s_full + NSB;      // [NSB] per S buffer
+  uint64_t* pv_done = p_ready + NSB;     // [NSB] PV(g) completes pv_done[g % NSB]
+  uint64_t* o_free = pv_done + NSB;      // the epilogue has read O
+  uint32_t* tmem_slot = (uint32_t*)(o_free + 1);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -838,7 +837,7 @@ __global__ void __launch_bounds__(THREADS3, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(q_full), 1);
-    mbar_init(smem_u32(q_empty), 256);
+    mbar_init(smem_u32(q_empty), 1);
     mbar_init(smem_u32(o_free), 256);
     for (int s = 0; s < KST3; ++s) {
       mbar_init(smem_u32(&k_full[s]), 1);
@@ -848,11 +847,10 @@ __global__ void __launch_bounds__(THREADS3, 1)
       mbar_init(smem_u32(&v_full[s]), 1);
       mbar_init(smem_u32(&v_empty[s]), 1);
     }
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < NSB; ++t) {
       mbar_init(smem_u32(&s_full[t]), 1);
       mbar_init(smem_u32(&p_ready[t]), 256);
       mbar_init(smem_u32(&pv_done[t]), 1);
-      mbar_init(smem_u32(&q_tm[t]), 256);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -919,8 +917,8 @@ __global__ void __launch_bounds__(THREADS3, 1)
     if (lane == 0) {
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
                              ((uint32_t)(128 >> 4) << 24);
-      // The global block sequence: block g belongs to tile tk[g], is key block jg[g] of it; the
-      // issuer walks it with two cursors (the next S to issue runs two blocks ahead of the PV).
+      // The global block sequence over this CTA's tiles; the issuer walks it with two cursors (the
+      // next S to issue runs NSB blocks ahead of the PV).
       struct Cursor {
         int k = 0, idx = -1, j = 0, last = -1, g = 0;
       };
@@ -948,28 +946,30 @@ __global__ void __launch_bounds__(THREADS3, 1)
         }
       };
       bool ok = true;
-      // S(g) = Q K^T into buffer g % 2; the first S of a tile waits for its Q, the last releases Q
+      const uint32_t sq = smem_u32(sQ);
+      // S(g) = Q K^T into buffer g % NSB; the first S of a tile waits for its Q, the last releases Q
       auto issue_s = [&](const Cursor& u) -> bool {
-        if (u.j == 0 && !mbar_wait(smem_u32(&q_tm[u.k & 1]), (u.k >> 1) & 1, abort_flag, p.err, 333)) return false;
+        if (u.j == 0 && !mbar_wait(smem_u32(q_full), u.k & 1, abort_flag, p.err, 333)) return false;
         if (!mbar_wait(smem_u32(&k_full[u.g % KST3]), (u.g / KST3) & 1, abort_flag, p.err, 334)) return false;
         fence_after();
         // descriptors of the tile bases; a k-step adds its offset (in 16-byte units) to the start
         // address field, which stays below 2^14 units for any shared-memory address
-        const uint64_t kd = sdesc(smem_u32(sKr + (u.g % KST3) * TILE));
-        const uint32_t dS = tmem + 128 + (u.g & 1) * 128, qa = tmem + 384 + (u.k & 1) * 64;
+        const uint64_t qd = sdesc(sq), kd = sdesc(smem_u32(sKr + (u.g % KST3) * TILE));
+        const uint32_t dS = tmem + 128 + (u.g % NSB) * 128;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (uint32_t)((k >> 2) * CHUNK + (k & 3) * 32) >> 4;
-          mma_bf16_ta(dS, qa + 8 * k, kd + off, idesc, k != 0);
+          mma_bf16(dS, qd + off, kd + off, idesc, k != 0);
         }
-        commit(smem_u32(&s_full[u.g & 1]));
+        commit(smem_u32(&s_full[u.g % NSB]));
         commit(smem_u32(&k_empty[u.g % KST3]));
+        if (u.j == u.last) commit(smem_u32(q_empty));
         return true;
       };
       Cursor sc, pc;
       first(sc);
       first(pc);
-      for (int i = 0; ok && i < 2 && sc.idx >= 0; ++i) {
+      for (int i = 0; ok && i < NSB && sc.idx >= 0; ++i) {
         ok = issue_s(sc);
         next(sc);
       }
@@ -978,21 +978,21 @@ __global__ void __launch_bounds__(THREADS3, 1)
         // PV of a tile's first block overwrites O: the previous tile's epilogue has read it
         if (pc.j == 0 && pc.k >= 1 && !(ok = mbar_wait(smem_u32(o_free), (pc.k - 1) & 1, abort_flag, p.err, 342)))
           break;
-        ok = mbar_wait(smem_u32(&p_ready[g & 1]), (g >> 1) & 1, abort_flag, p.err, 335) &&
+        ok = mbar_wait(smem_u32(&p_ready[g % NSB]), (g / NSB) & 1, abort_flag, p.err, 335) &&
              mbar_wait(smem_u32(&v_full[g % VST3]), (g / VST3) & 1, abort_flag, p.err, 336);
         if (!ok) break;
         fence_after();
         const bool mtr = tr && pc.k == 0 && pc.j < 16;
         if (mtr) tr[50 + 3 * pc.j] = gtimer();
         const uint64_t vd = vdesc(smem_u32(sVr + (g % VST3) * TILE));
-        const uint32_t pa = tmem + 128 + (g & 1) * 128, dO = tmem;
+        const uint32_t pa = tmem + 128 + (g % NSB) * 128, dO = tmem;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ta(dO, pa + 8 * k, vd + (uint64_t)(128 * k), idesc | kIdescBMajorMN, (pc.j | k) != 0);
-        commit(smem_u32(&pv_done[g & 1]));
+        commit(smem_u32(&pv_done[g % NSB]));
         commit(smem_u32(&v_empty[g % VST3]));
         if (mtr) tr[51 + 3 * pc.j] = gtimer();
-        // S(g + 2) overwrites the buffer PV(g) reads P(g) from; MMAs of one issuing thread run in
+        // S(g + NSB) overwrites the buffer PV(g) reads P(g) from; MMAs of one issuing thread run in
         // issue order, so PV(g) has read it first
         if (sc.idx >= 0) {
           ok = issue_s(sc);
@@ -1008,35 +1008,16 @@ __global__ void __launch_bounds__(THREADS3, 1)
     const int hf = (warp - 2) >> 2;      // column half
     const int r = quarter * 32 + lane;   // row within the tile = TMEM lane
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    // Q of tile k from its shared-memory tile (128-byte swizzled rows) into TMEM Q buffer k % 2, the
-    // A operand of the tile's QK^T: this thread's 64 columns of its row, as 32 packed bf16 words
-    auto q_to_tmem = [&](int k) -> bool {
-      if (!mbar_wait(smem_u32(q_full), k & 1, abort_flag, p.err, 343)) return false;
-      uint32_t w[32];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint4 v = *(const uint4*)(sQ + hf * CHUNK + r * 128 + ((u ^ (r & 7)) << 4));
-        w[4 * u] = v.x; w[4 * u + 1] = v.y; w[4 * u + 2] = v.z; w[4 * u + 3] = v.w;
-      }
-      tst32(tmem + 384 + (k & 1) * 64 + lane_base + hf * 32, w);
-      tst_wait();
-      fence_before();
-      mbar_arrive(smem_u32(&q_tm[k & 1]));
-      mbar_arrive(smem_u32(q_empty));  // the shared-memory Q tile may take the next tile's Q
-      return true;
-    };
-    bool ok = q_to_tmem(0);
-    ok = __all_sync(0xffffffffu, ok);
+    bool ok = true;
     int g = 0;
     for (int k = 0, idx; ok && (idx = tile_of(k, c, G, total)) >= 0; ++k) {
       int b, h, qb, last;
       tile_geo(idx, b, h, qb, last);
       const uint32_t tO = tmem + lane_base + hf * 64;
-      const int g0 = g;
       float m = -INFINITY, l = 0.0f;
       for (int j = 0; j <= last; ++j, ++g) {
-        const uint32_t tS = tmem + 128 + (g & 1) * 128 + lane_base;
-        ok = mbar_wait(smem_u32(&s_full[g & 1]), (g >> 1) & 1, abort_flag, p.err, 338);
+        const uint32_t tS = tmem + 128 + (g % NSB) * 128 + lane_base;
+        ok = mbar_wait(smem_u32(&s_full[g % NSB]), (g / NSB) & 1, abort_flag, p.err, 338);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         fence_after();
@@ -1087,7 +1068,7 @@ __global__ void __launch_bounds__(THREADS3, 1)
         m = mnew;
         if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
           // S(g) was issued before PV(g - 1): wait for PV(g - 1) before touching O
-          ok = mbar_wait(smem_u32(&pv_done[(g - 1) & 1]), ((g - 1) >> 1) & 1, abort_flag, p.err, 339);
+          ok = mbar_wait(smem_u32(&pv_done[(g - 1) % NSB]), ((g - 1) / NSB) & 1, abort_flag, p.err, 339);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           fence_after();
@@ -1104,20 +1085,14 @@ __global__ void __launch_bounds__(THREADS3, 1)
         tst32(tS + hf * 32, pk);
         tst_wait();
         fence_before();
-        mbar_arrive(smem_u32(&p_ready[g & 1]));
+        mbar_arrive(smem_u32(&p_ready[g % NSB]));
         if (tracer) tr[2 + 2 * j] = gtimer();
       }
       if (!ok) break;
-      // the next tile's Q: its buffer was last read by tile k - 1's QK^T, which has completed
-      if (tile_of(k + 1, c, G, total) >= 0) {
-        ok = __all_sync(0xffffffffu, q_to_tmem(k + 1));
-        if (!ok) break;
-      }
-      // the tile's last two PVs, each on its own barrier
-      for (int gg = (g - 2 < g0 ? g0 : g - 2); ok && gg < g; ++gg) {
-        ok = mbar_wait(smem_u32(&pv_done[gg & 1]), (gg >> 1) & 1, abort_flag, p.err, 340);
-        ok = __all_sync(0xffffffffu, ok);
-      }
+      // the tile's last PV (its commit tracks every earlier MMA); the previous completion of its
+      // barrier, PV(g - 1 - NSB), is done: S(g - 1) was issued after it
+      ok = mbar_wait(smem_u32(&pv_done[(g - 1) % NSB]), ((g - 1) / NSB) & 1, abort_flag, p.err, 340);
+      ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       fence_after();
       xl[hf * BQ + r] = l;
