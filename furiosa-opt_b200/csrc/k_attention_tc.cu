@@ -764,18 +764,18 @@ __global__ void __launch_bounds__(THREADS2, 1)
 
 
 // ---------------------------------------------------------------------------------------------
-// Persistent kernel: one query tile at a time per CTA, S and O double-buffered in tensor memory,
-// each row's softmax split over two threads.
+// Persistent kernel: one query tile at a time per CTA, three S buffers in tensor memory, each row's
+// softmax split over two threads.
 //
 // One CTA per SM. CTA c takes the query tiles c, 2G - 1 - c, 2G + c, ... of the longest-first
 // order (G CTAs, the tile list walked back and forth so that every CTA gets about the same number
 // of key blocks). The key blocks of all of a CTA's tiles form one sequence g = 0, 1, 2, ...: S(g)
-// goes to S buffer g % 2, and the K / V ring, the S buffers and their barriers run on g across
+// goes to S buffer g % 3, and the K / V rings, the S buffers and their barriers run on g across
 // tile boundaries, so the next tile's first QK^T runs while this tile finishes. 352 threads:
 //   warp 0     TMA producer of Q (per tile, once the previous tile's last S has read the Q buffer)
 //              and of K tiles into a 3-stage ring; warp 10 produces V tiles into a 2-stage ring;
-//   warp 1     TMEM owner and MMA issuer, in the order S(0) S(1) | PV(g) S(g + 2) ...; PV of tile
-//              t accumulates into O buffer t % 2, after the epilogue of tile t - 2 has read it;
+//   warp 1     TMEM owner and MMA issuer, in the order S(0) S(1) S(2) | PV(g) S(g + 3) ...; the
+//              first PV of a tile overwrites O once the previous tile's epilogue has read it;
 //   warps 2-9  softmax: warp w reads TMEM lanes 32 (w % 4) .. + 31 (rows), warps 2-5 columns 0-63
 //              and warps 6-9 columns 64-127 of each score row. The two threads of a row exchange
 //              their partial maxima through shared memory (a 64-thread named barrier per lane
