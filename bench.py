@@ -113,6 +113,9 @@ class Clocks:
 TRAFFIC = {
     "gemm_i8_4096x4096x4096": (33.6e6, "profiles/gemm_tc_i8_4096.md"),
     "attention_s2048": (25.2e6, "profiles/attention_tc2_s2048.md"),
+    "relayout_bf16_8192x8192": (217.9e6, "profiles/relayout_tile_h_bf16_8192.md"),
+    "relayout_padded_f32": (504.2e6, "profiles/relayout_pad_rows_f32.md"),
+    "elementwise_f32_zip": (772.1e6, "profiles/fopt_ew_gen_zip_f32.md"),
 }
 
 
