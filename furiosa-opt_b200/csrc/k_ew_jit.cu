@@ -599,8 +599,10 @@ RowLayout row_layout(const fopt_row_plan& P) {
       L.tpr = tpr;
       break;
     }
-  // enough warps to hide latency: about 48 a SM over the 148 SMs
-  while (L.tpr < 256 && P.rows * (L.tpr / 32) < 148 * 48) L.tpr *= 2;
+  // enough warps to hide latency: about 192 per SM over the 148 SMs, counted over the whole grid
+  // (RMSNorm + quantise over 4096 x 4096: 32 / 64 / 128 / 256 threads a row took 44.3 / 42.2 / 40.2
+  // / 38.2 us; more threads a row shorten each row's chain of passes)
+  while (L.tpr < 256 && P.rows * (L.tpr / 32) < 148 * 192) L.tpr *= 2;
   L.spt = 256 / L.tpr;
   // Held values beyond a register budget go to shared memory ([group][element][thread], one bank
   // per lane): a row's activation then takes fewer registers and more rows stay resident per SM.

@@ -431,7 +431,7 @@ def test_row_program_layouts_compile(monkeypatch, case):
     from furiosa_opt_b200 import ops, workloads as Wl
     B, be, built = _fake_backend(monkeypatch)
     if case == "held_warp_per_row":
-        T, F = 8192, 1024
+        T, F = 32768, 1024
         blk = Wl.DecoderBlockW8A8.__new__(Wl.DecoderBlockW8A8)
         blk.be, blk.T, blk.F, blk.ax = be, T, F, dict(T=T, F=F)
         gate, up = B.Storage(be, "bf16", T * F), B.Storage(be, "bf16", T * F)
