@@ -353,21 +353,36 @@ def wl_relayout_padded(fb, be, R=1 << 20, D=61):
                                                       "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
-def wl_elementwise(fb, be, n=64 << 20):
-    """A generated zip program (f32 a * b + a, 64 Mi elements: 768 MiB moved, well above L2)."""
+def wl_elementwise(fb, be, n=64 << 20, dt="f32"):
+    """A generated zip program over two inputs well above L2: f32 a * b + a (64 Mi elements, 768 MiB
+    moved); bf16 the same in f32 with the bf16 rounding of the result (128 Mi elements, 768 MiB);
+    i8 a + b clipped to [-128, 127] (256 Mi elements, 768 MiB)."""
     rng = np.random.default_rng(3)
     m = fb.Mapping("[E]", dict(E=n))
-    a = be.from_vec(m, rng.standard_normal(n).astype(np.float32), "f32")
-    b = be.from_vec(m, rng.standard_normal(n).astype(np.float32), "f32")
     p_ = fb.ops.Prog(2)
-    prog = p_.build(p_.emit("ADDF", p_.emit("MULF", 0, 1), 0))
-    OUT = be.zeroed(m, "f32")
+    if dt == "i8":
+        av, bv = (rng.integers(-128, 128, n, dtype=np.int64).astype(np.int8) for _ in range(2))
+        prog = p_.build(p_.emit("MINI", p_.emit("MAXI", p_.emit("ADD_FXP", 0, 1), p_.const_i32(-128)),
+                                p_.const_i32(127)))
+        desc, esz = "i8 a + b clipped to [-128, 127]", 1
+    else:
+        av, bv = (rng.standard_normal(n).astype(np.float32) for _ in range(2))
+        if dt == "bf16":
+            av, bv = fb.dtypes.f32_to_bf16_bits(av), fb.dtypes.f32_to_bf16_bits(bv)
+            prog = p_.build(p_.emit("F32_TO_BF16", p_.emit("ADDF", p_.emit("MULF", 0, 1), 0)))
+            desc, esz = "bf16 a * b + a (f32 arithmetic, bf16 result)", 2
+        else:
+            prog = p_.build(p_.emit("ADDF", p_.emit("MULF", 0, 1), 0))
+            desc, esz = "f32 a * b + a", 4
+    a = be.from_vec(m, av, dt)
+    b = be.from_vec(m, bv, dt)
+    OUT = be.zeroed(m, dt)
     lib = fb._lib.lib()
     ptrs = (C.c_void_p * 2)(a.addr, b.addr)
-    dts = (C.c_int32 * 2)(fb._lib.DTYPES["f32"], fb._lib.DTYPES["f32"])
+    dts = (C.c_int32 * 2)(fb._lib.DTYPES[dt], fb._lib.DTYPES[dt])
 
     def issue():
-        fb._lib.check(lib.fopt_elementwise(be.ctx, C.byref(prog), 2, ptrs, dts, OUT.ptr, fb._lib.DTYPES["f32"], n),
+        fb._lib.check(lib.fopt_elementwise(be.ctx, C.byref(prog), 2, ptrs, dts, OUT.ptr, fb._lib.DTYPES[dt], n),
                       be.ctx)
         return OUT
 
@@ -377,18 +392,80 @@ def wl_elementwise(fb, be, n=64 << 20):
         import oracle
 
         k = 1 << 16
-        ga, gb = a.to_numpy()[:k], b.to_numpy()[:k]
-        want = oracle.elementwise([(32, 2, 0, 1, 0, 0), (30, 3, 2, 0, 0, 0)], 3, [ga.tobytes(), gb.tobytes()],
-                                  ["f32", "f32"], "f32", k)
-        same = OUT.to_bytes()[: 4 * k] == want
+        insns = [(prog.insn[i].op, prog.insn[i].dst, prog.insn[i].a, prog.insn[i].b, prog.insn[i].c, prog.insn[i].imm_i)
+                 for i in range(prog.n_insn)]
+        want = oracle.elementwise(insns, prog.ret, [np.ascontiguousarray(av[:k]).tobytes(),
+                                                    np.ascontiguousarray(bv[:k]).tobytes()], [dt, dt], dt, k)
+        same = OUT.to_bytes()[: esz * k] == want
         return {"check": f"first {k} elements against the oracle", "bit_exact": same,
                 "result": "bit-exact" if same else "DIFFERS"}
 
-    return dict(step=step, units=12.0 * n, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
+    name = "elementwise_f32_zip" if dt == "f32" else f"elementwise_{dt}_zip"
+    return dict(step=step, units=3.0 * esz * n, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
                 cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
-                metric="generated elementwise program GB/s (f32 a * b + a, 64 Mi elements)",
-                workload="elementwise_f32_zip", dtype="f32",
+                metric=f"generated elementwise program GB/s ({desc}, {n >> 20} Mi elements)",
+                workload=name, dtype=dt,
                 config={"elements": n, "bytes": "2 reads + 1 write", "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
+
+
+def wl_broadcast(fb, be, A=4096, B=16384):
+    """A broadcast relayout [A] -> [A, B] (i32, 256 MiB written): `transpose` with a zero-stride
+    source axis (buf.rs:257-313 with allow_broadcast), materialised into a preallocated output."""
+    ax = dict(A=A, B=B)
+    S, D = fb.Mapping("[A]", ax), fb.Mapping("[A, B]", ax)
+    x = np.random.default_rng(4).integers(-2**31, 2**31 - 1, A).astype(np.int32)
+    X = be.from_vec(S, x, "i32")
+    Y = be.zeroed(D, "i32")
+
+    def issue():
+        be.transpose(Y, X, S, D, allow_broadcast=True)
+        return Y
+
+    step = graph_step(be, issue)
+
+    def parity(_rows=None, _b=None):
+        y = Y.to_numpy().reshape(A, B)
+        same = bool(np.array_equal(y, np.repeat(x[:, None], B, axis=1)))
+        return {"check": "whole output against numpy's repeat", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    return dict(step=step, units=4.0 * A * B + 4.0 * A, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
+                cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
+                metric="broadcast relayout GB/s ([A] -> [A, B] i32, 256 MiB written)", workload="broadcast_i32",
+                dtype="i32", config={"A": A, "B": B, "bytes": "source read + output written",
+                                     "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
+
+
+def wl_chip_layout(fb, be, A=4096, B=16384):
+    """The chip-shuffle example's HBM relayout (shuffle_slice_tests.rs: [A / 4 % 4, A / 16, A % 4, B]
+    -> [A / 4 % 4, B, A % 4, A / 16]), scaled from A = 256, B = 4096 to 256 MiB of i32."""
+    ax = dict(A=A, B=B)
+    S = fb.Mapping("[A / 4 % 4, A / 16, A % 4, B]", ax)
+    D = fb.Mapping("[A / 4 % 4, B, A % 4, A / 16]", ax)
+    x = np.arange(A * B, dtype=np.int64).astype(np.int32)
+    X = be.from_vec(S, x, "i32")
+    Y = be.zeroed(D, "i32")
+
+    def issue():
+        be.transpose(Y, X, S, D)
+        return Y
+
+    step = graph_step(be, issue)
+
+    def parity(_rows=None, _b=None):
+        # source position of (a4, a16, a1, b) is ((a4 * (A/16) + a16) * 4 + a1) * B + b; the output
+        # walks (a4, b, a1, a16)
+        y = Y.to_numpy().reshape(4, B, 4, A // 16)
+        src = x.reshape(4, A // 16, 4, B)
+        same = bool(np.array_equal(y, src.transpose(0, 3, 2, 1)))
+        return {"check": "whole output against numpy's axis permutation", "bit_exact": same,
+                "result": "bit-exact" if same else "DIFFERS"}
+
+    return dict(step=step, units=2.0 * 4 * A * B, unit="GB/s", scale=1e9, bound="hbm", parity=parity,
+                cpu=lambda rows=None, keep=None: (float("nan"), "not sampled"),
+                metric="chip-shuffle layout relayout GB/s (i32, 256 MiB each way)", workload="relayout_chip_layout_i32",
+                dtype="i32", config={"A": A, "B": B, "src": S.expr, "dst": D.expr,
+                                     "cuda_graph": not os.environ.get("FOPT_NO_GRAPH")})
 
 
 def wl_allreduce(fb, be, rank, world, count=8 * 2048 * 4096, comm_ready=False):
@@ -753,7 +830,7 @@ def report(wl, meas, world, pk, args, int8_peak=None, cpu=True):
             out["cpu_baseline"] = {"value": round(rate / wl["scale"], 6), "unit": wl["unit"],
                                    "cores": os.cpu_count(), "kind": "port", "sample": sample}
     if "parity" in wl and cpu and not args.no_cpu and (
-            "bytes" in keep or wl["workload"].startswith(("relayout", "elementwise"))):
+            "bytes" in keep or wl["workload"].startswith(("relayout", "elementwise", "broadcast"))):
         out["parity"] = wl["parity"](args.cpu_rows, keep.get("bytes"))
     return out
 
@@ -823,7 +900,8 @@ def collective_report(fb, be, rank, world, stream, flush, args, local):
     return rep
 
 
-SUB_CONFIGS = ("gemm_bf16", "attention", "decoder", "mnist", "relayout", "relayout_padded", "elementwise")
+SUB_CONFIGS = ("gemm_bf16", "attention", "decoder", "mnist", "relayout", "relayout_padded", "relayout_chip_layout",
+               "broadcast", "elementwise", "elementwise_bf16", "elementwise_i8")
 
 
 def run_ours(args, rank, world, local):
@@ -840,6 +918,9 @@ def run_ours(args, rank, world, local):
             "allreduce": lambda: wl_allreduce(fb, be, rank, world), "mnist": lambda: wl_mnist(fb, be),
             "decoder": lambda: wl_decoder(fb, be), "relayout_padded": lambda: wl_relayout_padded(fb, be),
             "elementwise": lambda: wl_elementwise(fb, be),
+            "elementwise_bf16": lambda: wl_elementwise(fb, be, 128 << 20, "bf16"),
+            "elementwise_i8": lambda: wl_elementwise(fb, be, 256 << 20, "i8"),
+            "broadcast": lambda: wl_broadcast(fb, be), "relayout_chip_layout": lambda: wl_chip_layout(fb, be),
             "decoder_tp": lambda: wl_decoder_tp(fb, be, rank, world)}
     wl = make[args.workload]()
     flush = L2Flush()
