@@ -95,6 +95,30 @@ __global__ void relayout_bcast(uint4* __restrict__ dst, const T* __restrict__ sr
   }
 }
 
+// Broadcast rows of at least 32 vectors: a warp per row, the row's source offset walked once, then
+// the warp's lanes store the row's vectors (512 contiguous bytes per warp store) instead of every
+// 16-byte vector dividing its index and walking the odometer.
+template <typename T>
+__global__ void relayout_bcast_rows(uint4* __restrict__ dst, const T* __restrict__ src, KWalk outer,
+                                    int64_t inner_units, int64_t rows, int64_t src_base, int64_t dst_base_v) {
+  constexpr int V = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+    int64_t off = 0;
+    if (!walk_offsets<1>(outer, row, &off)) continue;
+    const T v = src[src_base + off];
+    union {
+      uint4 q;
+      T e[V];
+    } pack;
+#pragma unroll
+    for (int k = 0; k < V; ++k) pack.e[k] = v;
+    uint4* d = dst + dst_base_v + row * inner_units;
+    for (int64_t u = lane; u < inner_units; u += 32) d[u] = pack.q;
+  }
+}
+
 // ---- tile path ----
 // `others` walks every wheel except the dst-innermost (i) and the src-unit-stride (j) ones; memory
 // 0 = src offset, memory 1 = dst position. A (32 V) x (32 V) tile moves through shared memory; each
@@ -572,6 +596,13 @@ void launch_relayout_typed(fopt_ctx* ctx, const RelayoutPlan& p, void* dst, cons
       outer.stride[0][i - 1] = w.stride[0][i];
     }
     int64_t inner_units = w.extent[0] / V, units = p.positions / V;
+    if (inner_units >= 32) {
+      const int64_t rows = units / inner_units;
+      relayout_bcast_rows<T><<<grid_for(rows * 32), kThreads, 0, st>>>((uint4*)d, s, outer, inner_units, rows,
+                                                                       src_base, dst_base / V);
+      launched(ctx, "relayout_bcast_rows");
+      return;
+    }
     relayout_bcast<T><<<grid_for(units), kThreads, 0, st>>>((uint4*)d, s, outer, inner_units, units, src_base,
                                                            dst_base / V);
     launched(ctx, "relayout_bcast");
