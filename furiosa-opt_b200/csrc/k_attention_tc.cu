@@ -1203,7 +1203,13 @@ bool launch_attention_tc(fopt_ctx* ctx, void* o, const void* q, const void* k, c
                "attention smem attribute");
     attr = true;
   }
-  if (getenv("FOPT_ATTN_SPLIT_ROWS")) {
+  // The persistent kernel for sequences up to 1024 (B = 8, S = 512: 57.3 against 63.5 us for the
+  // paired kernel; B = 4, S = 1024: 73.7 against 77.8), where the paired kernel's per-CTA start and
+  // finish weigh most; the paired kernel beyond (S = 2048: 59.4 against 61.4). FOPT_ATTN_SPLIT_ROWS /
+  // FOPT_ATTN_PAIRED force one or the other.
+  const bool split_rows = getenv("FOPT_ATTN_SPLIT_ROWS") || (S <= 1024 && !getenv("FOPT_ATTN_PAIRED") &&
+                                                             !getenv("FOPT_ATTN_ONE_TILE"));
+  if (split_rows) {
     constexpr int smem3 = (1 + KST3 + VST3) * TILE + 1024 + 3 * 2 * BQ * 4 + 256;
     static bool attr3 = false;
     if (!attr3) {

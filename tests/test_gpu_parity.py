@@ -513,12 +513,16 @@ def test_gather_rejects_negative_index(b200):
 # ---------------------------------------------------------------------------------------------
 @pytest.fixture(params=["paired", "one_tile", "split_rows"])
 def attn_kernel(request, monkeypatch):
-    """S % 256 == 0 runs the two-query-tile tcgen05 kernel, or with FOPT_ATTN_ONE_TILE the one-tile
-    kernel (which also serves odd block counts), or with FOPT_ATTN_SPLIT_ROWS the persistent kernel
-    with two threads per row."""
+    """Each tcgen05 attention kernel, forced: the two-query-tile kernel (FOPT_ATTN_PAIRED; the default
+    beyond S = 1024 when S % 256 == 0), the one-tile kernel (FOPT_ATTN_ONE_TILE, which also serves odd
+    block counts) and the persistent kernel with two threads per row (FOPT_ATTN_SPLIT_ROWS; the
+    default up to S = 1024)."""
     monkeypatch.delenv("FOPT_ATTN_ONE_TILE", raising=False)
     monkeypatch.delenv("FOPT_ATTN_SPLIT_ROWS", raising=False)
-    if request.param == "one_tile":
+    monkeypatch.delenv("FOPT_ATTN_PAIRED", raising=False)
+    if request.param == "paired":
+        monkeypatch.setenv("FOPT_ATTN_PAIRED", "1")
+    elif request.param == "one_tile":
         monkeypatch.setenv("FOPT_ATTN_ONE_TILE", "1")
     elif request.param == "split_rows":
         monkeypatch.setenv("FOPT_ATTN_SPLIT_ROWS", "1")
