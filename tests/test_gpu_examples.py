@@ -54,6 +54,21 @@ def test_chip_shuffle(b200):
     assert np.array_equal(got, expected.astype(np.int32))
 
 
+def test_cluster_shuffle(b200):
+    """dm_cluster_shuffle (memory.rs:1183-1206): `pattern[target] = source` over the Cluster axis of
+    a DM tensor [Chip, Cluster, Slice, Element], on 2 chips x 2 clusters with [1, 0] (the swap the
+    reference's doc names), against numpy."""
+    ax = dict(A=512, B=64)
+    dm = M("[A / 256, A / 128 % 2, A % 128, B]", **ax)              # Chip 2, Cluster 2, Slice 128, [B]
+    x = np.random.default_rng(11).integers(-2**31, 2**31 - 1, 512 * 64).astype(np.int32)
+    d = b200.from_vec(dm, x, "i32")
+    out = fb.dist.cluster_shuffle_local(b200, d, 2, 2, [1, 0])
+    want = x.reshape(2, 2, 128, 64)[:, [1, 0]].reshape(-1)
+    assert np.array_equal(out.to_numpy(), want)
+    with pytest.raises(ValueError):
+        fb.dist.cluster_shuffle_local(b200, d, 2, 2, [0, 0])
+
+
 # ---- pe_count_tests.rs (src/pe_count.rs): output == input + 1 on every device topology ----------
 PE_CONFIGS = {
     # name: (axis, size, DM mapping = Chip, Cluster, Slice, Element)
