@@ -235,6 +235,49 @@ __global__ void contract_cell_warp_kernel(CArgs a, KWalk ow, int64_t out_positio
   }
 }
 
+// i8 x i8 contractions whose residue is one fully live run of unit stride in both operands (a
+// dense dot product per cell, e.g. [B, I] x [H, I]): a warp per cell reads both rows as 16-byte
+// vectors and multiplies four byte pairs per instruction (dp4a). The i32 sum wraps like the fold's,
+// and integer sums do not depend on their order. Cells whose rows are not 16-byte aligned, or
+// reach past either operand, take the per-element loop.
+__global__ void contract_dense_i8_warp_kernel(CArgs a, KWalk ow, int64_t out_positions, int64_t K) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int8_t* lhs = (const int8_t*)a.lhs;
+  const int8_t* rhs = (const int8_t*)a.rhs;
+  for (int64_t o = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; o < out_positions; o += nw) {
+    int64_t off[3] = {0, 0, 0};
+    const bool live = walk_offsets<3>(ow, o, off);
+    uint32_t acc = 0;  // wraps, as the fold's sum does
+    if (live) {
+      const int64_t pl = off[0], pr = off[1];
+      const bool inside = pl >= 0 && pr >= 0 && pl + K <= a.lhs_elems && pr + K <= a.rhs_elems;
+      const bool vec = inside && ((((uintptr_t)(lhs + pl)) | ((uintptr_t)(rhs + pr))) & 15) == 0;
+      int64_t r0 = 0;
+      if (vec) {
+        const int4* x = (const int4*)(lhs + pl);
+        const int4* w = (const int4*)(rhs + pr);
+        const int64_t nv = K >> 4;
+        for (int64_t v = lane; v < nv; v += 32) {
+          const int4 xa = x[v], wa = w[v];
+          acc = (uint32_t)__dp4a(xa.x, wa.x, (int)acc);
+          acc = (uint32_t)__dp4a(xa.y, wa.y, (int)acc);
+          acc = (uint32_t)__dp4a(xa.z, wa.z, (int)acc);
+          acc = (uint32_t)__dp4a(xa.w, wa.w, (int)acc);
+        }
+        r0 = nv << 4;
+      }
+      for (int64_t r = r0 + lane; r < K; r += 32) {
+        const int64_t il = pl + r, ir = pr + r;
+        if (il < a.lhs_elems && ir < a.rhs_elems) acc += (uint32_t)((int32_t)lhs[il] * (int32_t)rhs[ir]);
+      }
+    }
+#pragma unroll
+    for (int m = 16; m; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+    if (lane == 0) store_word(a.out, a.out_dt, o, live ? int_finish(a, (int32_t)acc, off[2]) : 0u);
+  }
+}
+
 __global__ void contract_cell_nibble_kernel(CArgs a, KWalk ow, int64_t out_positions) {
   for (int64_t by = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; by * 2 < out_positions;
        by += (int64_t)gridDim.x * blockDim.x) {
@@ -345,6 +388,11 @@ void launch_contraction_generic(fopt_ctx* ctx, const FoldKPlan& p, void* out, in
   if (dtype_bits(out_dt) == 4) {
     contract_cell_nibble_kernel<<<grid_for((p.out_positions + 1) / 2), 256, 0, ctx->stream>>>(a, p.out,
                                                                                                p.out_positions);
+  } else if (in_dt == FOPT_I8 && p.residue.n == 1 && p.residue.live[0] == p.residue.extent[0] &&
+             p.residue.stride[0][0] == 1 && p.residue.stride[1][0] == 1 && nd >= 32 &&
+             !getenv("FOPT_FOLD_NO_DENSE")) {
+    contract_dense_i8_warp_kernel<<<grid_for(p.out_positions * 32), 256, 0, ctx->stream>>>(a, p.out, p.out_positions,
+                                                                                         p.residue.extent[0]);
   } else if (int_in_host(in_dt) && nd >= 32) {
     contract_cell_warp_kernel<<<grid_for(p.out_positions * 32), 256, 0, ctx->stream>>>(a, p.out, p.out_positions);
   } else {
