@@ -145,6 +145,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+// The load alone, and a wait that takes the loaded registers as operands, so that no use of them
+// can be scheduled before it: a chunk's load stays in flight while the previous chunk is processed.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : R32(0), R32(1), R32(2), R32(3), R32(4), R32(5), R32(6), R32(7), R32(8), R32(9), R32(10), R32(11), R32(12),
+        R32(13), R32(14), R32(15), R32(16), R32(17), R32(18), R32(19), R32(20), R32(21), R32(22), R32(23), R32(24),
+        R32(25), R32(26), R32(27), R32(28), R32(29), R32(30), R32(31)
+      : "r"(taddr));
+}
+#define RW32(i) "+r"(r[i])
+__device__ __forceinline__ void tmem_wait32(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : RW32(0), RW32(1), RW32(2), RW32(3), RW32(4), RW32(5), RW32(6), RW32(7), RW32(8), RW32(9), RW32(10),
+                 RW32(11), RW32(12), RW32(13), RW32(14), RW32(15), RW32(16), RW32(17), RW32(18), RW32(19), RW32(20),
+                 RW32(21), RW32(22), RW32(23), RW32(24), RW32(25), RW32(26), RW32(27), RW32(28), RW32(29), RW32(30),
+                 RW32(31)
+               :
+               : "memory");
+}
+#undef RW32
 #define W32(i) "r"(r[i])
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   asm volatile(
@@ -903,15 +925,32 @@ __global__ void __launch_bounds__(THREADS, 1)
             swiglu_store(p, m0 + row_in_tile, n0 / 2 + c * 32, rg, ru, cg, cu, rs);
           }
         } else if (good) {
-#pragma unroll 1
-          for (int c = half; c < ncols / 32; c += EPI_WARPS / 4) {
-            uint32_t r[32];
-            tmem_ld32(tbase + (uint32_t)(c * 32), r);
-            if (tracer && w.sp < 0 && c == half) p.trace[u * 5 + 4] = globaltimer();
-            if (w.sp >= 0) add_staged<IS_F16>(r, stage, (c - half) >> 1, lane);
+          // This warp's chunks are c = half + 2 i (i < nch); chunk i + 1's TMEM load is in flight
+          // while chunk i is converted and stored.
+          const int nch = ncols / 64;
+          auto chunk = [&](int i, uint32_t* r) {
+            const int c = half + 2 * i;
+            if (tracer && w.sp < 0 && i == 0) p.trace[u * 5 + 4] = globaltimer();
+            if (w.sp >= 0) add_staged<IS_F16>(r, stage, i, lane);
             const float* csc = kStaged ? wsc + (c - half) * 16 : p.scale + n0 + c * 32;
             const uint32_t nanmask = MODE == EP_RQ31 ? __ballot_sync(0xffffffffu, csc[lane] != csc[lane]) : 0u;
             epilogue_store<IS_F16, MODE>(p, m0 + row_in_tile, n0 + c * 32, r, csc, rs, nanmask);
+          };
+          auto taddr = [&](int i) { return tbase + (uint32_t)((half + 2 * i) * 32); };
+          uint32_t ra[32], rb[32];
+          tmem_ld32_nowait(taddr(0), ra);
+          tmem_wait32(ra);
+#pragma unroll 1
+          for (int i = 0; i < nch; i += 2) {
+            const bool n1 = i + 1 < nch, n2 = i + 2 < nch;
+            if (n1) tmem_ld32_nowait(taddr(i + 1), rb);
+            chunk(i, ra);
+            if (n1) {
+              tmem_wait32(rb);
+              if (n2) tmem_ld32_nowait(taddr(i + 2), ra);
+              chunk(i + 1, rb);
+              if (n2) tmem_wait32(ra);
+            }
           }
         }
         if (w.sp >= 0) {
