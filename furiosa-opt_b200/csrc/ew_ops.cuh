@@ -152,17 +152,22 @@ __device__ __forceinline__ unsigned qdiv_fxp(unsigned a, unsigned s, float rq, u
     // away from a tie, rounding half away from zero and to nearest even give the same integer; the
     // distance to the nearest integer |y - rint(y)| is exact below 4096, and 1/2 minus it is the
     // distance to the nearest half-integer
-    const float r = rintf(y), d = __fsub_rn(0.5f, fabsf(__fsub_rn(y, r)));
-    if (d > __fmaf_rn(ay, 4.76837158203125e-7f, 1e-30f)) return (unsigned)(int)r;
+    const float big = __fadd_rn(y, 12582912.0f);  // rounds y to an integer, as in qdiv_fxp_fast below
+    const float r = __fsub_rn(big, 12582912.0f), d = __fsub_rn(0.5f, fabsf(__fsub_rn(y, r)));
+    if (d > __fmaf_rn(ay, 4.76837158203125e-7f, 1e-30f)) return (unsigned)(__float_as_int(big) - 0x4B400000);
   }
   return (unsigned)vfp_to_fxp(__fdiv_rn(x, __uint_as_float(s)), iw);
 }
 // The fast path of qdiv_fxp alone, without branching: *ok false when the exact path must run.
+// Below 2^22 in magnitude, y + 1.5 * 2^23 rounds y to the nearest integer (ties to even, as rintf)
+// into the low bits of a float whose spacing is 1, so the rounding and the integer conversion take
+// two adds and an integer subtract on the FMA and ALU pipes instead of the conversion unit.
 __device__ __forceinline__ unsigned qdiv_fxp_fast(unsigned a, float rq, bool* ok) {
   const float y = __fmul_rn(__uint_as_float(a), rq), ay = fabsf(y);
-  const float r = rintf(y), d = __fsub_rn(0.5f, fabsf(__fsub_rn(y, r)));
+  const float big = __fadd_rn(y, 12582912.0f);
+  const float r = __fsub_rn(big, 12582912.0f), d = __fsub_rn(0.5f, fabsf(__fsub_rn(y, r)));
   *ok = ay < 4096.0f && d > __fmaf_rn(ay, 4.76837158203125e-7f, 1e-30f);
-  return *ok ? (unsigned)(int)r : 0u;
+  return *ok ? (unsigned)(__float_as_int(big) - 0x4B400000) : 0u;
 }
 // Sigmoid as the opcode table computes it: 1 / (1 + e^-x), the reciprocal correctly rounded.
 __device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(__fadd_rn(1.0f, expf(-x))); }
