@@ -524,3 +524,28 @@ def test_ctypes_structs_match_the_c_abi():
     assert _lib.lib().fopt_struct_sizes(sizes, 4) == 0
     assert list(sizes) == [C.sizeof(_lib.Program), C.sizeof(_lib.Epilogue), C.sizeof(_lib.RowSlot),
                            C.sizeof(_lib.RowPlan)]
+
+
+def test_magic_add_rounds_like_rint():
+    """The quantising division's fast path (`qdiv_fxp_fast`, `ew_ops.cuh`) rounds y with |y| < 4096
+    by adding 1.5 * 2^23 in f32 (round to nearest even) and reads the integer from the low bits of
+    the sum: checked here against rint in f32 arithmetic, over every f32 in the binades near the
+    half-integers that matter (|y| < 8, and the last binade below 4096) plus random values."""
+    magic = np.float32(12582912.0)
+
+    def check(y):
+        y = y[np.abs(y) < 4096].astype(np.float32)
+        big = (y + magic).astype(np.float32)
+        r = (big - magic).astype(np.float32)
+        assert np.array_equal(r, np.rint(y))
+        assert np.array_equal(big.view(np.int32) - 0x4B400000, np.rint(y).astype(np.int32))
+
+    lo = np.arange(0, 0x41000000, 61, dtype=np.uint32).view(np.float32)  # 0 <= y < 8, every 61st code
+    check(lo)
+    check(-lo)
+    top = np.arange(0x45000000, 0x45800000, dtype=np.uint32).view(np.float32)  # 2048 <= y < 4096, all
+    check(top)
+    check(-top)
+    halves = (np.arange(-4096, 4096, dtype=np.float32) + np.float32(0.5))
+    check(halves)  # exact ties go to even, as rint
+    check(np.random.default_rng(5).uniform(-4096, 4096, 1 << 20).astype(np.float32))
