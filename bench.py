@@ -968,7 +968,7 @@ def run_ours(args, rank, world, local):
         if line is not None:
             line["configs"] = configs
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def run_reference(args, rank, world):
@@ -994,10 +994,30 @@ def run_reference(args, rank, world):
             "cpu_baseline": {"value": round(v, 5), "unit": "TOPS", "cores": os.cpu_count(), "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(v, 5), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+# The result line goes to the process's original stdout; everything else written to file
+# descriptor 1 during the run (NCCL's version banner, native library prints) is sent to stderr, so
+# stdout holds exactly one JSON line.
+_RESULT_FD = None
+
+
+def emit(line):
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+        return
+    while data:
+        data = data[os.write(_RESULT_FD, data):]
 
 
 def main():
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
